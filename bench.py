@@ -1,0 +1,350 @@
+"""Headline benchmark: FFN-down W8A8 projection with online activation quantization.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (FFN-down at M=4096): A bf16 [4096, 16384] ~N(0,1)
+per GPU, W bf16 [4096, 16384] ~N(0, 0.02) quantized offline per output
+channel (symmetric INT8, amax/127).  One step = online per-token INT8
+quantization of A (row-prep kernel) + tcgen05 W8A8 GEMM with the fused
+(acc * sa) * sw -> bf16 epilogue.  Metric: 2*M*N*K / step time, in TOPS,
+summed over ranks (tokens are sharded: each rank owns its own M=4096 rows,
+weights replicated, no collective -> weak scaling).
+
+Three independent (A, W) sets are rotated so that no step reuses an operand
+from L2 (A alone is 134 MB > 126 MB L2).  Timing: CUDA events on the launching
+stream, barrier + synchronize around the K timed steps, max over ranks.
+`e2e` repeats the step through the public API from pinned host memory: H2D of
+A, the two kernels, D2H of the bf16 output, every step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "m5-max-kernels_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+M, K, N = 4096, 16384, 4096
+SETS = 3
+METRIC = "W8A8 proj TOPS incl. online quant @M=4096 (% INT8 peak); prep HBM GB/s"
+WORKLOAD = "ffn_down_w8a8_online_quant_M4096_K16384_N4096"
+
+
+def _peaks():
+    """Roofline denominators: MEASURED_PEAKS.json if present, else the fallback."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16": float(d["bf16_tflops"]),
+                "bf16_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread is not None:
+                self.thread.join(timeout=5)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_reference(steps: int, warmup: int, target_s: float = 12.0):
+    """The reference's CPU path on a bounded sample of the workload.
+
+    Per step: per-token INT8 quantization of `rows` activation rows with the
+    restated numerics.quantize_reference (float32 NumPy), the decoded float64
+    BLAS product against the INT8 weight (src/m5kernels/engine.py:173-175 —
+    the reference's own CPU GEMM), scale epilogue and BF16 rounding.
+    """
+    import numpy as np
+
+    from oracle import reference_numpy as ref
+
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02)
+    wq, ws = ref.quantize_reference(w, "int8")
+    wd = wq.astype(np.float64) * ws.astype(np.float64)[:, None]
+    del w
+
+    def one(rows):
+        a = rng.standard_normal((rows, K), dtype=np.float32)
+        t0 = time.perf_counter()
+        q, s = ref.quantize_reference(a, "int8")
+        y = (q.astype(np.float64) * s.astype(np.float64)[:, None]) @ wd.T
+        ref.bf16_round_reference(y)
+        return time.perf_counter() - t0
+
+    rows = 64
+    t = one(rows)
+    rows = int(max(16, min(M, rows * (target_s / max(steps, 1)) / max(t, 1e-3))))
+    for _ in range(max(warmup, 0)):
+        one(min(rows, 64))
+    times = [one(rows) for _ in range(max(steps, 1))]
+    per = statistics.median(times)
+    tops = 2.0 * rows * N * K / per / 1e12
+    cores = os.cpu_count() or 1
+    return {"value": tops, "unit": "TOPS", "cores": cores, "kind": "port",
+            "sample": f"{rows} of {M} activation rows per step (FFN-down K={K}, N={N}); "
+                      f"NumPy float32 quantize_reference + float64 BLAS decoded GEMM",
+            "seconds_per_step": per}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    cb = cpu_reference(args.steps, args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "TOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 2.0 * M * N * K / (cb["value"] * 1e12) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": "TOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    import m5kernels_b200 as m5
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    sets = []
+    for i in range(SETS):
+        a = torch.randn(M, K, device=dev, generator=gen, dtype=torch.float32).to(torch.bfloat16)
+        w = (torch.randn(N, K, device=dev, generator=gen, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+        wq, ws = m5.quantize(w, "int8")  # offline weight preparation (untimed)
+        del w
+        sets.append((a, wq, ws))
+    torch.cuda.synchronize()
+
+    def step(i):
+        a, wq, ws = sets[i % SETS]
+        q, s = m5.quantize(a, "int8")
+        return m5.gemm(q, wq, "int8", a_scales=s, b_scales=ws, output_dtype=torch.bfloat16)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier()
+
+    stream = torch.cuda.current_stream(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms_total = t0.elapsed_time(t1)
+    ms = torch.tensor([ms_total / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms_per_step = float(ms.item())
+    ops_per_rank = 2.0 * M * N * K
+    value = world * ops_per_rank / (ms_per_step * 1e-3) / 1e12
+
+    # Per-kernel device times (same stream, same rotation) for the roofline.
+    def time_kernel(fn, reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        fn(0)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(reps):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    prepped = [m5.quantize(a, "int8") for a, _, _ in sets]
+    gemm_ms = time_kernel(lambda i: m5.gemm(prepped[i % SETS][0], sets[i % SETS][1], "int8",
+                                            a_scales=prepped[i % SETS][1], b_scales=sets[i % SETS][2],
+                                            output_dtype=torch.bfloat16), max(args.steps, 10))
+    prep_ms = time_kernel(lambda i: m5.quantize(sets[i % SETS][0], "int8"), max(args.steps, 10))
+
+    # End to end through the public API from pinned host memory.
+    host_a = [sets[i][0].to("cpu").pin_memory() for i in range(SETS)]
+    host_out = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    dev_a = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
+
+    def e2e_step(i):
+        dev_a.copy_(host_a[i % SETS], non_blocking=True)
+        q, s = m5.quantize(dev_a, "int8")
+        y = m5.gemm(q, sets[i % SETS][1], "int8", a_scales=s, b_scales=sets[i % SETS][2],
+                    output_dtype=torch.bfloat16)
+        host_out.copy_(y, non_blocking=True)
+
+    for i in range(min(args.warmup, 3)):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, min(args.steps, 10))
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = world * ops_per_rank / (float(e2e_ms.item()) * 1e-3) / 1e12
+
+    peaks = _peaks()
+    int8_peak = 2.0 * peaks["bf16"]  # dense INT8 = 2x dense BF16 on B200 (4.5 / 2.25 PF nominal)
+    gemm_tops = ops_per_rank / (gemm_ms * 1e-3) / 1e12
+    prep_bytes = M * (3 * K + 4)
+    prep_gbs = prep_bytes / (prep_ms * 1e-3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "roofline_traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get("gemm_dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    out = None
+    if rank == 0:
+        cb = cpu_reference(1, 0, target_s=10.0) if world == 1 else None
+        clock = clocks.summary()
+        out = {
+            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "M_per_gpu": M, "K": K, "N": N,
+                       "global_M": M * world, "parallelism": f"token-sharded x{world}",
+                       "l2": f"inputs larger than L2; {SETS} rotating operand sets"},
+            "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
+                         "unit": "TFLOP/s", "frac": gemm_tops / int8_peak, "traffic": traffic,
+                         "kernel": "gemm_tc_kernel<i8>",
+                         "peak_source": f"2 x {peaks['source']} dense bf16 ({peaks['bf16']} TF/s)"},
+            "prep": {"kernel": "row_prep_kernel<bf16,0,int8>", "ms": prep_ms,
+                     "achieved_gbs": prep_gbs, "peak_gbs": peaks["hbm_gbs"],
+                     "frac": prep_gbs / peaks["hbm_gbs"], "bytes": prep_bytes},
+            "gemm_ms": gemm_ms,
+            "pct_int8_peak_incl_quant": value / world / int8_peak,
+            "cpu_baseline": ({k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+                             if cb else None),
+            "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": M * K * 2,
+                    "d2h_bytes_per_step": M * N * 2},
+            "clocks": clock,
+            "gpu_launches": 2 * args.steps,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = _dist()
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+    return run_b200(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

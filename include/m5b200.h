@@ -1,0 +1,160 @@
+/*
+ * m5b200 — C ABI of the B200 (sm_100a) quantized linear-projection kernels.
+ *
+ * Each entry point replaces one operator contract of the reference project
+ * (9Tempest/m5-max-kernels, Python + Metal).  The reference's operators are
+ * Python functions in src/m5kernels/*.py that build Metal kernels through
+ * MLX; the functions below take plain device pointers, sizes and a CUDA
+ * stream instead, so any host language can bind them (ctypes, cgo, JNI ...).
+ *
+ * Conventions
+ *   - All tensor pointers are CUDA device pointers, row-major and contiguous.
+ *   - Outputs are preallocated by the caller; inputs are never written.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *     asynchronous: they enqueue kernels and return.
+ *   - Return value: M5B_OK, or an error code; m5b_last_error() then describes
+ *     the failure (thread-local, valid until the next call on this thread).
+ *       M5B_EINVAL       contract violation     (the reference raises ValueError)
+ *       M5B_EUNSUPPORTED unsupported shape/mode (the reference raises NotImplementedError)
+ *       M5B_ECUDA        CUDA runtime/driver error
+ *   - Value preconditions (finite inputs, +-1 signs, table-index bounds) are
+ *     the caller's, as in the reference; they are not checked here.
+ *   - Device-side waits are bounded; a wait that gives up records a bit in a
+ *     per-device status word readable with m5b_device_status().
+ */
+#ifndef M5B200_H
+#define M5B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define M5B_API __attribute__((visibility("default")))
+#else
+#define M5B_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define M5B_OK 0
+#define M5B_EINVAL 1
+#define M5B_EUNSUPPORTED 2
+#define M5B_ECUDA 3
+
+/* element types */
+#define M5B_F32 0
+#define M5B_F16 1
+#define M5B_BF16 2
+#define M5B_I8 3
+#define M5B_U8 4
+#define M5B_I32 5 /* raw INT32 GEMM accumulators (m5b_gemm, INT8 mode only) */
+
+/* quantization / GEMM modes */
+#define M5B_MODE_INT8 0 /* symmetric INT8, scale = amax/127 (INT32 accumulation) */
+#define M5B_MODE_FP8 1  /* OCP E4M3 codes (uint8 bits), scale = amax/448 (FP32 accumulation) */
+#define M5B_MODE_BF16 2 /* bf16 operands, FP32 accumulation (GEMM only) */
+#define M5B_MODE_FP16 3 /* fp16 operands, FP32 accumulation (GEMM only) */
+
+/* normalizations */
+#define M5B_NORM_RMS 1
+#define M5B_NORM_LAYER 2
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+M5B_API int m5b_version(void);
+
+/* Description of the last error on this thread ("" if none). */
+M5B_API const char* m5b_last_error(void);
+
+/* Device status word of the current device: bit 0 producer wait, bit 1 MMA
+ * wait, bit 2 epilogue wait, bit 3 drain wait gave up.  Synchronizes the
+ * device.  If clear != 0 the word is reset to zero afterwards. */
+M5B_API int m5b_device_status(unsigned int* status_out, int clear);
+
+/* Per-token symmetric quantization of x[rows, k] (bf16 / fp16 / fp32).
+ * mode INT8: q int8, scale = amax/127, q = clip(rint(x/scale), +-127).
+ * mode FP8 : q = E4M3 bits (RNE, saturating), scale = amax/448.
+ * All-zero rows get scale 1.
+ * Replaces src/m5kernels/metal.py:106-123 (quantize) with the arithmetic of
+ * src/m5kernels/numerics.py:29-46 (quantize_reference). */
+M5B_API int m5b_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int mode, void* q,
+                 float* scales, void* stream);
+
+/* FP32 signed block Hadamard rotation y = x D H (H normalized Sylvester,
+ * blocks of block_size along k, block_size in {32..1024}, k % block_size == 0).
+ * signs: int8[k] of +-1, or NULL for D = I.
+ * Replaces src/m5kernels/hadamard.py:33-77 (rotate). */
+M5B_API int m5b_rotate(const void* x, int x_dtype, int64_t rows, int64_t k, int block_size,
+               const int8_t* signs, float* y, void* stream);
+
+/* quantize(rotate(x)) in one pass, bit-identical to the two-step path.
+ * Replaces the online preparation of src/m5kernels/hadamard_gemm.py:65-66. */
+M5B_API int m5b_hadamard_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int block_size,
+                          const int8_t* signs, int mode, void* q, float* scales, void* stream);
+
+/* Fused normalization + AdaLN modulation + rotation + quantization:
+ *   y = norm(x) * gamma * (1 + scale[map]) + shift[map]   (FP32)
+ *   y = round_through(x_dtype, y)  if round_output
+ *   q, s = quantize(y D H, mode)
+ * norm M5B_NORM_RMS (mean of squares) or M5B_NORM_LAYER (centered, population
+ * variance); epsilon inside the square root.  scale/shift are [k] vectors when
+ * row_map == NULL, else [table_rows, k] tables indexed by row_map[rows].
+ * Replaces src/m5kernels/norm_hadamard.py:122-176
+ * (fused_norm_hadamard_quantize), extended with an E4M3 output mode. */
+M5B_API int m5b_fused_norm_hadamard_quantize(const void* x, int x_dtype, int64_t rows, int64_t k,
+                                     const void* gamma, int gamma_dtype, const void* scale,
+                                     int scale_dtype, const void* shift, int shift_dtype,
+                                     const int32_t* row_map, int64_t table_rows,
+                                     const int8_t* signs, int block_size, int norm,
+                                     float epsilon, int round_output, int mode, void* q,
+                                     float* scales, void* stream);
+
+/* As above, on the updated residual R' = cast(R + branch * gate[gate_map])
+ * (one FP32 fused multiply-add, then RNE to x_dtype), which is also written
+ * to residual_out.  gate is [k] when gate_row_map == NULL, else
+ * [gate_rows, k].  Replaces src/m5kernels/norm_hadamard.py:198-265
+ * (fused_gated_residual_norm_hadamard_quantize). */
+M5B_API int m5b_fused_gated_residual_norm_hadamard_quantize(
+    const void* residual, const void* branch, int x_dtype, int64_t rows, int64_t k,
+    const void* gate, int gate_dtype, const int32_t* gate_row_map, int64_t gate_rows,
+    const void* gamma, int gamma_dtype, const void* scale, int scale_dtype, const void* shift,
+    int shift_dtype, const int32_t* row_map, int64_t table_rows, const int8_t* signs,
+    int block_size, int norm, float epsilon, int round_output, int mode, void* q, float* scales,
+    void* residual_out, void* stream);
+
+/* C[m, n] = epilogue(A[m, k] . B[n, k]^T) on tcgen05 tensor cores.
+ *   mode INT8: int8 operands, INT32 accumulation; FP8: E4M3 operands, FP32
+ *   accumulation (k % 128 == 0); BF16 / FP16: FP32 accumulation.
+ *   Quantized modes require a_scales[m], b_scales[n]:
+ *       v = (float(acc) * a_scales[m]) * b_scales[n]
+ *   bias (INT8 only): v += bias[n] (bias_row_map == NULL) or
+ *       bias[bias_row_map[m], n] (bias is [bias_rows, n]).
+ *   gated residual (INT8 / BF16, bf16 output): out = R[m, n] + bf16(v) * gate,
+ *       gate [n] or [gate_rows, n] with gate_row_map.
+ *   out_dtype: M5B_BF16, M5B_F16 or M5B_F32; M5B_I32 (INT8 mode, no scales,
+ *       bias or gate) stores the raw INT32 accumulators.
+ * Replaces src/m5kernels/metal.py:237-348 (gemm). */
+M5B_API int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
+             const float* a_scales, const float* b_scales, void* out, int out_dtype,
+             const float* bias, const int32_t* bias_row_map, int64_t bias_rows,
+             const void* residual, const void* gate, const int32_t* gate_row_map,
+             int64_t gate_rows, void* stream);
+
+/* Q or K projection with per-head RMSNorm and split-half RoPE, head-major:
+ *   z = bf16(v)  (v as in m5b_gemm), per (row, head): r = 1/sqrt(mean(z^2) + eps)
+ *   u_j = z_j * r * gamma_j; for j < R: (u_j, u_{j+R}) rotated by
+ *   (cos, sin)[row, j]; channels >= 2R unrotated; out bf16 [n/128, m, 128].
+ * gamma bf16[128]; cos, sin bf16[m, rope_half], 1 <= rope_half <= 64.
+ * mode INT8 (with scales) or BF16 (without).
+ * Replaces src/m5kernels/qk_rope.py:120-182 (projection_qk_rope). */
+M5B_API int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
+                           int mode, const float* a_scales, const float* b_scales,
+                           const void* gamma, const void* cos, const void* sin, int rope_half,
+                           float epsilon, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* M5B200_H */

@@ -1,0 +1,470 @@
+// C-ABI entry points of libm5b200.so (declared in include/m5b200.h).
+//
+// This layer checks the operator contracts that can be checked from sizes
+// and pointers, builds TMA descriptors, picks launch shapes and enqueues the
+// kernels of prep.cu / gemm.cu on the caller's stream.  It never allocates
+// device memory.
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "m5b200.h"
+#include "m5b_internal.h"
+
+using namespace m5b;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_err[0] = '\0';
+  return M5B_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(M5B_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------- device state
+__device__ unsigned int g_status_word;
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mutex;
+unsigned int* g_status_ptr[kMaxDevices] = {};
+int g_num_sms[kMaxDevices] = {};
+
+int device_state(unsigned int** status, int* sms) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(M5B_ECUDA, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (!g_status_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_status_word);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    g_num_sms[dev] = n;
+    g_status_ptr[dev] = static_cast<unsigned int*>(p);
+  }
+  if (status) *status = g_status_ptr[dev];
+  if (sms) *sms = g_num_sms[dev];
+  return M5B_OK;
+}
+
+// ---------------------------------------------------------------- TMA maps
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) return fail(M5B_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  return M5B_OK;
+}
+
+// K-major [rows, k] operand, boxes of 128 bytes x box_rows, 128-byte swizzle.
+int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int elem_bytes,
+                    int box_rows) {
+  const CUtensorMapDataType dt =
+      elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k * elem_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem_bytes), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(M5B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return M5B_OK;
+}
+
+// ---------------------------------------------------------------- helpers
+bool float_dtype(int dt) { return dt == M5B_F32 || dt == M5B_F16 || dt == M5B_BF16; }
+int dtype_bytes(int dt) { return dt == M5B_F32 ? 4 : (dt == M5B_I8 || dt == M5B_U8) ? 1 : 2; }
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_block(int block, int64_t k) {
+  if (block <= 0 || (block & (block - 1)))
+    return fail(M5B_EINVAL, "block_size must be a positive integer power of two");
+  if (block < 32 || block > 1024)
+    return fail(M5B_EUNSUPPORTED, "supported block sizes are powers of two from 32 through 1024");
+  if (k % block)
+    return fail(M5B_EUNSUPPORTED, "K must be divisible by block_size; padding is not implicit");
+  return M5B_OK;
+}
+
+int check_rows(int64_t rows, int64_t k) {
+  if (rows <= 0 || k <= 0) return fail(M5B_EINVAL, "input must have nonempty shape [rows, K]");
+  if (rows > 0x7fffffffLL) return fail(M5B_EUNSUPPORTED, "rows exceed the launch grid limit");
+  return M5B_OK;
+}
+
+int run_row_prep(RowPrepArgs& a, int x_dtype, int block, int out, void* stream) {
+  a.warps = row_prep_warps(a.K, block);
+  if (a.warps > 16)
+    return fail(M5B_EUNSUPPORTED, "row width K=%lld exceeds the register-resident limit",
+                static_cast<long long>(a.K));
+  a.inv_sqrt_block = block > 0 ? static_cast<float>(1.0 / std::sqrt(static_cast<double>(block)))
+                               : 1.0f;
+  const int xb = dtype_bytes(x_dtype);
+  bool vec = (a.K % 8) == 0 && aligned(a.x, 16) && (!a.branch || aligned(a.branch, 16)) &&
+             (!a.r_out || aligned(a.r_out, 16)) && (!a.q || aligned(a.q, 8)) &&
+             (!a.y || aligned(a.y, 16));
+  (void)xb;
+  a.vec_ok = vec ? 1 : 0;
+  cudaError_t e = launch_row_prep(a, x_dtype, block, out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "row preparation launch");
+  return ok();
+}
+
+int prep_common(RowPrepArgs& a, const void* x, int x_dtype, int64_t rows, int64_t k) {
+  int rc = check_rows(rows, k);
+  if (rc) return rc;
+  if (!float_dtype(x_dtype)) return fail(M5B_EINVAL, "input dtype must be float16, bfloat16 or float32");
+  if (!x) return fail(M5B_EINVAL, "input pointer is NULL");
+  a = RowPrepArgs{};
+  a.x = x;
+  a.rows = rows;
+  a.K = k;
+  return M5B_OK;
+}
+
+int out_kind(int mode) {
+  if (mode == M5B_MODE_INT8) return OUT_INT8;
+  if (mode == M5B_MODE_FP8) return OUT_E4M3;
+  return -1;
+}
+
+int norm_setup(RowPrepArgs& a, const void* gamma, int gamma_dtype, const void* scale,
+               int scale_dtype, const void* shift, int shift_dtype, const int32_t* row_map,
+               int64_t table_rows, int norm, float epsilon, int round_output) {
+  if (norm != M5B_NORM_RMS && norm != M5B_NORM_LAYER)
+    return fail(M5B_EINVAL, "norm must be 'rms' or 'layer'");
+  if (!(epsilon > 0.0f) || !std::isfinite(epsilon))
+    return fail(M5B_EINVAL, "epsilon must be a positive finite real scalar");
+  if (!gamma || !scale || !shift) return fail(M5B_EINVAL, "gamma, scale and shift are required");
+  if (!float_dtype(gamma_dtype) || !float_dtype(scale_dtype) || !float_dtype(shift_dtype))
+    return fail(M5B_EINVAL, "gamma, scale and shift must have floating dtype");
+  if (row_map && table_rows <= 0)
+    return fail(M5B_EINVAL, "mapped scale and shift must have matching nonempty shape [P,K]");
+  a.gamma = gamma;
+  a.scale = scale;
+  a.shift = shift;
+  a.gamma_dtype = gamma_dtype;
+  a.scale_dtype = scale_dtype;
+  a.shift_dtype = shift_dtype;
+  a.row_map = row_map;
+  a.norm = norm == M5B_NORM_RMS ? NORM_RMS : NORM_LAYER;
+  a.eps = epsilon;
+  a.round_output = round_output ? 1 : 0;
+  return M5B_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int m5b_version(void) { return 100; }
+
+const char* m5b_last_error(void) { return g_err; }
+
+int m5b_device_status(unsigned int* status_out, int clear) {
+  unsigned int* p = nullptr;
+  int rc = device_state(&p, nullptr);
+  if (rc) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  unsigned int v = 0;
+  e = cudaMemcpy(&v, p, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device status word");
+  if (clear) {
+    e = cudaMemset(p, 0, sizeof(unsigned int));
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the device status word");
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  }
+  if (status_out) *status_out = v;
+  return ok();
+}
+
+int m5b_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int mode, void* q,
+                 float* scales, void* stream) {
+  RowPrepArgs a;
+  int rc = prep_common(a, x, x_dtype, rows, k);
+  if (rc) return rc;
+  const int out = out_kind(mode);
+  if (out < 0) return fail(M5B_EUNSUPPORTED, "quantize supports int8 and fp8 (E4M3)");
+  if (!q || !scales) return fail(M5B_EINVAL, "output pointers are NULL");
+  a.q = q;
+  a.s = scales;
+  return run_row_prep(a, x_dtype, 0, out, stream);
+}
+
+int m5b_rotate(const void* x, int x_dtype, int64_t rows, int64_t k, int block_size,
+               const int8_t* signs, float* y, void* stream) {
+  RowPrepArgs a;
+  int rc = prep_common(a, x, x_dtype, rows, k);
+  if (rc) return rc;
+  rc = check_block(block_size, k);
+  if (rc) return rc;
+  if (!y) return fail(M5B_EINVAL, "output pointer is NULL");
+  a.signs = signs;
+  a.y = y;
+  return run_row_prep(a, x_dtype, block_size, OUT_F32, stream);
+}
+
+int m5b_hadamard_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int block_size,
+                          const int8_t* signs, int mode, void* q, float* scales, void* stream) {
+  RowPrepArgs a;
+  int rc = prep_common(a, x, x_dtype, rows, k);
+  if (rc) return rc;
+  rc = check_block(block_size, k);
+  if (rc) return rc;
+  const int out = out_kind(mode);
+  if (out < 0) return fail(M5B_EUNSUPPORTED, "quantize supports int8 and fp8 (E4M3)");
+  if (!q || !scales) return fail(M5B_EINVAL, "output pointers are NULL");
+  a.signs = signs;
+  a.q = q;
+  a.s = scales;
+  return run_row_prep(a, x_dtype, block_size, out, stream);
+}
+
+int m5b_fused_norm_hadamard_quantize(const void* x, int x_dtype, int64_t rows, int64_t k,
+                                     const void* gamma, int gamma_dtype, const void* scale,
+                                     int scale_dtype, const void* shift, int shift_dtype,
+                                     const int32_t* row_map, int64_t table_rows,
+                                     const int8_t* signs, int block_size, int norm,
+                                     float epsilon, int round_output, int mode, void* q,
+                                     float* scales, void* stream) {
+  RowPrepArgs a;
+  int rc = prep_common(a, x, x_dtype, rows, k);
+  if (rc) return rc;
+  rc = norm_setup(a, gamma, gamma_dtype, scale, scale_dtype, shift, shift_dtype, row_map,
+                  table_rows, norm, epsilon, round_output);
+  if (rc) return rc;
+  rc = check_block(block_size, k);
+  if (rc) return rc;
+  const int out = out_kind(mode);
+  if (out < 0) return fail(M5B_EUNSUPPORTED, "the fused preparation emits int8 or fp8 (E4M3)");
+  if (!q || !scales) return fail(M5B_EINVAL, "output pointers are NULL");
+  a.signs = signs;
+  a.q = q;
+  a.s = scales;
+  return run_row_prep(a, x_dtype, block_size, out, stream);
+}
+
+int m5b_fused_gated_residual_norm_hadamard_quantize(
+    const void* residual, const void* branch, int x_dtype, int64_t rows, int64_t k,
+    const void* gate, int gate_dtype, const int32_t* gate_row_map, int64_t gate_rows,
+    const void* gamma, int gamma_dtype, const void* scale, int scale_dtype, const void* shift,
+    int shift_dtype, const int32_t* row_map, int64_t table_rows, const int8_t* signs,
+    int block_size, int norm, float epsilon, int round_output, int mode, void* q, float* scales,
+    void* residual_out, void* stream) {
+  RowPrepArgs a;
+  int rc = prep_common(a, residual, x_dtype, rows, k);
+  if (rc) return rc;
+  if (!branch || !gate || !residual_out)
+    return fail(M5B_EINVAL, "branch, gate and residual_out are required");
+  if (!float_dtype(gate_dtype)) return fail(M5B_EINVAL, "gate must have floating dtype");
+  if (gate_row_map && gate_rows <= 0)
+    return fail(M5B_EINVAL, "mapped gate must have nonempty shape [P,K]");
+  rc = norm_setup(a, gamma, gamma_dtype, scale, scale_dtype, shift, shift_dtype, row_map,
+                  table_rows, norm, epsilon, round_output);
+  if (rc) return rc;
+  rc = check_block(block_size, k);
+  if (rc) return rc;
+  const int out = out_kind(mode);
+  if (out < 0) return fail(M5B_EUNSUPPORTED, "the fused preparation emits int8 or fp8 (E4M3)");
+  if (!q || !scales) return fail(M5B_EINVAL, "output pointers are NULL");
+  a.branch = branch;
+  a.gate = gate;
+  a.gate_dtype = gate_dtype;
+  a.gate_row_map = gate_row_map;
+  a.signs = signs;
+  a.q = q;
+  a.s = scales;
+  a.r_out = residual_out;
+  return run_row_prep(a, x_dtype, block_size, out, stream);
+}
+
+static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, const void* a,
+                       const void* b, int64_t m, int64_t n, int64_t k, int mode, int bn) {
+  if (m <= 0 || n <= 0 || k <= 0) return fail(M5B_EINVAL, "A and B must be nonempty matrices");
+  if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL)
+    return fail(M5B_EUNSUPPORTED, "matrix dimensions exceed 2^31-1");
+  if (!a || !b) return fail(M5B_EINVAL, "operand pointer is NULL");
+  int kind;
+  switch (mode) {
+    case M5B_MODE_INT8: kind = KIND_I8; break;
+    case M5B_MODE_FP8: kind = KIND_F8; break;
+    case M5B_MODE_BF16: kind = KIND_BF16; break;
+    case M5B_MODE_FP16: kind = KIND_F16; break;
+    default: return fail(M5B_EUNSUPPORTED, "GEMM modes are int8, fp8, bf16 and fp16");
+  }
+  const int eb = (kind == KIND_BF16 || kind == KIND_F16) ? 2 : 1;
+  if (mode == M5B_MODE_FP8 && k % 128)
+    return fail(M5B_EUNSUPPORTED,
+                "FP8 requires K/row stride divisible by 128; padding is not implicit");
+  if (mode == M5B_MODE_INT8 && k > 133144)
+    return fail(M5B_EUNSUPPORTED, "INT32 worst-case overflow bound exceeded");
+  if ((k * eb) % 16)
+    return fail(M5B_EUNSUPPORTED, "row stride K*%d bytes must be a multiple of 16 for TMA", eb);
+  if (!aligned(a, 16) || !aligned(b, 16))
+    return fail(M5B_EINVAL, "operand base addresses must be 16-byte aligned");
+  int rc = get_encode();
+  if (rc) return rc;
+  rc = make_kmajor_map(&ta, a, m, k, eb, 128);
+  if (rc) return rc;
+  rc = make_kmajor_map(&tb, b, n, k, eb, bn);
+  if (rc) return rc;
+  g.M = static_cast<int>(m);
+  g.N = static_cast<int>(n);
+  g.K = static_cast<int>(k);
+  g.kind = kind;
+  const int k_elems = 128 / eb;
+  g.num_m_blocks = static_cast<int>((m + 127) / 128);
+  g.num_n_blocks = static_cast<int>((n + bn - 1) / bn);
+  g.num_k_blocks = static_cast<int>((k + k_elems - 1) / k_elems);
+  g.group_m = 8;
+  return M5B_OK;
+}
+
+static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, int bn,
+                       void* stream) {
+  unsigned int* status = nullptr;
+  int sms = 0;
+  int rc = device_state(&status, &sms);
+  if (rc) return rc;
+  g.status = status;
+  const int tiles = g.num_m_blocks * g.num_n_blocks;
+  const int grid = tiles < sms ? tiles : sms;
+  cudaError_t e = launch_gemm(ta, tb, g, bn, grid, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
+  return ok();
+}
+
+int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
+             const float* a_scales, const float* b_scales, void* out, int out_dtype,
+             const float* bias, const int32_t* bias_row_map, int64_t bias_rows,
+             const void* residual, const void* gate, const int32_t* gate_row_map,
+             int64_t gate_rows, void* stream) {
+  GemmArgs g{};
+  g.epi = EPI_PLAIN;
+  g.N = static_cast<int>(n);
+  const int bn = gemm_block_n(g);
+  CUtensorMap ta, tb;
+  int rc = gemm_common(g, ta, tb, a, b, m, n, k, mode, bn);
+  if (rc) return rc;
+  if (out_dtype == M5B_I32) {
+    // Raw INT32 accumulators: INT8 operands, no scales and no epilogue.
+    if (mode != M5B_MODE_INT8)
+      return fail(M5B_EUNSUPPORTED, "int32 accumulator output requires INT8 operands");
+    if (a_scales || b_scales || bias || bias_row_map || residual || gate || gate_row_map)
+      return fail(M5B_EINVAL, "int32 accumulator output takes no scales, bias or gate");
+    if (!out) return fail(M5B_EINVAL, "output pointer is NULL");
+    g.out = out;
+    g.out_dtype = DT_I32;
+    return gemm_launch(ta, tb, g, bn, stream);
+  }
+  const bool quant = (mode == M5B_MODE_INT8 || mode == M5B_MODE_FP8);
+  if (quant && (!a_scales || !b_scales)) return fail(M5B_EINVAL, "scales required");
+  if (!quant && (a_scales || b_scales))
+    return fail(M5B_EINVAL, "float GEMM modes do not accept quantization scales");
+  if (!out) return fail(M5B_EINVAL, "output pointer is NULL");
+  if (out_dtype != M5B_BF16 && out_dtype != M5B_F16 && out_dtype != M5B_F32)
+    return fail(M5B_EUNSUPPORTED, "output dtype must be bfloat16, float16 or float32");
+  g.quantized = quant ? 1 : 0;
+  g.a_scales = a_scales;
+  g.b_scales = b_scales;
+  g.out = out;
+  g.out_dtype = out_dtype;
+  const bool gated = residual || gate || gate_row_map;
+  if (gated) {
+    if (!residual || !gate) return fail(M5B_EINVAL, "gated GEMM requires both residual and gate");
+    if (mode != M5B_MODE_INT8 && mode != M5B_MODE_BF16)
+      return fail(M5B_EUNSUPPORTED, "gated GEMM supports INT8 and BF16 only");
+    if (out_dtype != M5B_BF16)
+      return fail(M5B_EUNSUPPORTED, "gated GEMM requires explicit BF16 output_dtype");
+    if (bias || bias_row_map)
+      return fail(M5B_EUNSUPPORTED, "combining GEMM bias and gated residual is unsupported");
+    if (gate_row_map && gate_rows <= 0)
+      return fail(M5B_EINVAL, "mapped gate must have nonempty shape [P,N]");
+    g.epi = gate_row_map ? EPI_GATE_TABLE : EPI_GATE_VEC;
+    g.residual = residual;
+    g.gate = gate;
+    g.gate_row_map = gate_row_map;
+  } else if (bias || bias_row_map) {
+    if (!bias) return fail(M5B_EINVAL, "bias_row_map requires a bias table");
+    if (mode != M5B_MODE_INT8)
+      return fail(M5B_EUNSUPPORTED, "optional GEMM bias currently supports INT8 only");
+    if (bias_row_map && bias_rows <= 0)
+      return fail(M5B_EINVAL, "mapped bias must have nonempty shape [P,N]");
+    g.epi = bias_row_map ? EPI_BIAS_TABLE : EPI_BIAS_VEC;
+    g.bias = bias;
+    g.bias_row_map = bias_row_map;
+  }
+  return gemm_launch(ta, tb, g, bn, stream);
+}
+
+int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
+                           int mode, const float* a_scales, const float* b_scales,
+                           const void* gamma, const void* cos, const void* sin, int rope_half,
+                           float epsilon, void* out, void* stream) {
+  if (mode != M5B_MODE_INT8 && mode != M5B_MODE_BF16)
+    return fail(M5B_EUNSUPPORTED, "Q/K projection fusion supports INT8 or BF16 only");
+  if (m <= 0 || n <= 0 || n % 128)
+    return fail(M5B_EINVAL, "projection must have nonempty [M,N] shape with whole 128-wide heads");
+  if (mode == M5B_MODE_INT8 && k > 131071)
+    return fail(M5B_EUNSUPPORTED, "INT32 worst-case overflow bound exceeded for signed INT8");
+  if (rope_half < 1 || rope_half > 64)
+    return fail(M5B_EINVAL, "cos must have shape [M,rope_half] with rope_half in [1,64]");
+  if (!(epsilon > 0.0f) || !std::isfinite(epsilon))
+    return fail(M5B_EINVAL, "epsilon must be a positive finite real scalar");
+  if (!gamma || !cos || !sin || !out) return fail(M5B_EINVAL, "gamma, cos, sin and out are required");
+  const bool quant = mode == M5B_MODE_INT8;
+  if (quant && (!a_scales || !b_scales))
+    return fail(M5B_EINVAL, "INT8 requires float32 a_scales[M] and b_scales[N]");
+  if (!quant && (a_scales || b_scales))
+    return fail(M5B_EINVAL, "BF16 projection does not accept quantization scales");
+  if (!aligned(out, 16)) return fail(M5B_EINVAL, "output base address must be 16-byte aligned");
+  GemmArgs g{};
+  g.epi = EPI_QK;
+  CUtensorMap ta, tb;
+  int rc = gemm_common(g, ta, tb, a, b, m, n, k, mode, 128);
+  if (rc) return rc;
+  g.quantized = quant ? 1 : 0;
+  g.a_scales = a_scales;
+  g.b_scales = b_scales;
+  g.out = out;
+  g.out_dtype = M5B_BF16;
+  g.gamma = gamma;
+  g.cos = cos;
+  g.sin = sin;
+  g.rope_half = rope_half;
+  g.eps = epsilon;
+  return gemm_launch(ta, tb, g, 128, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,275 @@
+// Shared device helpers for the m5b200 sm_100a kernels.
+//
+// Everything here is plain CUDA / inline PTX for Blackwell (sm_100a):
+//   * exact-rounding scalar helpers (bf16/fp16 round trips, RNE int8, E4M3),
+//   * mbarrier / TMA / tcgen05 wrappers used by the GEMM,
+//   * bounded waits: every spin on an mbarrier gives up after a wall-clock
+//     limit, records an error code in the device status word and lets the
+//     kernel unwind, so a broken pipeline ends with an error instead of a hang.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace m5b {
+
+// ---------------------------------------------------------------------------
+// Element types understood by the row kernels (values match include/m5b200.h)
+// ---------------------------------------------------------------------------
+enum DType : int { DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2, DT_I8 = 3, DT_U8 = 4, DT_I32 = 5 };
+
+template <typename T> struct DTypeOf;
+template <> struct DTypeOf<float> { static constexpr int value = DT_F32; };
+template <> struct DTypeOf<__half> { static constexpr int value = DT_F16; };
+template <> struct DTypeOf<__nv_bfloat16> { static constexpr int value = DT_BF16; };
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// Round an FP32 value through T with round-to-nearest-even and back.
+template <typename T> __device__ __forceinline__ float round_through(float v) {
+  return to_f32(from_f32<T>(v));
+}
+
+// Load one element of a small parameter table whose dtype is only known at
+// run time (gamma / scale / shift / gate may be bf16, fp16 or fp32).
+__device__ __forceinline__ float load_param(const void* base, int dtype, int64_t i) {
+  switch (dtype) {
+    case DT_BF16: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
+    case DT_F16: return __half2float(reinterpret_cast<const __half*>(base)[i]);
+    default: return reinterpret_cast<const float*>(base)[i];
+  }
+}
+
+// Symmetric INT8 code: clip(rint(v / scale), -127, 127) with IEEE division.
+__device__ __forceinline__ int8_t int8_code(float v, float scale) {
+  float z = rintf(__fdiv_rn(v, scale));
+  z = fminf(fmaxf(z, -127.0f), 127.0f);
+  return static_cast<int8_t>(static_cast<int>(z));
+}
+
+// OCP E4M3 code with round-to-nearest-even and saturation to +-448.
+__device__ __forceinline__ uint8_t e4m3_code(float v, float scale) {
+  float z = __fdiv_rn(v, scale);
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(z, __NV_SATFINITE, __NV_E4M3));
+}
+
+// ---------------------------------------------------------------------------
+// Device status word: error codes recorded by bounded waits.
+// ---------------------------------------------------------------------------
+enum DeviceError : unsigned int {
+  DEV_OK = 0,
+  DEV_TIMEOUT_PRODUCER = 1u << 0,
+  DEV_TIMEOUT_MMA = 1u << 1,
+  DEV_TIMEOUT_EPILOGUE = 1u << 2,
+  DEV_TIMEOUT_DRAIN = 1u << 3,
+};
+
+// Wall-clock limit for a single mbarrier wait (nanoseconds).
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory address helpers and mbarriers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbarrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and records `code` in *status) when the
+// barrier phase did not complete within kWaitLimitNs, or when another role of
+// the same CTA already aborted (*abort != 0).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort, unsigned int* status,
+                                                  unsigned int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 255u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - start > kWaitLimitNs) {
+        if (status) atomicOr(status, code);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TMA (non-multicast tiled loads only)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 (5th-generation tensor cores, TMEM accumulators)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Arrive once on `bar` when every tcgen05.mma issued so far by this thread
+// has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major tile stored as rows of 128
+// bytes with the 128-byte swizzle (the layout TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B).  Stride between 8-row groups is 1024 bytes.
+__device__ __forceinline__ uint64_t smem_desc_k128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);   // start address
+  d |= static_cast<uint64_t>(1u) << 16;                      // leading byte offset (unused)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;              // stride byte offset
+  d |= static_cast<uint64_t>(1u) << 46;                      // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2u) << 61;                      // SWIZZLE_128B
+  return d;
+}
+
+// MMA kinds used by the GEMM.
+enum MmaKind : int { KIND_I8 = 0, KIND_F8 = 1, KIND_BF16 = 2, KIND_F16 = 3 };
+
+// Instruction descriptor: K-major A and B, dense, M=128.
+__host__ __device__ constexpr uint32_t make_idesc(int kind, int n) {
+  // c_format: 1 = F32, 2 = S32; a/b format: S8 -> 1, E4M3 -> 0, BF16 -> 1, F16 -> 0
+  uint32_t c_fmt = (kind == KIND_I8) ? 2u : 1u;
+  uint32_t ab_fmt = (kind == KIND_I8 || kind == KIND_BF16) ? 1u : 0u;
+  return (c_fmt << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(128 >> 4) << 24);
+}
+
+template <int KIND>
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  if constexpr (KIND == KIND_I8) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else if constexpr (KIND == KIND_F8) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
+}
+
+// Load 32 consecutive 32-bit TMEM columns of this warp's 32 lanes: thread i of
+// the warp receives lane (base_lane + i), columns [col, col + 32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|P, %1;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred)
+      : "r"(0xffffffffu));
+  return pred;
+}
+
+}  // namespace m5b

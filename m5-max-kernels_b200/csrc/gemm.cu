@@ -1,0 +1,469 @@
+// Persistent tcgen05 GEMM with fused per-token x per-channel scale epilogues.
+//
+//   C[m, n] = epilogue( sum_k A[m, k] * B[n, k] )        A: [M, K], B: [N, K], both K-major
+//
+// Reference operator: src/m5kernels/metal.py:237-348 (gemm) with the epilogue
+// strings at metal.py:167-207, and the Q/K projection + RMSNorm + RoPE of
+// src/m5kernels/qk_rope.py:120-182 (shaders/qk_rope_projection.metal,
+// shaders/qk_rope_body.metal).
+//
+// Structure (one CTA per SM, 6 warps):
+//   warp 0     TMA producer: 128-byte K slices of A (128 rows) and B (BN rows)
+//              into a STAGES-deep ring of 128B-swizzled shared-memory tiles.
+//   warp 1     TMEM allocator + single-thread tcgen05.mma issuer
+//              (kind::i8 -> s32, kind::f8f6f4 E4M3 -> f32, kind::f16 -> f32),
+//              M=128, N=BN, K=32 bytes per instruction; tcgen05.commit frees a
+//              ring slot when its MMAs retire.
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator (thread = one output
+//              row), scale / bias / gate / RMS+RoPE in registers, direct
+//              vectorised global stores.
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
+// the MMAs of tile i+1.  Tiles are walked in grouped-M order, CTA b taking
+// tiles b, b + grid, ...  No TMA multicast is used anywhere.
+//
+// Rounding contract (bit-reproducible, mirrored by the C oracle):
+//   quantized:  v = fp32(acc) * sa[m] * sb[n]   (int32 -> fp32 RNE, then two
+//               IEEE multiplies in that order, no contraction)
+//   bias:       v = v + bias                    (IEEE add)
+//   gate:       out = fma(bf16(v), gate, R)     (bf16 x bf16 product is exact)
+//   output:     RNE to the output dtype.
+#include "common.cuh"
+#include "m5b_internal.h"
+
+namespace m5b {
+
+constexpr int kBM = 128;
+constexpr int kQKStride = 130;  // bf16 elements per staged Q/K row (conflict-free)
+
+template <int BN, bool QK>
+struct GemmCfg {
+  static constexpr int A_BYTES = kBM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = QK ? 5 : (BN == 256 ? 4 : 6);
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int QK_BYTES = QK ? kBM * kQKStride * 2 : 0;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + 16 + QK_BYTES;
+};
+
+__device__ __forceinline__ void tile_coords(int t, const GemmArgs& g, int& m_blk, int& n_blk) {
+  const int group_size = g.group_m * g.num_n_blocks;
+  const int group = t / group_size;
+  const int first_m = group * g.group_m;
+  const int rem = g.num_m_blocks - first_m;
+  const int gm = rem < g.group_m ? rem : g.group_m;
+  const int in_group = t - group * group_size;
+  m_blk = first_m + in_group % gm;
+  n_blk = in_group / gm;
+}
+
+template <int KIND>
+__device__ __forceinline__ float acc_value(uint32_t bits) {
+  if constexpr (KIND == KIND_I8)
+    return __int2float_rn(static_cast<int>(bits));
+  else
+    return __uint_as_float(bits);
+}
+
+__device__ __forceinline__ float bf16_load(const void* base, int64_t i) {
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
+}
+__device__ __forceinline__ float bf16_round(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// Plain / bias / gate epilogue for one thread's 32 consecutive columns.
+template <int KIND>
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t (&r)[32],
+                                               int64_t row, int col0, float sa) {
+  const int N = g.N;
+  const bool full = (col0 + 32 <= N);
+  if (g.out_dtype == DT_I32) {  // raw INT32 accumulators (no epilogue arithmetic)
+    if (row >= g.M) return;
+    int32_t* o = reinterpret_cast<int32_t*>(g.out) + row * int64_t(N) + col0;
+    if (full && (N % 4) == 0) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<int4*>(o + i) = make_int4(int(r[i]), int(r[i + 1]), int(r[i + 2]), int(r[i + 3]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) o[i] = int(r[i]);
+    }
+    return;
+  }
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float x = acc_value<KIND>(r[i]);
+    if (g.quantized) {
+      const int col = col0 + i;
+      const float sb = (full || col < N) ? __ldg(g.b_scales + (col < N ? col : 0)) : 0.0f;
+      x = __fmul_rn(__fmul_rn(x, sa), sb);
+    }
+    v[i] = x;
+  }
+  if (row >= g.M) return;
+  const int64_t base = row * int64_t(N) + col0;
+  if (g.epi == EPI_BIAS_VEC || g.epi == EPI_BIAS_TABLE) {
+    const int64_t boff = (g.epi == EPI_BIAS_TABLE) ? int64_t(g.bias_row_map[row]) * N : 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (full || col0 + i < N) v[i] = __fadd_rn(v[i], __ldg(g.bias + boff + col0 + i));
+  } else if (g.epi == EPI_GATE_VEC || g.epi == EPI_GATE_TABLE) {
+    const int64_t goff = (g.epi == EPI_GATE_TABLE) ? int64_t(g.gate_row_map[row]) * N : 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (full || col0 + i < N) {
+        const float branch = bf16_round(v[i]);
+        const float gate = bf16_load(g.gate, goff + col0 + i);
+        const float res = bf16_load(g.residual, base + i);
+        v[i] = __fmaf_rn(branch, gate, res);
+      }
+    }
+  }
+  // store
+  if (g.out_dtype == DT_F32) {
+    float* o = reinterpret_cast<float*>(g.out) + base;
+    if (full && (N % 4) == 0) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) o[i] = v[i];
+    }
+  } else if (g.out_dtype == DT_F16) {
+    __half* o = reinterpret_cast<__half*>(g.out) + base;
+    if (full && (N % 8) == 0) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 pk;
+        __half* h = reinterpret_cast<__half*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(v[i + e]);
+        *reinterpret_cast<uint4*>(o + i) = pk;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) o[i] = __float2half_rn(v[i]);
+    }
+  } else {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + base;
+    if (full && (N % 8) == 0) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 pk;
+        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[e] = __float2bfloat16_rn(v[i + e]);
+        *reinterpret_cast<uint4*>(o + i) = pk;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) o[i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+template <int KIND, int BN, bool QK>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_b, const GemmArgs g) {
+  using Cfg = GemmCfg<BN, QK>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int K_ELEMS = (KIND == KIND_BF16 || KIND == KIND_F16) ? 64 : 128;
+  constexpr uint32_t IDESC = make_idesc(KIND, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __nv_bfloat16* qk_stage =
+      reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(full) + Cfg::BAR_BYTES + 16);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = g.num_m_blocks * g.num_n_blocks;
+  const int nkb = g.num_k_blocks;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        int m_blk, n_blk;
+        tile_coords(t, g, m_blk, n_blk);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, g.status,
+                                 DEV_TIMEOUT_PRODUCER))
+            break;
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmap_a, &full[stage], kb * K_ELEMS,
+                      m_blk * kBM);
+          tma_load_2d(sB + stage * Cfg::B_BYTES, &tmap_b, &full[stage], kb * K_ELEMS,
+                      n_blk * BN);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Drain: wait (bounded) until the copies already issued into the
+        // ring have landed, so no TMA write targets this CTA after it exits.
+        int s = stage, ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          s = (s == 0) ? STAGES - 1 : s - 1;
+          if (s == STAGES - 1) ph ^= 1;
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[s], ph)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              atomicOr(g.status, DEV_TIMEOUT_DRAIN);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, abort_flag, g.status,
+                               DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, g.status, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            tc_mma<KIND>(d_tmem, smem_desc_k128(a_base + k * 32), smem_desc_k128(b_base + k * 32),
+                         IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[acc]);
+      }
+      if (!ok) {
+        // Aborted: let every MMA already issued retire before TMEM is freed.
+        tc_commit(drain);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(g.status, DEV_TIMEOUT_DRAIN);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      int m_blk, n_blk;
+      tile_coords(t, g, m_blk, n_blk);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, g.status,
+                             DEV_TIMEOUT_EPILOGUE))
+        break;
+      __syncwarp();
+      tc_fence_after();
+      const int64_t row = int64_t(m_blk) * kBM + row_in_tile;
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const float sa = (g.quantized && row < g.M) ? __ldg(g.a_scales + row) : 1.0f;
+      if constexpr (!QK) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+          epilogue_chunk<KIND>(g, r, row, n_blk * BN + c * 32, sa);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      } else {
+        // Pass 1: BF16 projection z, its square sum (sequential over the 128
+        // head channels) and a private staged copy of this row.
+        __nv_bfloat16* zrow = qk_stage + row_in_tile * kQKStride;
+        float sumsq = 0.0f;
+        const int head = n_blk;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float z0 = acc_value<KIND>(r[i]), z1 = acc_value<KIND>(r[i + 1]);
+            if (g.quantized) {
+              const int col = head * 128 + c * 32 + i;
+              z0 = __fmul_rn(__fmul_rn(z0, sa), __ldg(g.b_scales + col));
+              z1 = __fmul_rn(__fmul_rn(z1, sa), __ldg(g.b_scales + col + 1));
+            }
+            const __nv_bfloat162 zz = __floats2bfloat162_rn(z0, z1);
+            const float f0 = __low2float(zz), f1 = __high2float(zz);
+            sumsq = __fmaf_rn(f0, f0, sumsq);
+            sumsq = __fmaf_rn(f1, f1, sumsq);
+            *reinterpret_cast<__nv_bfloat162*>(zrow + c * 32 + i) = zz;
+          }
+        }
+        // The accumulator is no longer needed: hand it back to the MMA warp.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (row < g.M) {
+          const float inv =
+              __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, 128.0f), g.eps)));
+          const int R = g.rope_half;
+          const __nv_bfloat16* cs = reinterpret_cast<const __nv_bfloat16*>(g.cos) + row * R;
+          const __nv_bfloat16* sn = reinterpret_cast<const __nv_bfloat16*>(g.sin) + row * R;
+          const __nv_bfloat16* gm = reinterpret_cast<const __nv_bfloat16*>(g.gamma);
+          __nv_bfloat16* yrow =
+              reinterpret_cast<__nv_bfloat16*>(g.out) + (int64_t(head) * g.M + row) * 128;
+#pragma unroll 1
+          for (int j0 = 0; j0 < 128; j0 += 8) {
+            uint4 pk;
+            __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int j = j0 + e;
+              const float uj = __fmul_rn(__fmul_rn(__bfloat162float(zrow[j]), inv),
+                                         __bfloat162float(gm[j]));
+              float out = uj;
+              if (j < 2 * R) {
+                const int p = j < R ? j + R : j - R;
+                const int ang = j < R ? j : j - R;
+                const float up = __fmul_rn(__fmul_rn(__bfloat162float(zrow[p]), inv),
+                                           __bfloat162float(gm[p]));
+                const float c = __bfloat162float(cs[ang]);
+                const float s = __bfloat162float(sn[ang]);
+                out = j < R ? __fsub_rn(__fmul_rn(uj, c), __fmul_rn(up, s))
+                            : __fadd_rn(__fmul_rn(uj, c), __fmul_rn(up, s));
+              }
+              h[e] = __float2bfloat16_rn(out);
+            }
+            *reinterpret_cast<uint4*>(yrow + j0) = pk;
+          }
+        }
+      }
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+template <int KIND, int BN, bool QK>
+static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
+                            int grid, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN, QK>;
+  auto kern = gemm_tc_kernel<KIND, BN, QK>;
+  static bool configured = false;  // attribute is per function, idempotent
+  if (!configured) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ta, tb, g);
+  return cudaGetLastError();
+}
+
+int gemm_block_n(const GemmArgs& g) {
+  if (g.epi == EPI_QK) return 128;
+  return g.N <= 128 ? 128 : 256;
+}
+
+cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, int bn,
+                        int grid, cudaStream_t stream) {
+  const bool qk = g.epi == EPI_QK;
+#define M5B_KIND_CASE(KIND_)                                                   \
+  case KIND_:                                                                  \
+    if (qk) return launch_k<KIND_, 128, true>(ta, tb, g, grid, stream);        \
+    if (bn == 128) return launch_k<KIND_, 128, false>(ta, tb, g, grid, stream); \
+    return launch_k<KIND_, 256, false>(ta, tb, g, grid, stream);
+  switch (g.kind) {
+    M5B_KIND_CASE(KIND_I8)
+    M5B_KIND_CASE(KIND_F8)
+    M5B_KIND_CASE(KIND_BF16)
+    M5B_KIND_CASE(KIND_F16)
+    default: return cudaErrorInvalidValue;
+  }
+#undef M5B_KIND_CASE
+}
+
+}  // namespace m5b

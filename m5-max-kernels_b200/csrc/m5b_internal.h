@@ -1,0 +1,81 @@
+// Launch-argument structs shared by the kernels (prep.cu, gemm.cu) and the
+// C-ABI layer (api.cu).  Nothing in here is exported from the library.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace m5b {
+
+enum NormKind : int { NORM_NONE = 0, NORM_RMS = 1, NORM_LAYER = 2 };
+enum RowOut : int { OUT_INT8 = 0, OUT_E4M3 = 1, OUT_F32 = 2 };
+
+struct RowPrepArgs {
+  const void* x;               // [rows, K] input (the residual R when gated)
+  const void* branch;          // [rows, K] gated branch, or null
+  const void* gate;            // [K] or [P, K] gate table, or null
+  const int32_t* gate_row_map; // [rows] gate table index, or null
+  int gate_dtype;
+  const void* gamma;           // [K] (norm only)
+  const void* scale;           // [K] or [P, K] AdaLN scale (norm only)
+  const void* shift;           // [K] or [P, K] AdaLN shift (norm only)
+  int gamma_dtype, scale_dtype, shift_dtype;
+  const int32_t* row_map;      // [rows] modulation table index, or null
+  const int8_t* signs;         // [K] +-1 Hadamard signs, or null (all +1)
+  int64_t rows, K;
+  int norm;                    // NormKind
+  float eps;
+  int round_output;            // round the modulated value through the input dtype
+  float inv_sqrt_block;        // fp32(1/sqrt(block)) for the rotation
+  int warps;                   // warps per CTA (row_prep_warps)
+  int vec_ok;                  // 16-byte vector loads / stores are aligned
+  void* q;                     // [rows, K] int8 or E4M3 codes
+  float* s;                    // [rows] per-row scales
+  float* y;                    // [rows, K] fp32 rotated values (OUT_F32)
+  void* r_out;                 // [rows, K] updated residual (gated)
+};
+
+int row_prep_warps(int64_t K, int block);
+cudaError_t launch_row_prep(const RowPrepArgs& a, int x_dtype, int block, int out,
+                            cudaStream_t stream);
+
+// GEMM epilogues.  C[m, n] for the plain epilogues, [N/128, M, 128] for QK.
+enum Epilogue : int {
+  EPI_PLAIN = 0,       // out = acc (float GEMM) or (acc * sa[m]) * sb[n] (quantized)
+  EPI_BIAS_VEC = 1,    // ... + bias[n]
+  EPI_BIAS_TABLE = 2,  // ... + bias[bias_row_map[m], n]
+  EPI_GATE_VEC = 3,    // out = R[m, n] + bf16(branch) * gate[n]
+  EPI_GATE_TABLE = 4,  // out = R[m, n] + bf16(branch) * gate[gate_row_map[m], n]
+  EPI_QK = 5,          // bf16 branch -> per-head RMSNorm * gamma -> split-half RoPE
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int kind;                   // MmaKind
+  int epi;                    // Epilogue
+  int quantized;              // apply a_scales / b_scales
+  const float* a_scales;      // [M]
+  const float* b_scales;      // [N]
+  void* out;                  // output
+  int out_dtype;              // DT_BF16 / DT_F16 / DT_F32 (plain epilogues)
+  const float* bias;          // [N] or [P, N]
+  const int32_t* bias_row_map;
+  const void* residual;       // [M, N] bf16
+  const void* gate;           // [N] or [P, N] bf16
+  const int32_t* gate_row_map;
+  const void* gamma;          // [128] bf16 (QK)
+  const void* cos;            // [M, R] bf16 (QK)
+  const void* sin;            // [M, R] bf16 (QK)
+  int rope_half;
+  float eps;
+  int num_m_blocks, num_n_blocks, num_k_blocks;
+  int group_m;
+  unsigned int* status;       // device status word (bounded-wait errors)
+};
+
+cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, int bn,
+                        int grid, cudaStream_t stream);
+int gemm_block_n(const GemmArgs& g);
+
+}  // namespace m5b

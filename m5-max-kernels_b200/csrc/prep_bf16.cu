@@ -1,0 +1,8 @@
+// Row-preparation kernel instantiations for __nv_bfloat16 inputs (see prep_impl.cuh).
+#include "prep_impl.cuh"
+
+namespace m5b {
+cudaError_t launch_row_prep_bf16(const RowPrepArgs& a, int block, int out, cudaStream_t stream) {
+  return launch_o<__nv_bfloat16>(a, block, out, stream);
+}
+}  // namespace m5b

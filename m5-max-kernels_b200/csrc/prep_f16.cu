@@ -1,0 +1,8 @@
+// Row-preparation kernel instantiations for __half inputs (see prep_impl.cuh).
+#include "prep_impl.cuh"
+
+namespace m5b {
+cudaError_t launch_row_prep_f16(const RowPrepArgs& a, int block, int out, cudaStream_t stream) {
+  return launch_o<__half>(a, block, out, stream);
+}
+}  // namespace m5b

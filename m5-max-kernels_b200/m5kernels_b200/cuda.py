@@ -1,0 +1,173 @@
+"""quantize / gemm on B200 tensor cores: the `cuda-b200` twin of m5kernels.metal.
+
+Operator contracts follow src/m5kernels/metal.py (reference): the same
+argument names and meanings, ValueError for contract violations and
+NotImplementedError for unsupported shapes or semantics.  Inputs are never
+mutated and outputs are freshly allocated torch CUDA tensors.  The `tile`
+argument is accepted for signature compatibility and validated; the B200
+kernels choose their own tiles (128 x 256 tcgen05 tiles, 128 x 128 for
+narrow outputs).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr
+
+FLOAT_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+
+
+def _validate_tile(tile):
+    if not isinstance(tile, (tuple, list)) or len(tile) != 4:
+        raise ValueError("tile must contain TM, TN, SIMD groups and M swizzle")
+
+
+def quantize(x: torch.Tensor, mode: str, tag: str = "packed"):
+    """Per-row symmetric quantization -> (codes, fp32 scales).
+
+    int8: scale = amax/127, codes = clip(rint(x/scale), +-127) (int8).
+    fp8:  scale = amax/448, codes = E4M3 bits (uint8), RNE, saturating.
+    All-zero rows use scale 1.  Mirrors src/m5kernels/metal.py:106-123.
+    """
+    del tag
+    if mode == "mxint8":
+        raise NotImplementedError("MXINT8 packing is not part of the cuda-b200 backend")
+    if mode not in ("int8", "fp8"):
+        raise ValueError(f"unknown quantization mode {mode!r}")
+    if x.dim() != 2 or 0 in x.shape:
+        raise ValueError("input must have nonempty shape [rows, K]")
+    if x.dtype not in FLOAT_DTYPES:
+        raise ValueError("input dtype must be float16, bfloat16 or float32")
+    dev = _lib.require_cuda(x)
+    x = x.contiguous()
+    rows, k = x.shape
+    q = torch.empty((rows, k), dtype=torch.int8 if mode == "int8" else torch.uint8, device=dev)
+    s = torch.empty((rows,), dtype=torch.float32, device=dev)
+    check(_lib.lib().m5b_quantize(ptr(x), _lib.DTYPE_CODE[x.dtype], rows, k, _lib.MODE[mode],
+                                  ptr(q), ptr(s), _lib.stream_handle(dev)))
+    return q, s
+
+
+def _pad_k(t: torch.Tensor, multiple: int) -> torch.Tensor:
+    k = t.shape[1]
+    pad = (-k) % multiple
+    if pad == 0:
+        return t
+    out = torch.zeros((t.shape[0], k + pad), dtype=t.dtype, device=t.device)
+    out[:, :k] = t
+    return out
+
+
+def gemm(a, b, mode="bf16", tile=(64, 64, 4, 1), a_scales=None, b_scales=None,
+         output_dtype=None, bias=None, bias_row_map=None, residual=None, gate=None,
+         gate_row_map=None):
+    """A[M,K] @ B[N,K].T with INT32 (int8) or FP32 accumulation and a fused epilogue.
+
+    Quantized modes: out = (float(acc) * a_scales[m]) * b_scales[n].
+    INT8 optionally adds an FP32 bias [N] or a bias table [P,N] selected by
+    int32 bias_row_map[M].  INT8/BF16 optionally fuse the gated residual
+    out = R + bf16(branch) * gate with BF16 residual [M,N] and gate [N] or
+    [P,N] + gate_row_map.  Mirrors src/m5kernels/metal.py:237-348; output
+    dtype defaults to float32 like the reference.  output_dtype=torch.int32
+    (INT8, no scales) returns the raw INT32 accumulators.
+    """
+    _validate_tile(tile)
+    if a.dim() != 2 or b.dim() != 2:
+        raise ValueError("A and B must be matrices")
+    m, k = a.shape
+    n, kb = b.shape
+    if k != kb:
+        raise ValueError("K mismatch")
+    if mode not in _lib.MODE:
+        if mode in ("fp32", "mxint8"):
+            raise NotImplementedError(f"{mode} GEMM is not part of the cuda-b200 backend")
+        raise ValueError(f"unknown GEMM mode {mode!r}")
+    if mode == "fp8" and k % 128:
+        raise NotImplementedError(
+            "FP8 requires K/row stride divisible by 128; padding is not implicit")
+    if mode == "int8" and k > 133144:
+        raise NotImplementedError("INT32 worst-case overflow bound exceeded")
+    expected = {"int8": (torch.int8,), "fp8": (torch.uint8,), "bf16": (torch.bfloat16,),
+                "fp16": (torch.float16,)}[mode]
+    if a.dtype not in expected or b.dtype not in expected:
+        raise ValueError("operand dtypes must match the declared mode")
+    out_dtype = output_dtype or torch.float32
+    gated = residual is not None or gate is not None or gate_row_map is not None
+    if gated:
+        if residual is None or gate is None:
+            raise ValueError("gated GEMM requires both residual and gate")
+        if mode not in ("int8", "bf16"):
+            raise NotImplementedError("gated GEMM supports INT8 and BF16 only")
+        if output_dtype is None or output_dtype != torch.bfloat16:
+            raise NotImplementedError("gated GEMM requires explicit BF16 output_dtype")
+        if bias is not None or bias_row_map is not None:
+            raise NotImplementedError("combining GEMM bias and gated residual is unsupported")
+        if tuple(residual.shape) != (m, n) or residual.dtype != torch.bfloat16:
+            raise ValueError("residual must have BF16 dtype and shape [M,N]")
+        if gate.dtype != torch.bfloat16:
+            raise ValueError("gate must have BF16 dtype")
+        if gate_row_map is None:
+            if tuple(gate.shape) != (n,):
+                raise ValueError("gate must have shape [N] without gate_row_map")
+        else:
+            if gate.dim() != 2 or 0 in gate.shape or gate.shape[1] != n:
+                raise ValueError("mapped gate must have nonempty shape [P,N]")
+            if tuple(gate_row_map.shape) != (m,) or gate_row_map.dtype != torch.int32:
+                raise ValueError("gate_row_map must be an int32 vector of length M")
+        if mode == "int8" and (
+            a_scales is None or b_scales is None or tuple(a_scales.shape) != (m,)
+            or tuple(b_scales.shape) != (n,) or a_scales.dtype != torch.float32
+            or b_scales.dtype != torch.float32
+        ):
+            raise ValueError("gated INT8 GEMM requires float32 scales with shapes [M] and [N]")
+    if bias is None:
+        if bias_row_map is not None:
+            raise ValueError("bias_row_map requires a bias table")
+    else:
+        if mode != "int8":
+            raise NotImplementedError("optional GEMM bias currently supports INT8 only")
+        if bias.dtype != torch.float32:
+            raise ValueError("bias must have float32 dtype")
+        if bias_row_map is None:
+            if tuple(bias.shape) != (n,):
+                raise ValueError("bias must have shape [N] without bias_row_map")
+        else:
+            if bias.dim() != 2 or 0 in bias.shape or bias.shape[1] != n:
+                raise ValueError("mapped bias must have nonempty shape [P,N]")
+            if tuple(bias_row_map.shape) != (m,) or bias_row_map.dtype != torch.int32:
+                raise ValueError("bias_row_map must be an int32 vector of length M")
+    quant = mode in ("int8", "fp8")
+    if out_dtype == torch.int32:
+        if mode != "int8" or a_scales is not None or b_scales is not None or gated or bias is not None:
+            raise ValueError("int32 output returns raw INT8 accumulators without scales")
+    elif quant:
+        if a_scales is None or b_scales is None:
+            raise ValueError("scales required")
+        if (tuple(a_scales.shape) != (m,) or tuple(b_scales.shape) != (n,)
+                or a_scales.dtype != torch.float32 or b_scales.dtype != torch.float32):
+            raise ValueError("scales must be float32 vectors of length M and N")
+    if out_dtype not in (torch.bfloat16, torch.float16, torch.float32, torch.int32):
+        raise NotImplementedError("output dtype must be bfloat16, float16 or float32")
+    dev = _lib.require_cuda(a, b, a_scales, b_scales, bias, bias_row_map, residual, gate,
+                            gate_row_map)
+    if m == 0 or n == 0 or k == 0:
+        raise ValueError("A and B must be nonempty matrices")
+    # TMA needs 16-byte row strides; zero K-padding leaves every sum unchanged.
+    elem = 1 if mode in ("int8", "fp8") else 2
+    a = _pad_k(a.contiguous(), 16 // elem)
+    b = _pad_k(b.contiguous(), 16 // elem)
+    kp = a.shape[1]
+    args = [t.contiguous() if t is not None else None
+            for t in (a_scales, b_scales, bias, bias_row_map, residual, gate, gate_row_map)]
+    a_scales, b_scales, bias, bias_row_map, residual, gate, gate_row_map = args
+    out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    check(_lib.lib().m5b_gemm(
+        ptr(a), ptr(b), m, n, kp, _lib.MODE[mode], ptr(a_scales), ptr(b_scales), ptr(out),
+        _lib.DTYPE_CODE[out_dtype], ptr(bias), ptr(bias_row_map),
+        bias.shape[0] if (bias is not None and bias.dim() == 2) else 0,
+        ptr(residual), ptr(gate), ptr(gate_row_map),
+        gate.shape[0] if (gate is not None and gate.dim() == 2) else 0,
+        _lib.stream_handle(dev)))
+    return out

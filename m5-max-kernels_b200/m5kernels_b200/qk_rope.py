@@ -1,0 +1,108 @@
+"""Head-aligned Q/K projection + per-head RMSNorm + split-half RoPE on B200.
+
+Twin of m5kernels.qk_rope.projection_qk_rope (src/m5kernels/qk_rope.py:120-182).
+One tcgen05 GEMM tile of 128 x 128 is exactly one head of 128 rows; its
+epilogue rounds the projection to BF16, computes the row's RMS over the
+head's 128 channels, applies gamma and rotates the pairs (j, j + R) for j < R,
+and writes the head-major [H, M, 128] BF16 output.  Boundaries: BF16
+projection, FP32 RMS/gamma/RoPE, BF16 output (no BF16 norm intermediate).
+"""
+
+from __future__ import annotations
+
+import math
+import struct
+from numbers import Real
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr
+
+HEAD_DIM = 128
+
+
+def _epsilon(epsilon):
+    if (isinstance(epsilon, bool) or not isinstance(epsilon, Real) or not math.isfinite(epsilon)
+            or epsilon <= 0):
+        raise ValueError("epsilon must be a positive finite real scalar")
+    try:
+        value = struct.unpack("=f", struct.pack("=f", float(epsilon)))[0]
+    except OverflowError:
+        raise ValueError("epsilon must remain finite and positive in float32") from None
+    if not math.isfinite(value) or value <= 0:
+        raise ValueError("epsilon must remain finite and positive in float32")
+    return value
+
+
+def _validate_norm(m, n, gamma, cos, sin, epsilon):
+    if m <= 0 or n <= 0 or n % HEAD_DIM:
+        raise ValueError("projection must have nonempty [M,N] shape with whole 128-wide heads")
+    if tuple(gamma.shape) != (HEAD_DIM,) or gamma.dtype != torch.bfloat16:
+        raise ValueError("gamma must be a shared bfloat16 vector of length 128")
+    if cos.dim() != 2 or cos.shape[0] != m or not 1 <= cos.shape[1] <= HEAD_DIM // 2:
+        raise ValueError("cos must have shape [M,rope_half] with rope_half in [1,64]")
+    if tuple(sin.shape) != tuple(cos.shape) or cos.dtype != torch.bfloat16 or sin.dtype != torch.bfloat16:
+        raise ValueError("cos and sin must have matching bfloat16 [M,rope_half] shapes")
+    return cos.shape[1], _epsilon(epsilon)
+
+
+def projection_qk_rope(a, b, gamma, cos, sin, mode="int8", tile=(32, 128, 4, 1), *,
+                       a_scales=None, b_scales=None, epsilon=1e-5):
+    """Return BF16 [heads, M, 128] Q or K after projection, RMSNorm and RoPE."""
+    if mode not in ("int8", "bf16"):
+        raise NotImplementedError("Q/K projection fusion supports INT8 or BF16 only")
+    if a.dim() != 2 or b.dim() != 2 or 0 in a.shape or 0 in b.shape:
+        raise ValueError("A and B must be nonempty matrices")
+    m, k = a.shape
+    n, kb = b.shape
+    if k != kb:
+        raise ValueError("K mismatch")
+    expected = torch.int8 if mode == "int8" else torch.bfloat16
+    if a.dtype != expected or b.dtype != expected:
+        raise ValueError(f"A and B must both have {mode} dtype")
+    if mode == "int8":
+        if k > 131071:
+            raise NotImplementedError("INT32 worst-case overflow bound exceeded for signed INT8")
+        if (a_scales is None or b_scales is None or tuple(a_scales.shape) != (m,)
+                or tuple(b_scales.shape) != (n,) or a_scales.dtype != torch.float32
+                or b_scales.dtype != torch.float32):
+            raise ValueError("INT8 requires float32 a_scales[M] and b_scales[N]")
+    elif a_scales is not None or b_scales is not None:
+        raise ValueError("BF16 projection does not accept quantization scales")
+    rope_half, eps = _validate_norm(m, n, gamma, cos, sin, epsilon)
+    if not isinstance(tile, (tuple, list)) or len(tile) != 4:
+        raise ValueError("tile must contain TM, TN, SIMD groups and M swizzle")
+    dev = _lib.require_cuda(a, b, gamma, cos, sin, a_scales, b_scales)
+    elem = 1 if mode == "int8" else 2
+    pad = (-k) % (16 // elem)
+    a, b = a.contiguous(), b.contiguous()
+    if pad:
+        a = torch.nn.functional.pad(a, (0, pad))
+        b = torch.nn.functional.pad(b, (0, pad))
+    gamma, cos, sin = gamma.contiguous(), cos.contiguous(), sin.contiguous()
+    a_scales = a_scales.contiguous() if a_scales is not None else None
+    b_scales = b_scales.contiguous() if b_scales is not None else None
+    out = torch.empty((n // HEAD_DIM, m, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    check(_lib.lib().m5b_projection_qk_rope(
+        ptr(a), ptr(b), m, n, a.shape[1], _lib.MODE[mode], ptr(a_scales), ptr(b_scales),
+        ptr(gamma), ptr(cos), ptr(sin), rope_half, eps, ptr(out), _lib.stream_handle(dev)))
+    return out
+
+
+def rope_tables(m: int, rope_half: int = 64, theta: float = 10000.0, *, positions=None,
+                device=None):
+    """BF16 cos/sin tables [M, R] for split-half RoPE.
+
+    angle[p, j] = p * theta ** (-j / R) for j < R (positions 0..M-1 unless
+    given), evaluated in float64 and rounded to BF16 once.  This is the table
+    definition the B200 workloads use (the reference takes cos/sin as inputs).
+    """
+    pos = torch.arange(m, dtype=torch.float64) if positions is None else positions.double().cpu()
+    inv_freq = theta ** (-torch.arange(rope_half, dtype=torch.float64) / rope_half)
+    ang = pos[:, None] * inv_freq[None, :]
+    cos = torch.cos(ang).to(torch.float32).to(torch.bfloat16)
+    sin = torch.sin(ang).to(torch.float32).to(torch.bfloat16)
+    if device is not None:
+        cos, sin = cos.to(device), sin.to(device)
+    return cos, sin

@@ -1,0 +1,366 @@
+/*
+ * m5_oracle.c — CPU restatement of the quantized-projection hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker: tests/, the smoke()
+ * entry point and bench.py's CPU-baseline leg are the only callers.  No
+ * product code path links, loads or calls it.
+ *
+ * What it restates (reference file:line, 9Tempest/m5-max-kernels):
+ *   per-token INT8 / E4M3 quantization   src/m5kernels/numerics.py:29-46 (quantize_reference),
+ *                                          numerics.py:17-26 (fp8_encode)
+ *   signed block Hadamard X D H          src/m5kernels/hadamard_reference.py:26-68,
+ *                                          shaders/hadamard.metal:1-26
+ *   norm + AdaLN modulation              src/m5kernels/norm_hadamard_reference.py:24-64,
+ *                                          shaders/norm_hadamard.metal:1-121
+ *   gated residual update                src/m5kernels/gated_residual_reference.py:21-60,
+ *                                          norm_hadamard.py:62-70
+ *   W8A8 GEMM + scale/bias/gate epilogue src/m5kernels/metal.py:167-207
+ *   Q/K RMSNorm + split-half RoPE        src/m5kernels/qk_rope_reference.py:45-134,
+ *                                          shaders/qk_rope_body.metal:1-20
+ *
+ * The reference's own references are float64; its GPU kernels round in FP32
+ * with an unspecified reduction order, which is why the reference accepts a
+ * one-code difference.  This restatement instead fixes the FP32 order so it is
+ * bit-comparable with the CUDA kernels:
+ *   - row reductions: each (warp, lane) accumulates its elements sequentially
+ *     in (slot, slice, element) order, lanes combine with a xor butterfly
+ *     (offsets 16, 8, 4, 2, 1), warps are summed 0..W-1 in order;
+ *   - sum of squares uses fmaf(x, x, acc), the centered LayerNorm pass
+ *     fmaf(d, d, acc) with d = x - mean;
+ *   - Hadamard butterflies in natural Sylvester order with increasing stride,
+ *     then one multiply by fp32(1/sqrt(B));
+ *   - every other operation is a single IEEE-754 binary32 operation in the
+ *     order written (compile with -ffp-contract=off).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define O_F32 0
+#define O_F16 1
+#define O_BF16 2
+
+#define NORM_NONE 0
+#define NORM_RMS 1
+#define NORM_LAYER 2
+
+#define OUT_INT8 0
+#define OUT_E4M3 1
+#define OUT_F32 2
+
+#define MAX_VALUES 64
+
+/* ------------------------------------------------------------------ dtypes */
+static float bf16_to_f32(uint16_t h) {
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+static uint16_t f32_to_bf16(float f) { /* round to nearest even; inputs are finite */
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  uint32_t rounding = 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)((u + rounding) >> 16);
+}
+
+static float f16_to_f32(uint16_t h) {
+  _Float16 v;
+  memcpy(&v, &h, 2);
+  return (float)v;
+}
+
+static uint16_t f32_to_f16(float f) {
+  _Float16 v = (_Float16)f; /* IEEE round to nearest even */
+  uint16_t h;
+  memcpy(&h, &v, 2);
+  return h;
+}
+
+static float load_elem(const void* base, int dtype, int64_t i) {
+  switch (dtype) {
+    case O_BF16: return bf16_to_f32(((const uint16_t*)base)[i]);
+    case O_F16: return f16_to_f32(((const uint16_t*)base)[i]);
+    default: return ((const float*)base)[i];
+  }
+}
+
+static void store_elem(void* base, int dtype, int64_t i, float v) {
+  switch (dtype) {
+    case O_BF16: ((uint16_t*)base)[i] = f32_to_bf16(v); break;
+    case O_F16: ((uint16_t*)base)[i] = f32_to_f16(v); break;
+    default: ((float*)base)[i] = v; break;
+  }
+}
+
+static float round_through(float v, int dtype) {
+  switch (dtype) {
+    case O_BF16: return bf16_to_f32(f32_to_bf16(v));
+    case O_F16: return f16_to_f32(f32_to_f16(v));
+    default: return v;
+  }
+}
+
+/* ------------------------------------------------------------------ codes */
+static int8_t int8_code(float v, float scale) {
+  float z = rintf(v / scale);
+  if (z > 127.0f) z = 127.0f;
+  if (z < -127.0f) z = -127.0f;
+  return (int8_t)(int)z;
+}
+
+/* OCP E4M3 (finite-only "fn" variant): RNE, saturate to 448 (code 0x7E). */
+uint8_t m5o_e4m3_encode(float z) {
+  const uint8_t sign = signbit(z) ? 0x80 : 0x00;
+  const float a = fabsf(z);
+  if (!(a < 448.0f)) return sign | 0x7E;
+  if (a < 0.015625f) { /* subnormal range: step 2^-9; code 8 is the first normal */
+    const float m = rintf(a * 512.0f);
+    return sign | (uint8_t)(int)m;
+  }
+  int e2;
+  const float f = frexpf(a, &e2); /* a = f * 2^e2, f in [0.5, 1) */
+  int exp = e2 - 1;              /* a = (2f) * 2^exp, 2f in [1, 2) */
+  float t = rintf(ldexpf(f, 4)); /* mantissa in eighths: [8, 16] */
+  if (t == 16.0f) {
+    t = 8.0f;
+    exp += 1;
+  }
+  int code = ((exp + 7) << 3) | ((int)t - 8);
+  if (code > 0x7E) code = 0x7E;
+  return sign | (uint8_t)code;
+}
+
+static uint8_t e4m3_code(float v, float scale) { return m5o_e4m3_encode(v / scale); }
+
+/* ------------------------------------------------------------------ layout */
+int m5o_row_prep_warps(int64_t K, int block) {
+  const int unit = block > 256 ? block : 256;
+  const int vpu = unit / 256;
+  const int slots = MAX_VALUES / (8 * vpu);
+  const int64_t units = (K + unit - 1) / unit;
+  int64_t w = (units + slots - 1) / slots;
+  if (w < 1) w = 1;
+  return w > 1024 ? 1024 : (int)w;
+}
+
+/* Sum of f(v[j]) over one row in the kernel's order.  kind 0: sum of v,
+ * kind 1: sum of v*v (fma), kind 2: sum of (v-mean)^2 (fma). */
+static float row_reduce(const float* v, int64_t K, int block, int W, int kind, float mean) {
+  const int unit = block > 256 ? block : 256;
+  const int vpu = unit / 256;
+  const int slots = MAX_VALUES / (8 * vpu);
+  const int units = (int)((K + unit - 1) / unit);
+  float warp_part[1024];
+  for (int w = 0; w < W; ++w) {
+    float lane_acc[32];
+    for (int l = 0; l < 32; ++l) {
+      float acc = 0.0f;
+      for (int s = 0; s < slots; ++s) {
+        const int u = s * W + w;
+        if (u >= units) continue;
+        for (int vv = 0; vv < vpu; ++vv) {
+          for (int e = 0; e < 8; ++e) {
+            const int64_t j = (int64_t)u * unit + vv * 256 + l * 8 + e;
+            if (j >= K) continue;
+            const float x = v[j];
+            if (kind == 0) {
+              acc = acc + x;
+            } else if (kind == 1) {
+              acc = fmaf(x, x, acc);
+            } else {
+              const float d = x - mean;
+              acc = fmaf(d, d, acc);
+            }
+          }
+        }
+      }
+      lane_acc[l] = acc;
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+      float nxt[32];
+      for (int l = 0; l < 32; ++l) nxt[l] = lane_acc[l] + lane_acc[l ^ off];
+      memcpy(lane_acc, nxt, sizeof(nxt));
+    }
+    warp_part[w] = lane_acc[0];
+  }
+  float t = warp_part[0];
+  for (int w = 1; w < W; ++w) t = t + warp_part[w];
+  return t;
+}
+
+static void fwht_block(float* v, int B) {
+  for (int h = 1; h < B; h <<= 1)
+    for (int i = 0; i < B; ++i)
+      if ((i & h) == 0) {
+        const float lo = v[i], hi = v[i + h];
+        v[i] = lo + hi;
+        v[i + h] = lo - hi;
+      }
+}
+
+/*
+ * One call = the row-preparation kernel over all rows.  Pointers are host
+ * arrays with the same meaning as RowPrepArgs in the CUDA library.  `block`
+ * 0 means no rotation; `norm` NORM_NONE skips normalization/modulation.
+ */
+void m5o_row_prep(const void* x, int x_dtype, const void* branch, const void* gate,
+                  int gate_dtype, const int32_t* gate_row_map, const void* gamma,
+                  int gamma_dtype, const void* scale, int scale_dtype, const void* shift,
+                  int shift_dtype, const int32_t* row_map, const int8_t* signs, int64_t rows,
+                  int64_t K, int norm, float eps, int round_output, int block, int out, void* q,
+                  float* s, float* y, void* r_out) {
+  float* v = (float*)malloc(sizeof(float) * (size_t)K);
+  const int W = m5o_row_prep_warps(K, block);
+  const float inv_sqrt_block = block > 0 ? (float)(1.0 / sqrt((double)block)) : 1.0f;
+  for (int64_t r = 0; r < rows; ++r) {
+    /* load, gated residual update */
+    const int64_t goff = (gate && gate_row_map) ? (int64_t)gate_row_map[r] * K : 0;
+    for (int64_t j = 0; j < K; ++j) {
+      float xv = load_elem(x, x_dtype, r * K + j);
+      if (branch) {
+        const float b = load_elem(branch, x_dtype, r * K + j);
+        const float g = load_elem(gate, gate_dtype, goff + j);
+        xv = round_through(fmaf(b, g, xv), x_dtype);
+        store_elem(r_out, x_dtype, r * K + j, xv);
+      }
+      v[j] = xv;
+    }
+    /* statistics */
+    float mean = 0.0f, inv = 1.0f;
+    if (norm != NORM_NONE) {
+      const float kf = (float)K;
+      const float first =
+          row_reduce(v, K, block, W, norm == NORM_LAYER ? 0 : 1, 0.0f) / kf;
+      float moment = first;
+      if (norm == NORM_LAYER) {
+        mean = first;
+        moment = row_reduce(v, K, block, W, 2, mean) / kf;
+      }
+      inv = 1.0f / sqrtf(moment + eps);
+    }
+    /* modulation, rounding, signs */
+    const int64_t moff = row_map ? (int64_t)row_map[r] * K : 0;
+    for (int64_t j = 0; j < K; ++j) {
+      float t = v[j];
+      if (norm != NORM_NONE) {
+        const float g = load_elem(gamma, gamma_dtype, j);
+        const float sc = load_elem(scale, scale_dtype, moff + j);
+        const float sh = load_elem(shift, shift_dtype, moff + j);
+        const float n = ((t - mean) * inv) * g;
+        t = fmaf(n, 1.0f + sc, sh);
+        if (round_output) t = round_through(t, x_dtype);
+      }
+      if (signs && signs[j] < 0) t = -t;
+      v[j] = t;
+    }
+    /* rotation */
+    if (block > 0) {
+      for (int64_t b0 = 0; b0 < K; b0 += block) fwht_block(v + b0, block);
+      for (int64_t j = 0; j < K; ++j) v[j] = v[j] * inv_sqrt_block;
+    }
+    if (out == OUT_F32) {
+      memcpy(y + r * K, v, sizeof(float) * (size_t)K);
+      continue;
+    }
+    float peak = 0.0f;
+    for (int64_t j = 0; j < K; ++j) peak = fmaxf(peak, fabsf(v[j]));
+    const float qmax = out == OUT_E4M3 ? 448.0f : 127.0f;
+    const float sc = peak == 0.0f ? 1.0f : peak / qmax;
+    s[r] = sc;
+    uint8_t* qrow = (uint8_t*)q + r * K;
+    for (int64_t j = 0; j < K; ++j)
+      qrow[j] = out == OUT_E4M3 ? e4m3_code(v[j], sc) : (uint8_t)int8_code(v[j], sc);
+  }
+  free(v);
+}
+
+/* ------------------------------------------------------------------ GEMM */
+/* Exact INT32 accumulators acc[m, n] = sum_k a[m, k] * b[n, k]. */
+void m5o_gemm_i8_acc(const int8_t* a, const int8_t* b, int64_t M, int64_t N, int64_t K,
+                     int32_t* acc) {
+  for (int64_t m = 0; m < M; ++m) {
+    const int8_t* ar = a + m * K;
+    for (int64_t n = 0; n < N; ++n) {
+      const int8_t* br = b + n * K;
+      int32_t t = 0;
+      for (int64_t k = 0; k < K; ++k) t += (int32_t)ar[k] * (int32_t)br[k];
+      acc[m * N + n] = t;
+    }
+  }
+}
+
+#define EPI_PLAIN 0
+#define EPI_BIAS_VEC 1
+#define EPI_BIAS_TABLE 2
+#define EPI_GATE_VEC 3
+#define EPI_GATE_TABLE 4
+
+/*
+ * Epilogue of the quantized GEMM given exact accumulators (INT32 as float
+ * source for INT8: float(acc) with round-to-nearest-even):
+ *   v = (float(acc) * sa[m]) * sb[n]
+ *   bias: v = v + bias[...]; gate: out = fmaf(bf16(v), gate[...], R[m, n])
+ *   out rounded to out_dtype (bf16 / f16 / f32).
+ */
+void m5o_gemm_epilogue_i32(const int32_t* acc, int64_t M, int64_t N, const float* sa,
+                           const float* sb, int epi, const float* bias,
+                           const int32_t* bias_row_map, const uint16_t* residual,
+                           const uint16_t* gate, const int32_t* gate_row_map, void* out,
+                           int out_dtype) {
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t n = 0; n < N; ++n) {
+      float v = (float)acc[m * N + n];
+      if (sa) v = (v * sa[m]) * sb[n];
+      if (epi == EPI_BIAS_VEC) v = v + bias[n];
+      if (epi == EPI_BIAS_TABLE) v = v + bias[(int64_t)bias_row_map[m] * N + n];
+      if (epi == EPI_GATE_VEC || epi == EPI_GATE_TABLE) {
+        const int64_t go = epi == EPI_GATE_TABLE ? (int64_t)gate_row_map[m] * N : 0;
+        const float br = bf16_to_f32(f32_to_bf16(v));
+        v = fmaf(br, bf16_to_f32(gate[go + n]), bf16_to_f32(residual[m * N + n]));
+      }
+      store_elem(out, out_dtype, m * N + n, v);
+    }
+  }
+}
+
+/*
+ * Q/K epilogue for one projection given exact accumulators acc[M, N]
+ * (N = heads * 128): z = bf16((float(acc) * sa) * sb) (or bf16(acc) when sa
+ * is NULL), per (row, head) sumsq = sequential fmaf over the 128 channels,
+ * inv = 1 / sqrt(sumsq / 128 + eps), u_j = (z_j * inv) * gamma_j,
+ * split-half RoPE on j < 2R, bf16 head-major out [heads, M, 128].
+ */
+void m5o_qk_rope_from_acc(const float* accf, int64_t M, int64_t N, const float* sa,
+                          const float* sb, const uint16_t* gamma, const uint16_t* cosb,
+                          const uint16_t* sinb, int R, float eps, uint16_t* out) {
+  const int64_t heads = N / 128;
+  float z[128], u[128];
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t h = 0; h < heads; ++h) {
+      float sumsq = 0.0f;
+      for (int j = 0; j < 128; ++j) {
+        const int64_t col = h * 128 + j;
+        float v = accf[m * N + col];
+        if (sa) v = (v * sa[m]) * sb[col];
+        z[j] = bf16_to_f32(f32_to_bf16(v));
+        sumsq = fmaf(z[j], z[j], sumsq);
+      }
+      const float inv = 1.0f / sqrtf(sumsq / 128.0f + eps);
+      for (int j = 0; j < 128; ++j) u[j] = (z[j] * inv) * bf16_to_f32(gamma[j]);
+      for (int j = 0; j < 128; ++j) {
+        float o = u[j];
+        if (j < 2 * R) {
+          const int p = j < R ? j + R : j - R;
+          const int ang = j < R ? j : j - R;
+          const float c = bf16_to_f32(cosb[m * R + ang]);
+          const float s = bf16_to_f32(sinb[m * R + ang]);
+          o = j < R ? (u[j] * c) - (u[p] * s) : (u[j] * c) + (u[p] * s);
+        }
+        out[(h * M + m) * 128 + j] = f32_to_bf16(o);
+      }
+    }
+  }
+}

@@ -1,0 +1,171 @@
+"""GPU parity of the tcgen05 GEMM and its fused epilogues.
+
+Bar: INT32 accumulators bit-exact (exact integer dot products); INT8 BF16 /
+FP16 / FP32 outputs bit-exact against the C epilogue restatement
+((float(acc) * sa) * sb, then bias or gate, then RNE); FP8 within relative
+L2 5e-3 of the float64 decoded dot; BF16 GEMM within relative L2 1e-3.
+Shapes cover the reference's tail cases (tests/test_metal.py:28-53,
+tests/test_qk_rope_metal.py:39-52): M, N and K not multiples of the tile.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import c_oracle as co
+from oracle import reference_numpy as ref
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+TAIL_SHAPES = [(1, 33, 64), (127, 65, 96), (65, 17, 257), (129, 128, 33), (17, 384, 96),
+               (300, 520, 1024), (512, 2048, 2048)]
+
+
+@pytest.fixture(scope="module")
+def ops():
+    import m5kernels_b200 as m
+
+    return m
+
+
+def _operands(m, n, k, seed=5, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=g).to(dtype)
+    b = (torch.randn(n, k, generator=g) * 0.02).to(dtype)
+    return a, b
+
+
+def _q(ops, t, mode="int8"):
+    q, s = ops.quantize(t.to(DEV), mode)
+    return q, s
+
+
+@pytest.mark.parametrize("shape", TAIL_SHAPES)
+def test_int8_accumulators_bit_exact(ops, shape):
+    m, n, k = shape
+    a, b = _operands(m, n, k)
+    aq, _ = _q(ops, a)
+    bq, _ = _q(ops, b)
+    acc = ops.gemm(aq, bq, "int8", output_dtype=torch.int32).cpu()
+    expect = co.gemm_i8_acc(aq.cpu(), bq.cpu())
+    assert torch.equal(acc, expect)
+
+
+@pytest.mark.parametrize("shape", TAIL_SHAPES)
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_int8_scaled_epilogue_bit_exact(ops, shape, out_dtype):
+    m, n, k = shape
+    a, b = _operands(m, n, k)
+    aq, sa = _q(ops, a)
+    bq, sb = _q(ops, b)
+    y = ops.gemm(aq, bq, "int8", a_scales=sa, b_scales=sb, output_dtype=out_dtype).cpu()
+    acc = co.gemm_i8_acc(aq.cpu(), bq.cpu())
+    expect = co.gemm_epilogue(acc, sa.cpu(), sb.cpu(), out_dtype=out_dtype)
+    assert torch.equal(y, expect)
+    # quality against the float64 decoded dot (reference engine tolerance)
+    dec = (aq.cpu().double() * sa.cpu().double()[:, None]) @ (bq.cpu().double() * sb.cpu().double()[:, None]).T
+    assert ref.metrics(y.double().numpy(), dec.numpy())["relative_l2"] <= 8e-3
+
+
+def test_c1_config_w8a8(ops):
+    """A [512,2048] ~N(0,1), W [2048,2048] ~N(0,0.02), seed 0."""
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn(512, 2048, generator=g).to(torch.bfloat16)
+    w = (torch.randn(2048, 2048, generator=g) * 0.02).to(torch.bfloat16)
+    aq, sa = _q(ops, a)
+    wq, sw = _q(ops, w)
+    y = ops.gemm(aq, wq, "int8", a_scales=sa, b_scales=sw, output_dtype=torch.bfloat16).cpu()
+    expect = co.gemm_epilogue(co.gemm_i8_acc_fast(aq.cpu(), wq.cpu()), sa.cpu(), sw.cpu())
+    assert torch.equal(y, expect)
+
+
+@pytest.mark.parametrize("table", [False, True])
+def test_int8_bias_epilogue(ops, table):
+    m, n, k = 200, 384, 512
+    a, b = _operands(m, n, k, seed=7)
+    aq, sa = _q(ops, a)
+    bq, sb = _q(ops, b)
+    g = torch.Generator().manual_seed(8)
+    bias = torch.randn(3, n, generator=g) if table else torch.randn(n, generator=g)
+    brm = (torch.arange(m, dtype=torch.int32) % 3) if table else None
+    y = ops.gemm(aq, bq, "int8", a_scales=sa, b_scales=sb, output_dtype=torch.bfloat16,
+                 bias=bias.to(DEV), bias_row_map=brm.to(DEV) if table else None).cpu()
+    acc = co.gemm_i8_acc(aq.cpu(), bq.cpu())
+    expect = co.gemm_epilogue(acc, sa.cpu(), sb.cpu(), epi="bias_table" if table else "bias_vec",
+                              bias=bias, bias_row_map=brm)
+    assert torch.equal(y, expect)
+
+
+@pytest.mark.parametrize("table", [False, True])
+def test_int8_gated_epilogue_equals_staged(ops, table):
+    m, n, k = 130, 256, 384
+    a, b = _operands(m, n, k, seed=9)
+    aq, sa = _q(ops, a)
+    bq, sb = _q(ops, b)
+    g = torch.Generator().manual_seed(10)
+    residual = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    gate = (0.1 * torch.randn(2, n, generator=g)).to(torch.bfloat16)
+    gate = gate if table else gate[0]
+    grm = (torch.arange(m, dtype=torch.int32) // 65) if table else None
+    y = ops.gemm(aq, bq, "int8", a_scales=sa, b_scales=sb, output_dtype=torch.bfloat16,
+                 residual=residual.to(DEV), gate=gate.to(DEV),
+                 gate_row_map=grm.to(DEV) if table else None).cpu()
+    acc = co.gemm_i8_acc(aq.cpu(), bq.cpu())
+    expect = co.gemm_epilogue(acc, sa.cpu(), sb.cpu(), epi="gate_table" if table else "gate_vec",
+                              residual=residual, gate=gate, gate_row_map=grm)
+    assert torch.equal(y, expect)
+    # staged: bf16 branch output, then the gated update (reference chain semantics)
+    branch = ops.gemm(aq, bq, "int8", a_scales=sa, b_scales=sb, output_dtype=torch.bfloat16).cpu()
+    gsel = gate[grm.long()] if table else gate[None, :]
+    staged = torch.addcmul(residual.float(), branch.float(), gsel.float()).to(torch.bfloat16)
+    assert torch.equal(y, staged)
+
+
+@pytest.mark.parametrize("shape", [(65, 33, 256), (300, 520, 1024), (256, 4096, 4096)])
+def test_fp8_gemm_tolerance(ops, shape):
+    m, n, k = shape
+    a, b = _operands(m, n, k, seed=11)
+    aq, sa = _q(ops, a, "fp8")
+    bq, sb = _q(ops, b, "fp8")
+    y = ops.gemm(aq, bq, "fp8", a_scales=sa, b_scales=sb, output_dtype=torch.bfloat16).cpu()
+    da = ref.dequantize(aq.cpu().numpy(), sa.cpu().numpy(), "fp8").astype(np.float64)
+    db = ref.dequantize(bq.cpu().numpy(), sb.cpu().numpy(), "fp8").astype(np.float64)
+    assert ref.metrics(y.float().numpy(), da @ db.T)["relative_l2"] <= 5e-3
+
+
+def test_fp8_full_misaligned_output_tail(ops):
+    a = torch.ones(65, 256, device=DEV)
+    b = torch.ones(33, 256, device=DEV)
+    aq, sa = ops.quantize(a, "fp8")
+    bq, sb = ops.quantize(b, "fp8")
+    y = ops.gemm(aq, bq, "fp8", a_scales=sa, b_scales=sb).cpu()
+    torch.testing.assert_close(y, torch.full((65, 33), 256.0), rtol=1e-5, atol=0)
+
+
+@pytest.mark.parametrize("mode", ["bf16", "fp16"])
+@pytest.mark.parametrize("shape", [(1, 33, 64), (127, 65, 96), (300, 520, 1024)])
+def test_float_gemm_tolerance(ops, mode, shape):
+    m, n, k = shape
+    dt = torch.bfloat16 if mode == "bf16" else torch.float16
+    a, b = _operands(m, n, k, seed=12, dtype=dt)
+    y = ops.gemm(a.to(DEV), b.to(DEV), mode, output_dtype=torch.float32).cpu()
+    expect = a.double() @ b.double().T
+    assert ref.metrics(y.numpy(), expect.numpy())["relative_l2"] <= 1e-5
+
+
+def test_gemm_contract_rejections(ops):
+    a = torch.ones(2, 96, device=DEV)
+    b = torch.ones(3, 96, device=DEV)
+    aq, sa = ops.quantize(a, "fp8")
+    bq, sb = ops.quantize(b, "fp8")
+    with pytest.raises(NotImplementedError, match="stride"):
+        ops.gemm(aq, bq, "fp8", a_scales=sa, b_scales=sb)
+    qa, qsa = ops.quantize(torch.ones(4, 64, device=DEV), "int8")
+    with pytest.raises(ValueError, match="scales"):
+        ops.gemm(qa, qa, "int8")
+    with pytest.raises(NotImplementedError, match="BF16 output"):
+        ops.gemm(qa, qa, "int8", a_scales=qsa, b_scales=qsa, residual=torch.zeros(4, 4, device=DEV),
+                 gate=torch.zeros(4, device=DEV, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="K mismatch"):
+        ops.gemm(qa, qa[:, :32], "int8", a_scales=qsa, b_scales=qsa)
