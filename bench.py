@@ -254,6 +254,14 @@ def run_b200(args, world, rank, local):
                                             output_dtype=torch.bfloat16), max(args.steps, 10))
     prep_ms = time_kernel(lambda i: m5.quantize(sets[i % SETS][0], "int8"), max(args.steps, 10))
 
+    if args.profile:
+        if rank == 0:
+            print(json.dumps({"profile": True, "ms_per_step": ms_per_step, "gemm_ms": gemm_ms,
+                              "prep_ms": prep_ms}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+
     # End to end through the public API from pinned host memory.
     host_a = [sets[i][0].to("cpu").pin_memory() for i in range(SETS)]
     host_out = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
@@ -337,6 +345,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling run: timed steps and per-kernel timing only (no e2e, no CPU leg)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

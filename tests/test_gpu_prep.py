@@ -28,7 +28,7 @@ def _x(rows, k, dtype, kind="normal", seed=0):
     elif kind == "outliers":
         x[:, ::31] *= 30
     elif kind == "rowzero":
-        x[1] = 0
+        x[rows // 2] = 0
     return x.to(dtype)
 
 
