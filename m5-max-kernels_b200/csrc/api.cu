@@ -121,20 +121,60 @@ int check_rows(int64_t rows, int64_t k) {
   return M5B_OK;
 }
 
+// 3D view {E, K/E, rows} of a row-major [rows, K] input (E = 128 / elem_bytes
+// elements per 128-byte box row), loaded whole rows at a time with the
+// 128-byte swizzle.  Returns false when the rows cannot be staged this way.
+bool make_row_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int eb,
+                  int* box_rows) {
+  if (!ptr || !aligned(ptr, 16) || (k % 64) != 0) return false;
+  const int64_t e = 128 / eb;
+  const int64_t nbr = k / e;  // box rows per input row
+  const int64_t nb = nbr < 256 ? nbr : 256;
+  if (nbr % nb) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(e), static_cast<cuuint64_t>(nbr),
+                        static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(k * eb)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(e), static_cast<cuuint32_t>(nb), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt =
+      eb == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  CUresult r = g_encode(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  *box_rows = static_cast<int>(nb);
+  return true;
+}
+
 int run_row_prep(RowPrepArgs& a, int x_dtype, int block, int out, void* stream) {
   a.warps = row_prep_warps(a.K, block);
   if (a.warps > 16)
-    return fail(M5B_EUNSUPPORTED, "row width K=%lld exceeds the register-resident limit",
+    return fail(M5B_EUNSUPPORTED, "row width K=%lld exceeds the register-resident limit (32768)",
                 static_cast<long long>(a.K));
   a.inv_sqrt_block = block > 0 ? static_cast<float>(1.0 / std::sqrt(static_cast<double>(block)))
                                : 1.0f;
-  const int xb = dtype_bytes(x_dtype);
-  bool vec = (a.K % 8) == 0 && aligned(a.x, 16) && (!a.branch || aligned(a.branch, 16)) &&
-             (!a.r_out || aligned(a.r_out, 16)) && (!a.q || aligned(a.q, 8)) &&
-             (!a.y || aligned(a.y, 16));
-  (void)xb;
+  const bool vec = (a.K % 8) == 0 && aligned(a.x, 16) && (!a.branch || aligned(a.branch, 16)) &&
+                   (!a.r_out || aligned(a.r_out, 16)) && (!a.q || aligned(a.q, 16)) &&
+                   (!a.y || aligned(a.y, 16));
   a.vec_ok = vec ? 1 : 0;
-  cudaError_t e = launch_row_prep(a, x_dtype, block, out, static_cast<cudaStream_t>(stream));
+  const bool pvec = (a.K % 8) == 0 && (!a.gamma || aligned(a.gamma, 16)) &&
+                    (!a.scale || aligned(a.scale, 16)) && (!a.shift || aligned(a.shift, 16)) &&
+                    (!a.gate || aligned(a.gate, 16)) && (!a.signs || aligned(a.signs, 16));
+  a.params_vec = pvec ? 1 : 0;
+  unsigned int* status = nullptr;
+  int rc = device_state(&status, nullptr);
+  if (rc) return rc;
+  a.status = status;
+  RowMaps maps{};
+  rc = get_encode();
+  if (rc) return rc;
+  const int eb = dtype_bytes(x_dtype);
+  int box_rows = 0, box_rows_b = 0;
+  bool staged = vec && make_row_map(&maps.x, a.x, a.rows, a.K, eb, &box_rows);
+  if (staged && a.branch) staged = make_row_map(&maps.b, a.branch, a.rows, a.K, eb, &box_rows_b);
+  maps.valid = staged ? 1 : 0;
+  maps.box_rows = box_rows;
+  cudaError_t e = launch_row_prep(a, maps, x_dtype, block, out, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "row preparation launch");
   return ok();
 }

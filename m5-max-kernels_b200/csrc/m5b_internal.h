@@ -29,16 +29,26 @@ struct RowPrepArgs {
   int round_output;            // round the modulated value through the input dtype
   float inv_sqrt_block;        // fp32(1/sqrt(block)) for the rotation
   int warps;                   // warps per CTA (row_prep_warps)
-  int vec_ok;                  // 16-byte vector loads / stores are aligned
+  int vec_ok;                  // 16-byte vector loads / stores of rows are aligned
+  int params_vec;              // gamma / scale / shift / gate rows allow 16-byte loads
   void* q;                     // [rows, K] int8 or E4M3 codes
   float* s;                    // [rows] per-row scales
   float* y;                    // [rows, K] fp32 rotated values (OUT_F32)
   void* r_out;                 // [rows, K] updated residual (gated)
+  unsigned int* status;        // device status word (bounded-wait errors)
+};
+
+// TMA descriptors of the row-streamed inputs (x and, gated, branch).
+struct RowMaps {
+  CUtensorMap x;
+  CUtensorMap b;
+  int valid;      // rows are staged through shared memory with these maps
+  int box_rows;   // 128-byte box rows per TMA load
 };
 
 int row_prep_warps(int64_t K, int block);
-cudaError_t launch_row_prep(const RowPrepArgs& a, int x_dtype, int block, int out,
-                            cudaStream_t stream);
+cudaError_t launch_row_prep(const RowPrepArgs& a, const RowMaps& maps, int x_dtype, int block,
+                            int out, cudaStream_t stream);
 
 // GEMM epilogues.  C[m, n] for the plain epilogues, [N/128, M, 128] for QK.
 enum Epilogue : int {

@@ -2,7 +2,8 @@
 #include "prep_impl.cuh"
 
 namespace m5b {
-cudaError_t launch_row_prep_f32(const RowPrepArgs& a, int block, int out, cudaStream_t stream) {
-  return launch_o<float>(a, block, out, stream);
+cudaError_t launch_row_prep_f32(const RowPrepArgs& a, const RowMaps& m, int block, int out,
+                                 cudaStream_t stream) {
+  return launch_o<float>(a, m, block, out, stream);
 }
 }  // namespace m5b

@@ -1,4 +1,4 @@
-// Row-preparation kernels: one CTA per activation row.
+// Row-preparation kernels (template shared by prep_{bf16,f16,f32}.cu).
 //
 // One kernel template covers every memory-bound stage of the online activation
 // path (reference operator contracts in parentheses):
@@ -13,93 +13,121 @@
 //       (src/m5kernels/norm_hadamard.py:198-265, gated_residual_reference.py:21-60)
 //
 // Data layout in HBM: row-major [rows, K] activations; codes [rows, K] int8 /
-// uint8 (E4M3 bits); scales fp32 [rows].  Each row is read once (128-bit loads,
-// a warp reads 512 contiguous bytes of bf16 per instruction) and its codes are
-// written once: 3K + 4 bytes per row for bf16 in / int8 out.
+// uint8 (E4M3 bits); scales fp32 [rows].  Each row is read once and its codes
+// are written once: 3K + 4 bytes per row for bf16 in / int8 out (7K + 4 for the
+// gated form, which also reads the branch and writes R').
 //
-// Thread layout: a row is split into "units" of max(B, 256) elements.  Lane l
-// of a warp owns elements l*8 .. l*8+7 of each 256-element slice of a unit, so
-// Hadamard strides 1, 2, 4 are register butterflies, strides 8 .. 128 are
-// warp shuffles (lane xor 1 .. 16) and strides 256 .. 512 are register
-// butterflies across the slices a lane holds.  Units go round-robin to warps
-// (unit = slot * W + warp).  Reductions (sum, sum of squares, max) are
-// deterministic: per-thread sequential in (slot, slice, element) order, then a
-// xor-butterfly over the warp, then warps 0..W-1 summed in order.  The C
-// restatement in oracle/ follows the same order, which is what makes the
-// codes and scales bit-comparable.
+// Execution: persistent CTAs of W warps (W = ceil(K / 2048)), one row at a
+// time per CTA.  A ring of STAGES row buffers in shared memory is filled by
+// TMA tile loads (one thread issues, completion on an mbarrier), so the next
+// rows stream in while the current one is transformed.  Rows that are not
+// whole 64-element chunks or not 16-byte aligned are read with plain loads.
+//
+// Ownership: thread t of the CTA owns the contiguous chunk of kChunk = 64
+// elements [64 t, 64 t + 64) of the row, held in registers.  Hence Hadamard
+// strides 1..32 are register butterflies and strides 64..B/2 are warp
+// shuffles (lane xor 1 .. B/128).  Row reductions have one canonical order,
+// mirrored by the C oracle: each thread sums its chunk sequentially; lanes
+// combine with a xor butterfly of increasing offset (1, 2, 4, 8, 16 — a
+// pairwise tree over chunk index); warps combine pairwise in index order
+// (w0+w1, w2+w3, ... then pairs of pairs).
 #pragma once
 #include "common.cuh"
 #include "m5b_internal.h"
 
 namespace m5b {
 
-constexpr int kMaxValues = 64;  // FP32 values a thread keeps in registers
+constexpr int kChunk = 64;  // elements per thread
 
+// ---------------------------------------------------------------- quantization
+// rint(v / scale) clipped to +-127 with the exact semantics of an IEEE divide
+// followed by rint.  t = v * (1/scale) is within 2^-15.6 of the correctly
+// rounded quotient when |v| <= peak; unless t lies within 2^-14 of a
+// half-integer both round to the same integer, and in that rare case the
+// quotient is recomputed with an IEEE division.
+__device__ __forceinline__ int quant_i8(float v, float scale, float inv, bool fast) {
+  float r;
+  const float t = __fmul_rn(v, inv);
+  r = rintf(t);
+  if (!fast || fabsf(__fsub_rn(t, r)) > 0.5f - 0x1p-14f) r = rintf(__fdiv_rn(v, scale));
+  r = fminf(fmaxf(r, -127.0f), 127.0f);
+  return static_cast<int>(r);
+}
+
+// E4M3 code of RN(v / scale) (RNE, saturating).  The conversion is monotonic,
+// so when t(1 - 2^-18) and t(1 + 2^-18), which bracket the correctly rounded
+// quotient, share one code, that is the code; otherwise divide exactly.
+__device__ __forceinline__ uint32_t quant_e4m3(float v, float scale, float inv, bool fast) {
+  if (fast) {
+    const float t = __fmul_rn(v, inv);
+    const __nv_fp8x2_storage_t two = __nv_cvt_float2_to_fp8x2(
+        make_float2(__fmul_rn(t, 1.0f - 0x1p-18f), __fmul_rn(t, 1.0f + 0x1p-18f)), __NV_SATFINITE,
+        __NV_E4M3);
+    if ((two & 0xFFu) == (two >> 8)) return two & 0xFFu;
+  }
+  return static_cast<uint32_t>(
+      __nv_cvt_float_to_fp8(__fdiv_rn(v, scale), __NV_SATFINITE, __NV_E4M3));
+}
+
+// ---------------------------------------------------------------- loads
 template <typename T>
-__device__ __forceinline__ void load8(const T* __restrict__ p, int64_t j0, int64_t K, bool vec,
-                                      float (&out)[8]) {
-  if (vec && j0 + 8 <= K) {
-    if constexpr (sizeof(T) == 2) {
-      uint4 raw = __ldg(reinterpret_cast<const uint4*>(p + j0));
-      const T* h = reinterpret_cast<const T*>(&raw);
+__device__ __forceinline__ void cvt8(const uint4& raw, float* out) {
+  if constexpr (sizeof(T) == 2) {
+    const T* h = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) out[e] = to_f32(h[e]);
-    } else {
-      float4 lo = __ldg(reinterpret_cast<const float4*>(p + j0));
-      float4 hi = __ldg(reinterpret_cast<const float4*>(p + j0 + 4));
-      out[0] = lo.x; out[1] = lo.y; out[2] = lo.z; out[3] = lo.w;
-      out[4] = hi.x; out[5] = hi.y; out[6] = hi.z; out[7] = hi.w;
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) out[e] = (j0 + e < K) ? to_f32(p[j0 + e]) : 0.0f;
+    for (int e = 0; e < 8; ++e) out[e] = to_f32(h[e]);
   }
 }
 
-template <typename T>
-__device__ __forceinline__ void store8(T* __restrict__ p, int64_t j0, int64_t K, bool vec,
-                                       const float (&v)[8]) {
-  if (vec && j0 + 8 <= K) {
-    if constexpr (sizeof(T) == 2) {
-      uint4 raw;
-      T* h = reinterpret_cast<T*>(&raw);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(v[e]);
-      *reinterpret_cast<uint4*>(p + j0) = raw;
+// Eight parameter values starting at element j of a bf16 / fp16 / fp32 table.
+__device__ __forceinline__ void param8(const void* base, int dtype, int64_t j, bool vec,
+                                       float* out) {
+  if (vec) {
+    if (dtype == DT_F32) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(base) + (j >> 2));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(base) + (j >> 2) + 1);
+      out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+      out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
     } else {
-      *reinterpret_cast<float4*>(p + j0) = make_float4(v[0], v[1], v[2], v[3]);
-      *reinterpret_cast<float4*>(p + j0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(
+          reinterpret_cast<const uint16_t*>(base) + j));
+      if (dtype == DT_BF16)
+        cvt8<__nv_bfloat16>(raw, out);
+      else
+        cvt8<__half>(raw, out);
     }
   } else {
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (j0 + e < K) p[j0 + e] = from_f32<T>(v[e]);
+    for (int e = 0; e < 8; ++e) out[e] = load_param(base, dtype, j + e);
   }
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
+// ---------------------------------------------------------------- reductions
+__device__ __forceinline__ float warp_sum_tree(float v) {
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
-  return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  for (int off = 1; off < 32; off <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
   return v;
 }
 
-// Sum the per-warp partials in warp order; every thread gets the same value.
-__device__ __forceinline__ float block_sum(float v, float* red, int W) {
-  v = warp_sum(v);
+// Canonical sum over the CTA: lanes pairwise (xor 1..16), warps pairwise.
+__device__ __forceinline__ float cta_sum(float v, float* red, int W) {
+  v = warp_sum_tree(v);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  float t = red[0];
-  for (int w = 1; w < W; ++w) t = __fadd_rn(t, red[w]);
+  float part[16];
+#pragma unroll
+  for (int w = 0; w < 16; ++w) part[w] = (w < W) ? red[w] : 0.0f;
+#pragma unroll
+  for (int step = 1; step < 16; step <<= 1)
+#pragma unroll
+    for (int w = 0; w + step < 16; w += 2 * step) part[w] = __fadd_rn(part[w], part[w + step]);
   __syncthreads();
-  return t;
+  return part[0];
 }
-__device__ __forceinline__ float block_max(float v, float* red, int W) {
-  v = warp_max(v);
+
+__device__ __forceinline__ float cta_max(float v, float* red, int W) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   float t = red[0];
@@ -108,240 +136,340 @@ __device__ __forceinline__ float block_max(float v, float* red, int W) {
   return t;
 }
 
+// ---------------------------------------------------------------- TMA row tiles
+// A row of K elements is viewed as [K / E] box rows of E = 128 / sizeof(T)
+// elements (128 bytes); the 3D tensor map {E, K/E, rows} loads whole rows
+// with the 128-byte swizzle, so 16-byte slot i of box row r sits at physical
+// slot i ^ (r & 7): threads that read their own chunk slot by slot hit eight
+// different bank groups.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// 16-byte slot `slot` (0..7 within the chunk's 128-byte box row `br`) of a
+// swizzled row buffer.
+__device__ __forceinline__ const uint4* swz_slot(const uint8_t* base, int br, int slot) {
+  return reinterpret_cast<const uint4*>(base + br * 128 + ((slot ^ (br & 7)) << 4));
+}
+
 template <typename T, int B, int OUT>
-__global__ void __launch_bounds__(512) row_prep_kernel(const RowPrepArgs a) {
-  constexpr int UNIT = (B > 256) ? B : 256;
-  constexpr int VPU = UNIT / 256;                    // 8-element slices per lane per unit
-  constexpr int SLOTS = kMaxValues / (8 * VPU);      // units a warp can hold
-  constexpr int LANE_SPAN = (B == 0) ? 1 : ((B < 256 ? B : 256) / 8);  // lanes per block slice
-  __shared__ float red[32];
+__global__ void __launch_bounds__(512)
+    row_prep_kernel(const __grid_constant__ CUtensorMap map_x,
+                    const __grid_constant__ CUtensorMap map_b, const RowPrepArgs a,
+                    const int stages, const int box_rows) {
+  constexpr int IN_THREAD = (B == 0) ? 0 : (B < kChunk ? B : kChunk);  // in-register block span
+  constexpr int LANE_SPAN = (B > kChunk) ? B / kChunk : 1;              // lanes per block
+  extern __shared__ uint8_t dsmem_raw[];
+  uint8_t* dsmem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  __shared__ float red[16];
+  __shared__ __align__(8) uint64_t full_bar[4];
+  __shared__ int abort_flag;
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int W = a.warps;
-  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int W = blockDim.x >> 5;
   const int64_t K = a.K;
-  const int units = static_cast<int>((K + UNIT - 1) / UNIT);
+  const int64_t j0 = int64_t(tid) * kChunk;  // first element of this thread's chunk
+  const bool have = j0 < K;
+  const int cnt = have ? static_cast<int>(K - j0 < kChunk ? K - j0 : kChunk) : 0;
+  const bool fullchunk = cnt == kChunk;
   const bool vec = a.vec_ok != 0;
+  const bool gated = a.branch != nullptr;
+  const int inputs = gated ? 2 : 1;
+  const int64_t row_bytes = K * int64_t(sizeof(T));
+  const int64_t buf_stride = (row_bytes + 1023) & ~int64_t(1023);  // 1024-aligned buffers
+  const int64_t stride = gridDim.x;
 
-  const T* __restrict__ xrow = reinterpret_cast<const T*>(a.x) + row * K;
-  float v[SLOTS][VPU][8];
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full_bar[s], 1);
+    abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
 
-  // ---- load (and gated residual update) ---------------------------------
-  const T* __restrict__ brow = a.branch ? reinterpret_cast<const T*>(a.branch) + row * K : nullptr;
-  const int64_t gate_off = (a.gate && a.gate_row_map) ? int64_t(a.gate_row_map[row]) * K : 0;
-#pragma unroll
-  for (int s = 0; s < SLOTS; ++s) {
-    const int u = s * W + warp;
-#pragma unroll
-    for (int vv = 0; vv < VPU; ++vv) {
-      const int64_t j0 = int64_t(u) * UNIT + vv * 256 + lane * 8;
-      if (u < units) {
-        load8<T>(xrow, j0, K, vec, v[s][vv]);
-        if (brow) {
-          float br[8];
-          load8<T>(brow, j0, K, vec, br);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            if (j0 + e < K) {
-              const float g = load_param(a.gate, a.gate_dtype, gate_off + j0 + e);
-              v[s][vv][e] = round_through<T>(__fmaf_rn(br[e], g, v[s][vv][e]));
-            }
-          }
-          store8<T>(reinterpret_cast<T*>(a.r_out) + row * K, j0, K, vec, v[s][vv]);
+  // Box rows of one input row, and TMA loads per input row (box_rows each).
+  const int row_box_rows = static_cast<int>(row_bytes / 128);
+  auto issue = [&](int64_t row, int s) {
+    uint8_t* dst = dsmem + int64_t(s) * inputs * buf_stride;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(inputs * row_bytes));
+    for (int c = 0; c < row_box_rows; c += box_rows) {
+      tma_load_3d(dst + c * 128, &map_x, &full_bar[s], 0, c, static_cast<int32_t>(row));
+      if (gated)
+        tma_load_3d(dst + buf_stride + c * 128, &map_b, &full_bar[s], 0, c,
+                    static_cast<int32_t>(row));
+    }
+  };
+  if (stages > 0 && tid == 0) {
+    for (int s = 0; s < stages; ++s) {
+      const int64_t row = blockIdx.x + s * stride;
+      if (row < a.rows) issue(row, s);
+    }
+  }
+
+  float v[kChunk];
+  int it = 0;
+  for (int64_t row = blockIdx.x; row < a.rows; row += stride, ++it) {
+    const int s = stages > 0 ? it % stages : 0;
+    // ---- load the chunk (and apply the gated residual update) -------------
+    const uint8_t* xs = nullptr;  // swizzled ring slot (staged) ...
+    const uint8_t* bs = nullptr;
+    const T* xg = reinterpret_cast<const T*>(a.x) + row * K;  // ... or the row in HBM
+    const T* bg = gated ? reinterpret_cast<const T*>(a.branch) + row * K : nullptr;
+    if (stages > 0) {
+      const uint32_t parity = static_cast<uint32_t>((it / stages) & 1);
+      if (!mbar_wait_bounded(&full_bar[s], parity, &abort_flag, a.status, DEV_TIMEOUT_PRODUCER))
+        break;
+      xs = dsmem + int64_t(s) * inputs * buf_stride;
+      if (gated) bs = xs + buf_stride;
+    }
+    // Elements [j0 + i, j0 + i + 8) of this thread's chunk -> registers, from
+    // the swizzled ring slot (staged rows hold whole chunks: 16-bit types use
+    // one 128-byte box row per chunk, fp32 two) or straight from HBM.
+    auto load8_at = [&](const uint8_t* sbase, const T* gbase, int i, float* out) {
+      if (sbase != nullptr) {
+        if constexpr (sizeof(T) == 2) {
+          cvt8<T>(*swz_slot(sbase, tid, i / 8), out);
+        } else {
+          const int br = 2 * tid + (i >= 32 ? 1 : 0);
+          const int sl = (i % 32) / 4;
+          const uint4 p = *swz_slot(sbase, br, sl);
+          const uint4 q = *swz_slot(sbase, br, sl + 1);
+          out[0] = __uint_as_float(p.x); out[1] = __uint_as_float(p.y);
+          out[2] = __uint_as_float(p.z); out[3] = __uint_as_float(p.w);
+          out[4] = __uint_as_float(q.x); out[5] = __uint_as_float(q.y);
+          out[6] = __uint_as_float(q.z); out[7] = __uint_as_float(q.w);
+        }
+      } else if (fullchunk && vec) {
+        if constexpr (sizeof(T) == 2) {
+          cvt8<T>(__ldg(reinterpret_cast<const uint4*>(gbase + j0 + i)), out);
+        } else {
+          const float4 p = __ldg(reinterpret_cast<const float4*>(gbase + j0 + i));
+          const float4 q = __ldg(reinterpret_cast<const float4*>(gbase + j0 + i + 4));
+          out[0] = p.x; out[1] = p.y; out[2] = p.z; out[3] = p.w;
+          out[4] = q.x; out[5] = q.y; out[6] = q.z; out[7] = q.w;
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[s][vv][e] = 0.0f;
+        for (int e = 0; e < 8; ++e) out[e] = (i + e < cnt) ? to_f32(gbase[j0 + i + e]) : 0.0f;
       }
+    };
+    if (have) {
+#pragma unroll
+      for (int i = 0; i < kChunk; i += 8) load8_at(xs, xg, i, v + i);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i) v[i] = 0.0f;
     }
-  }
-
-  // ---- normalization statistics --------------------------------------------
-  float mean = 0.0f, inv = 1.0f;
-  if (a.norm != NORM_NONE) {
-    float acc = 0.0f;
+    if (gated && have) {
+      const int64_t goff = a.gate_row_map ? int64_t(a.gate_row_map[row]) * K : 0;
+      T* rrow = reinterpret_cast<T*>(a.r_out) + row * K;
+      const bool pvec = fullchunk && a.params_vec;
 #pragma unroll
-    for (int s = 0; s < SLOTS; ++s) {
-      const int u = s * W + warp;
-      if (u < units) {
+      for (int i = 0; i < kChunk; i += 8) {
+        if (i < cnt) {
+          float br[8], g[8];
+          load8_at(bs, bg, i, br);
+          param8(a.gate, a.gate_dtype, goff + j0 + i, pvec, g);
 #pragma unroll
-        for (int vv = 0; vv < VPU; ++vv) {
-          const int64_t j0 = int64_t(u) * UNIT + vv * 256 + lane * 8;
+          for (int e = 0; e < 8; ++e)
+            if (i + e < cnt) v[i + e] = round_through<T>(__fmaf_rn(br[e], g[e], v[i + e]));
+          if (fullchunk && vec) {
+            if constexpr (sizeof(T) == 2) {
+              uint4 raw;
+              T* h = reinterpret_cast<T*>(&raw);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            if (j0 + e < K) {
-              const float x = v[s][vv][e];
-              acc = (a.norm == NORM_LAYER) ? __fadd_rn(acc, x) : __fmaf_rn(x, x, acc);
+              for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(v[i + e]);
+              *reinterpret_cast<uint4*>(rrow + j0 + i) = raw;
+            } else {
+              *reinterpret_cast<float4*>(rrow + j0 + i) =
+                  make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+              *reinterpret_cast<float4*>(rrow + j0 + i + 4) =
+                  make_float4(v[i + 4], v[i + 5], v[i + 6], v[i + 7]);
             }
-          }
-        }
-      }
-    }
-    const float kf = static_cast<float>(K);
-    const float first = __fdiv_rn(block_sum(acc, red, W), kf);
-    float moment = first;
-    if (a.norm == NORM_LAYER) {
-      mean = first;
-      float acc2 = 0.0f;
-#pragma unroll
-      for (int s = 0; s < SLOTS; ++s) {
-        const int u = s * W + warp;
-        if (u < units) {
-#pragma unroll
-          for (int vv = 0; vv < VPU; ++vv) {
-            const int64_t j0 = int64_t(u) * UNIT + vv * 256 + lane * 8;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              if (j0 + e < K) {
-                const float d = __fsub_rn(v[s][vv][e], mean);
-                acc2 = __fmaf_rn(d, d, acc2);
-              }
-            }
-          }
-        }
-      }
-      moment = __fdiv_rn(block_sum(acc2, red, W), kf);
-    }
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(moment, a.eps)));
-  }
-
-  // ---- modulation, optional rounding, signs ----------------------------------
-  const int64_t mod_off = a.row_map ? int64_t(a.row_map[row]) * K : 0;
-#pragma unroll
-  for (int s = 0; s < SLOTS; ++s) {
-    const int u = s * W + warp;
-    if (u < units) {
-#pragma unroll
-      for (int vv = 0; vv < VPU; ++vv) {
-        const int64_t j0 = int64_t(u) * UNIT + vv * 256 + lane * 8;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int64_t j = j0 + e;
-          if (j < K) {
-            float y = v[s][vv][e];
-            if (a.norm != NORM_NONE) {
-              const float g = load_param(a.gamma, a.gamma_dtype, j);
-              const float sc = load_param(a.scale, a.scale_dtype, mod_off + j);
-              const float sh = load_param(a.shift, a.shift_dtype, mod_off + j);
-              const float t = __fmul_rn(__fmul_rn(__fsub_rn(y, mean), inv), g);
-              y = __fmaf_rn(t, __fadd_rn(1.0f, sc), sh);
-              if (a.round_output) y = round_through<T>(y);
-            }
-            if (a.signs && a.signs[j] < 0) y = -y;
-            v[s][vv][e] = y;
-          }
-        }
-      }
-    }
-  }
-
-  // ---- block Walsh-Hadamard transform (natural Sylvester order) -------------
-  if constexpr (B > 0) {
-#pragma unroll
-    for (int s = 0; s < SLOTS; ++s) {
-      const int u = s * W + warp;
-      if (u < units) {  // warp-uniform: shuffles below see all 32 lanes
-#pragma unroll
-        for (int vv = 0; vv < VPU; ++vv) {
-#pragma unroll
-          for (int st = 1; st < 8; st <<= 1) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              if ((e & st) == 0) {
-                const float lo = v[s][vv][e], hi = v[s][vv][e + st];
-                v[s][vv][e] = __fadd_rn(lo, hi);
-                v[s][vv][e + st] = __fsub_rn(lo, hi);
-              }
-            }
-          }
-#pragma unroll
-          for (int off = 1; off < LANE_SPAN; off <<= 1) {
-            const bool upper = (lane & off) != 0;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float own = v[s][vv][e];
-              const float peer = __shfl_xor_sync(0xffffffffu, own, off);
-              v[s][vv][e] = upper ? __fsub_rn(peer, own) : __fadd_rn(own, peer);
-            }
-          }
-        }
-#pragma unroll
-        for (int st = 1; st < VPU; st <<= 1) {
-#pragma unroll
-          for (int vv = 0; vv < VPU; ++vv) {
-            if ((vv & st) == 0) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float lo = v[s][vv][e], hi = v[s][vv + st][e];
-                v[s][vv][e] = __fadd_rn(lo, hi);
-                v[s][vv + st][e] = __fsub_rn(lo, hi);
-              }
-            }
-          }
-        }
-#pragma unroll
-        for (int vv = 0; vv < VPU; ++vv)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[s][vv][e] = __fmul_rn(v[s][vv][e], a.inv_sqrt_block);
-      }
-    }
-  }
-
-  // ---- FP32 rotated output (standalone rotation) ----------------------------
-  if constexpr (OUT == OUT_F32) {
-    float* yrow = a.y + row * K;
-#pragma unroll
-    for (int s = 0; s < SLOTS; ++s) {
-      const int u = s * W + warp;
-      if (u < units) {
-#pragma unroll
-        for (int vv = 0; vv < VPU; ++vv)
-          store8<float>(yrow, int64_t(u) * UNIT + vv * 256 + lane * 8, K, vec, v[s][vv]);
-      }
-    }
-    return;
-  } else {
-    // ---- row peak and symmetric per-row scale ------------------------------
-    float peak = 0.0f;
-#pragma unroll
-    for (int s = 0; s < SLOTS; ++s)
-#pragma unroll
-      for (int vv = 0; vv < VPU; ++vv)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) peak = fmaxf(peak, fabsf(v[s][vv][e]));
-    peak = block_max(peak, red, W);
-    const float qmax = (OUT == OUT_E4M3) ? 448.0f : 127.0f;
-    const float scale = (peak == 0.0f) ? 1.0f : __fdiv_rn(peak, qmax);
-    if (threadIdx.x == 0) a.s[row] = scale;
-
-    uint8_t* qrow = reinterpret_cast<uint8_t*>(a.q) + row * K;
-#pragma unroll
-    for (int s = 0; s < SLOTS; ++s) {
-      const int u = s * W + warp;
-      if (u < units) {
-#pragma unroll
-        for (int vv = 0; vv < VPU; ++vv) {
-          const int64_t j0 = int64_t(u) * UNIT + vv * 256 + lane * 8;
-          uint8_t c[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            if constexpr (OUT == OUT_E4M3)
-              c[e] = e4m3_code(v[s][vv][e], scale);
-            else
-              c[e] = static_cast<uint8_t>(int8_code(v[s][vv][e], scale));
-          }
-          if (vec && j0 + 8 <= K) {
-            uint2 packed;
-            packed.x = uint32_t(c[0]) | (uint32_t(c[1]) << 8) | (uint32_t(c[2]) << 16) |
-                       (uint32_t(c[3]) << 24);
-            packed.y = uint32_t(c[4]) | (uint32_t(c[5]) << 8) | (uint32_t(c[6]) << 16) |
-                       (uint32_t(c[7]) << 24);
-            *reinterpret_cast<uint2*>(qrow + j0) = packed;
           } else {
 #pragma unroll
             for (int e = 0; e < 8; ++e)
-              if (j0 + e < K) qrow[j0 + e] = c[e];
+              if (i + e < cnt) rrow[j0 + i + e] = from_f32<T>(v[i + e]);
           }
+        }
+      }
+    }
+    if (stages > 0) {
+      __syncthreads();  // every thread has read ring slot s
+      const int64_t next = row + int64_t(stages) * stride;
+      if (tid == 0 && next < a.rows) issue(next, s);
+    }
+
+    // ---- normalization statistics ----------------------------------------
+    float mean = 0.0f, inv = 1.0f;
+    if (a.norm != NORM_NONE) {
+      float acc = 0.0f;
+      if (a.norm == NORM_LAYER) {
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i)
+          if (i < cnt) acc = __fadd_rn(acc, v[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i)
+          if (i < cnt) acc = __fmaf_rn(v[i], v[i], acc);
+      }
+      const float kf = static_cast<float>(K);
+      const float first = __fdiv_rn(cta_sum(acc, red, W), kf);
+      float moment = first;
+      if (a.norm == NORM_LAYER) {
+        mean = first;
+        float acc2 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          if (i < cnt) {
+            const float d = __fsub_rn(v[i], mean);
+            acc2 = __fmaf_rn(d, d, acc2);
+          }
+        }
+        moment = __fdiv_rn(cta_sum(acc2, red, W), kf);
+      }
+      inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(moment, a.eps)));
+
+      // ---- modulation, optional rounding --------------------------------
+      const int64_t moff = a.row_map ? int64_t(a.row_map[row]) * K : 0;
+      const bool pvec = fullchunk && a.params_vec;
+#pragma unroll
+      for (int i = 0; i < kChunk; i += 8) {
+        if (i < cnt) {
+          float g[8], sc[8], sh[8];
+          param8(a.gamma, a.gamma_dtype, j0 + i, pvec, g);
+          param8(a.scale, a.scale_dtype, moff + j0 + i, pvec, sc);
+          param8(a.shift, a.shift_dtype, moff + j0 + i, pvec, sh);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (i + e < cnt) {
+              const float t = __fmul_rn(__fmul_rn(__fsub_rn(v[i + e], mean), inv), g[e]);
+              float y = __fmaf_rn(t, __fadd_rn(1.0f, sc[e]), sh[e]);
+              if (a.round_output) y = round_through<T>(y);
+              v[i + e] = y;
+            }
+          }
+        }
+      }
+    }
+    // ---- signs -----------------------------------------------------------
+    if (a.signs) {
+      if (fullchunk && a.params_vec) {
+#pragma unroll
+        for (int i = 0; i < kChunk; i += 16) {
+          const uint4 sg = __ldg(reinterpret_cast<const uint4*>(a.signs + j0 + i));
+          const int8_t* s8 = reinterpret_cast<const int8_t*>(&sg);
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (s8[e] < 0) v[i + e] = -v[i + e];
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i)
+          if (i < cnt && a.signs[j0 + i] < 0) v[i] = -v[i];
+      }
+    }
+
+    // ---- block Walsh-Hadamard transform (natural Sylvester order) ---------
+    if constexpr (B > 0) {
+#pragma unroll
+      for (int h = 1; h < IN_THREAD; h <<= 1) {
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          if ((i & h) == 0) {
+            const float lo = v[i], hi = v[i + h];
+            v[i] = __fadd_rn(lo, hi);
+            v[i + h] = __fsub_rn(lo, hi);
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 1; off < LANE_SPAN; off <<= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          const float own = v[i];
+          const float peer = __shfl_xor_sync(0xffffffffu, own, off);
+          v[i] = upper ? __fsub_rn(peer, own) : __fadd_rn(own, peer);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i) v[i] = __fmul_rn(v[i], a.inv_sqrt_block);
+    }
+
+    if constexpr (OUT == OUT_F32) {
+      float* yrow = a.y + row * K;
+      if (fullchunk && vec) {
+#pragma unroll
+        for (int i = 0; i < kChunk; i += 4)
+          *reinterpret_cast<float4*>(yrow + j0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i)
+          if (i < cnt) yrow[j0 + i] = v[i];
+      }
+    } else {
+      // ---- row peak, per-row scale, codes ----------------------------------
+      float peak = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i)
+        if (i < cnt) peak = fmaxf(peak, fabsf(v[i]));
+      peak = cta_max(peak, red, W);
+      const float qmax = (OUT == OUT_E4M3) ? 448.0f : 127.0f;
+      const float scale = (peak == 0.0f) ? 1.0f : __fdiv_rn(peak, qmax);
+      const float rinv = __frcp_rn(scale);
+      const bool fast = scale >= 0x1p-100f;
+      if (tid == 0) a.s[row] = scale;
+      uint8_t* qrow = reinterpret_cast<uint8_t*>(a.q) + row * K;
+      if (fullchunk && vec && (K % 16) == 0) {
+#pragma unroll
+        for (int i = 0; i < kChunk; i += 16) {
+          uint32_t w[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            uint32_t b0, b1, b2, b3;
+            if constexpr (OUT == OUT_E4M3) {
+              b0 = quant_e4m3(v[i + 4 * p + 0], scale, rinv, fast);
+              b1 = quant_e4m3(v[i + 4 * p + 1], scale, rinv, fast);
+              b2 = quant_e4m3(v[i + 4 * p + 2], scale, rinv, fast);
+              b3 = quant_e4m3(v[i + 4 * p + 3], scale, rinv, fast);
+            } else {
+              b0 = quant_i8(v[i + 4 * p + 0], scale, rinv, fast) & 0xFF;
+              b1 = quant_i8(v[i + 4 * p + 1], scale, rinv, fast) & 0xFF;
+              b2 = quant_i8(v[i + 4 * p + 2], scale, rinv, fast) & 0xFF;
+              b3 = quant_i8(v[i + 4 * p + 3], scale, rinv, fast) & 0xFF;
+            }
+            w[p] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+          }
+          *reinterpret_cast<uint4*>(qrow + j0 + i) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          if (i < cnt) {
+            if constexpr (OUT == OUT_E4M3)
+              qrow[j0 + i] = static_cast<uint8_t>(quant_e4m3(v[i], scale, rinv, fast));
+            else
+              qrow[j0 + i] = static_cast<uint8_t>(quant_i8(v[i], scale, rinv, fast));
+          }
+        }
+      }
+    }
+  }
+  if (stages > 0 && abort_flag && tid == 0) {
+    // A wait gave up: let the copies already issued land before the CTA exits.
+    for (int s2 = 0; s2 < stages; ++s2) {
+      const unsigned long long t0 = globaltimer_ns();
+      for (uint32_t ph = 0; ph < 2; ++ph) {
+        while (!mbar_try_wait(&full_bar[s2], ph)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
         }
       }
     }
@@ -349,32 +477,59 @@ __global__ void __launch_bounds__(512) row_prep_kernel(const RowPrepArgs a) {
 }
 
 template <typename T, int B, int OUT>
-static cudaError_t launch_t(const RowPrepArgs& a, cudaStream_t stream) {
-  const unsigned threads = static_cast<unsigned>(a.warps) * 32u;
-  row_prep_kernel<T, B, OUT><<<static_cast<unsigned>(a.rows), threads, 0, stream>>>(a);
+static cudaError_t launch_t(const RowPrepArgs& a, const RowMaps& maps, cudaStream_t stream) {
+  auto kern = row_prep_kernel<T, B, OUT>;
+  const int threads = a.warps * 32;
+  const int64_t row_bytes = a.K * int64_t(sizeof(T));
+  const int inputs = a.branch ? 2 : 1;
+  const int64_t buf_stride = (row_bytes + 1023) & ~int64_t(1023);
+  int stages = 0;
+  if (maps.valid) {
+    const int64_t per_stage = buf_stride * inputs;
+    stages = per_stage <= 24 * 1024 ? 4 : (per_stage <= 48 * 1024 ? 3 : (per_stage <= 96 * 1024 ? 2 : 0));
+  }
+  const int smem = stages > 0 ? static_cast<int>(stages * buf_stride * inputs) + 1024 : 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) per_sm = 1;
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  int64_t grid = int64_t(sms) * per_sm;
+  if (grid > a.rows) grid = a.rows;
+  kern<<<static_cast<unsigned>(grid), threads, smem, stream>>>(maps.x, maps.b, a, stages,
+                                                               maps.box_rows);
   return cudaGetLastError();
 }
 
 template <typename T, int OUT>
-static cudaError_t launch_b(const RowPrepArgs& a, int block, cudaStream_t stream) {
+static cudaError_t launch_b(const RowPrepArgs& a, const RowMaps& m, int block,
+                           cudaStream_t stream) {
   switch (block) {
-    case 0: return launch_t<T, 0, OUT>(a, stream);
-    case 32: return launch_t<T, 32, OUT>(a, stream);
-    case 64: return launch_t<T, 64, OUT>(a, stream);
-    case 128: return launch_t<T, 128, OUT>(a, stream);
-    case 256: return launch_t<T, 256, OUT>(a, stream);
-    case 512: return launch_t<T, 512, OUT>(a, stream);
-    case 1024: return launch_t<T, 1024, OUT>(a, stream);
+    case 0: return launch_t<T, 0, OUT>(a, m, stream);
+    case 32: return launch_t<T, 32, OUT>(a, m, stream);
+    case 64: return launch_t<T, 64, OUT>(a, m, stream);
+    case 128: return launch_t<T, 128, OUT>(a, m, stream);
+    case 256: return launch_t<T, 256, OUT>(a, m, stream);
+    case 512: return launch_t<T, 512, OUT>(a, m, stream);
+    case 1024: return launch_t<T, 1024, OUT>(a, m, stream);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <typename T>
-static cudaError_t launch_o(const RowPrepArgs& a, int block, int out, cudaStream_t stream) {
+static cudaError_t launch_o(const RowPrepArgs& a, const RowMaps& m, int block, int out,
+                           cudaStream_t stream) {
   switch (out) {
-    case OUT_INT8: return launch_b<T, OUT_INT8>(a, block, stream);
-    case OUT_E4M3: return launch_b<T, OUT_E4M3>(a, block, stream);
-    case OUT_F32: return launch_b<T, OUT_F32>(a, block, stream);
+    case OUT_INT8: return launch_b<T, OUT_INT8>(a, m, block, stream);
+    case OUT_E4M3: return launch_b<T, OUT_E4M3>(a, m, block, stream);
+    case OUT_F32: return launch_b<T, OUT_F32>(a, m, block, stream);
     default: return cudaErrorInvalidValue;
   }
 }

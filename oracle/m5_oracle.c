@@ -22,9 +22,11 @@
  * with an unspecified reduction order, which is why the reference accepts a
  * one-code difference.  This restatement instead fixes the FP32 order so it is
  * bit-comparable with the CUDA kernels:
- *   - row reductions: each (warp, lane) accumulates its elements sequentially
- *     in (slot, slice, element) order, lanes combine with a xor butterfly
- *     (offsets 16, 8, 4, 2, 1), warps are summed 0..W-1 in order;
+ *   - row reductions: thread t of the row owns the contiguous 64-element chunk
+ *     [64 t, 64 t + 64) and sums it sequentially; the 32 lanes of a warp
+ *     combine with a xor butterfly of increasing offset (1, 2, 4, 8, 16), i.e.
+ *     a pairwise tree over chunk index; the W = ceil(K / 2048) warp partials
+ *     (padded with zeros to 16) combine pairwise (w0+w1, w2+w3, ...);
  *   - sum of squares uses fmaf(x, x, acc), the centered LayerNorm pass
  *     fmaf(d, d, acc) with d = x - mean;
  *   - Hadamard butterflies in natural Sylvester order with increasing stride,
@@ -49,7 +51,6 @@
 #define OUT_E4M3 1
 #define OUT_F32 2
 
-#define MAX_VALUES 64
 
 /* ------------------------------------------------------------------ dtypes */
 static float bf16_to_f32(uint16_t h) {
@@ -136,59 +137,49 @@ uint8_t m5o_e4m3_encode(float z) {
 static uint8_t e4m3_code(float v, float scale) { return m5o_e4m3_encode(v / scale); }
 
 /* ------------------------------------------------------------------ layout */
+#define CHUNK 64
+
 int m5o_row_prep_warps(int64_t K, int block) {
-  const int unit = block > 256 ? block : 256;
-  const int vpu = unit / 256;
-  const int slots = MAX_VALUES / (8 * vpu);
-  const int64_t units = (K + unit - 1) / unit;
-  int64_t w = (units + slots - 1) / slots;
-  if (w < 1) w = 1;
-  return w > 1024 ? 1024 : (int)w;
+  (void)block;
+  const int64_t w = (K + 2047) / 2048;
+  return w < 1 ? 1 : (w > 1024 ? 1024 : (int)w);
 }
 
-/* Sum of f(v[j]) over one row in the kernel's order.  kind 0: sum of v,
- * kind 1: sum of v*v (fma), kind 2: sum of (v-mean)^2 (fma). */
-static float row_reduce(const float* v, int64_t K, int block, int W, int kind, float mean) {
-  const int unit = block > 256 ? block : 256;
-  const int vpu = unit / 256;
-  const int slots = MAX_VALUES / (8 * vpu);
-  const int units = (int)((K + unit - 1) / unit);
-  float warp_part[1024];
+/* Sum of f(v[j]) over one row in the kernel's canonical order.  kind 0: sum
+ * of v, kind 1: sum of v*v (fma), kind 2: sum of (v-mean)^2 (fma). */
+static float row_reduce(const float* v, int64_t K, int W, int kind, float mean) {
+  float part[16];
+  for (int w = 0; w < 16; ++w) part[w] = 0.0f;
   for (int w = 0; w < W; ++w) {
     float lane_acc[32];
     for (int l = 0; l < 32; ++l) {
+      const int64_t j0 = ((int64_t)w * 32 + l) * CHUNK;
       float acc = 0.0f;
-      for (int s = 0; s < slots; ++s) {
-        const int u = s * W + w;
-        if (u >= units) continue;
-        for (int vv = 0; vv < vpu; ++vv) {
-          for (int e = 0; e < 8; ++e) {
-            const int64_t j = (int64_t)u * unit + vv * 256 + l * 8 + e;
-            if (j >= K) continue;
-            const float x = v[j];
-            if (kind == 0) {
-              acc = acc + x;
-            } else if (kind == 1) {
-              acc = fmaf(x, x, acc);
-            } else {
-              const float d = x - mean;
-              acc = fmaf(d, d, acc);
-            }
-          }
+      for (int i = 0; i < CHUNK; ++i) {
+        const int64_t j = j0 + i;
+        if (j >= K) break;
+        const float x = v[j];
+        if (kind == 0) {
+          acc = acc + x;
+        } else if (kind == 1) {
+          acc = fmaf(x, x, acc);
+        } else {
+          const float d = x - mean;
+          acc = fmaf(d, d, acc);
         }
       }
       lane_acc[l] = acc;
     }
-    for (int off = 16; off > 0; off >>= 1) {
+    for (int off = 1; off < 32; off <<= 1) {
       float nxt[32];
       for (int l = 0; l < 32; ++l) nxt[l] = lane_acc[l] + lane_acc[l ^ off];
       memcpy(lane_acc, nxt, sizeof(nxt));
     }
-    warp_part[w] = lane_acc[0];
+    part[w] = lane_acc[0];
   }
-  float t = warp_part[0];
-  for (int w = 1; w < W; ++w) t = t + warp_part[w];
-  return t;
+  for (int step = 1; step < 16; step <<= 1)
+    for (int w = 0; w + step < 16; w += 2 * step) part[w] = part[w] + part[w + step];
+  return part[0];
 }
 
 static void fwht_block(float* v, int B) {
@@ -233,11 +224,11 @@ void m5o_row_prep(const void* x, int x_dtype, const void* branch, const void* ga
     if (norm != NORM_NONE) {
       const float kf = (float)K;
       const float first =
-          row_reduce(v, K, block, W, norm == NORM_LAYER ? 0 : 1, 0.0f) / kf;
+          row_reduce(v, K, W, norm == NORM_LAYER ? 0 : 1, 0.0f) / kf;
       float moment = first;
       if (norm == NORM_LAYER) {
         mean = first;
-        moment = row_reduce(v, K, block, W, 2, mean) / kf;
+        moment = row_reduce(v, K, W, 2, mean) / kf;
       }
       inv = 1.0f / sqrtf(moment + eps);
     }

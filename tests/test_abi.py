@@ -1,0 +1,110 @@
+"""The C-ABI library loads here (no GPU needed) and exports every declared symbol.
+
+No compute call is made: these tests only check the boundary itself and that
+the product path has no CPU fallback.
+"""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "m5b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"M5B_API\s+[\w\s\*]+?\b(m5b_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_operator_contracts():
+    names = declared_symbols()
+    for required in ("m5b_quantize", "m5b_rotate", "m5b_hadamard_quantize",
+                     "m5b_fused_norm_hadamard_quantize",
+                     "m5b_fused_gated_residual_norm_hadamard_quantize", "m5b_gemm",
+                     "m5b_projection_qk_rope", "m5b_last_error", "m5b_device_status"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    from m5kernels_b200 import _lib
+
+    lib = _lib.lib()
+    for name in declared_symbols():
+        assert isinstance(getattr(lib, name), ctypes._CFuncPtr), name
+    assert set(declared_symbols()) <= set(_lib.exported_symbols()) | {"m5b_version"}
+    assert lib.m5b_version() >= 100
+    assert lib.m5b_last_error() == b""
+
+
+def test_status_codes_match_header():
+    from m5kernels_b200 import _lib
+
+    text = HEADER.read_text()
+    for name, value in (("M5B_OK", _lib.OK), ("M5B_EINVAL", _lib.EINVAL),
+                        ("M5B_EUNSUPPORTED", _lib.EUNSUPPORTED), ("M5B_ECUDA", _lib.ECUDA),
+                        ("M5B_BF16", _lib.BF16), ("M5B_I32", _lib.I32)):
+        assert re.search(rf"#define {name} {value}\b", text), name
+
+
+def test_contract_errors_come_back_through_the_abi_without_a_gpu():
+    """Size checks run on the host: bad arguments fail before any CUDA call."""
+    from m5kernels_b200 import _lib
+
+    lib = _lib.lib()
+    rc = lib.m5b_quantize(None, _lib.BF16, 0, 16, 0, None, None, None)
+    assert rc == _lib.EINVAL and b"nonempty" in lib.m5b_last_error()
+    rc = lib.m5b_rotate(ctypes.c_void_p(16), _lib.BF16, 4, 96, 64, None, ctypes.c_void_p(16), None)
+    assert rc == _lib.EUNSUPPORTED and b"divisible" in lib.m5b_last_error()
+    rc = lib.m5b_gemm(ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 4, 96, 1, None, None, None, 2,
+                      None, None, 0, None, None, None, 0, None)
+    assert rc == _lib.EUNSUPPORTED and b"FP8" in lib.m5b_last_error()
+    with pytest.raises(NotImplementedError, match="FP8"):
+        _lib.check(rc)
+
+
+def test_operators_refuse_cpu_tensors():
+    import m5kernels_b200 as m
+    from m5kernels_b200._lib import ExtensionMissing
+
+    with pytest.raises(ExtensionMissing):
+        m.quantize(torch.ones(4, 64), "int8")
+    with pytest.raises(ExtensionMissing):
+        m.rotate(torch.ones(4, 64), 32, torch.ones(64, dtype=torch.int8))
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    from m5kernels_b200 import _lib
+
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "libm5b200.so")
+    with pytest.raises(_lib.ExtensionMissing, match="not built"):
+        _lib.lib()
+
+
+def test_python_contract_validation_matches_reference_messages():
+    import m5kernels_b200 as m
+
+    with pytest.raises(NotImplementedError):
+        m.quantize(torch.ones(2, 64), "mxint8")
+    with pytest.raises(ValueError, match="nonempty"):
+        m.quantize(torch.ones(0, 64), "int8")
+    with pytest.raises(ValueError, match="power of two"):
+        m.rotate(torch.ones(2, 96), 48, torch.ones(96, dtype=torch.int8))
+    with pytest.raises(NotImplementedError, match="divisible"):
+        m.rotate(torch.ones(2, 96), 64, torch.ones(96, dtype=torch.int8))
+    a = torch.ones(2, 96, dtype=torch.uint8)
+    with pytest.raises(NotImplementedError, match="stride"):
+        m.gemm(a, a, "fp8", a_scales=torch.ones(2), b_scales=torch.ones(2))
+    with pytest.raises(ValueError, match="norm"):
+        m.fused_norm_hadamard_quantize(torch.ones(2, 64), torch.ones(64), torch.ones(64),
+                                       torch.ones(64), torch.ones(64, dtype=torch.int8), 32,
+                                       norm="batch")
+    with pytest.raises(ValueError, match="128-wide"):
+        m.projection_qk_rope(torch.ones(2, 64, dtype=torch.int8), torch.ones(100, 64, dtype=torch.int8),
+                             torch.ones(128, dtype=torch.bfloat16), torch.ones(2, 4, dtype=torch.bfloat16),
+                             torch.ones(2, 4, dtype=torch.bfloat16), a_scales=torch.ones(2),
+                             b_scales=torch.ones(100))
