@@ -349,8 +349,13 @@ int m5b_fused_gated_residual_norm_hadamard_quantize(
   return run_row_prep(a, x_dtype, block_size, out, stream);
 }
 
+// A CTA pair (cta_group::2, 256 x 256 tiles) when the problem has at least
+// one full pair tile of rows and more than 128 output columns.
+static bool use_pair(int epi, int64_t m, int64_t n) { return epi != EPI_QK && m >= 256 && n > 128; }
+
 static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, const void* a,
-                       const void* b, int64_t m, int64_t n, int64_t k, int mode, int bn) {
+                       const void* b, int64_t m, int64_t n, int64_t k, int mode, int bn,
+                       bool pair) {
   if (m <= 0 || n <= 0 || k <= 0) return fail(M5B_EINVAL, "A and B must be nonempty matrices");
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL)
     return fail(M5B_EUNSUPPORTED, "matrix dimensions exceed 2^31-1");
@@ -377,14 +382,15 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, const void
   if (rc) return rc;
   rc = make_kmajor_map(&ta, a, m, k, eb, 128);
   if (rc) return rc;
-  rc = make_kmajor_map(&tb, b, n, k, eb, bn);
+  rc = make_kmajor_map(&tb, b, n, k, eb, pair ? bn / 2 : bn);
   if (rc) return rc;
   g.M = static_cast<int>(m);
   g.N = static_cast<int>(n);
   g.K = static_cast<int>(k);
   g.kind = kind;
   const int k_elems = 128 / eb;
-  g.num_m_blocks = static_cast<int>((m + 127) / 128);
+  const int tile_m = pair ? 256 : 128;
+  g.num_m_blocks = static_cast<int>((m + tile_m - 1) / tile_m);
   g.num_n_blocks = static_cast<int>((n + bn - 1) / bn);
   g.num_k_blocks = static_cast<int>((k + k_elems - 1) / k_elems);
   g.group_m = 8;
@@ -392,15 +398,16 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, const void
 }
 
 static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, int bn,
-                       void* stream) {
+                       bool pair, void* stream) {
   unsigned int* status = nullptr;
   int sms = 0;
   int rc = device_state(&status, &sms);
   if (rc) return rc;
   g.status = status;
   const int tiles = g.num_m_blocks * g.num_n_blocks;
-  const int grid = tiles < sms ? tiles : sms;
-  cudaError_t e = launch_gemm(ta, tb, g, bn, grid, static_cast<cudaStream_t>(stream));
+  const int units = pair ? sms / 2 : sms;  // persistent CTAs (pairs)
+  const int grid = (tiles < units ? tiles : units) * (pair ? 2 : 1);
+  cudaError_t e = launch_gemm(ta, tb, g, bn, grid, pair, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
   return ok();
 }
@@ -414,8 +421,9 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
   g.epi = EPI_PLAIN;
   g.N = static_cast<int>(n);
   const int bn = gemm_block_n(g);
+  const bool pair = use_pair(EPI_PLAIN, m, n);
   CUtensorMap ta, tb;
-  int rc = gemm_common(g, ta, tb, a, b, m, n, k, mode, bn);
+  int rc = gemm_common(g, ta, tb, a, b, m, n, k, mode, bn, pair);
   if (rc) return rc;
   if (out_dtype == M5B_I32) {
     // Raw INT32 accumulators: INT8 operands, no scales and no epilogue.
@@ -426,7 +434,7 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
     if (!out) return fail(M5B_EINVAL, "output pointer is NULL");
     g.out = out;
     g.out_dtype = DT_I32;
-    return gemm_launch(ta, tb, g, bn, stream);
+    return gemm_launch(ta, tb, g, bn, pair, stream);
   }
   const bool quant = (mode == M5B_MODE_INT8 || mode == M5B_MODE_FP8);
   if (quant && (!a_scales || !b_scales)) return fail(M5B_EINVAL, "scales required");
@@ -465,7 +473,7 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
     g.bias = bias;
     g.bias_row_map = bias_row_map;
   }
-  return gemm_launch(ta, tb, g, bn, stream);
+  return gemm_launch(ta, tb, g, bn, pair, stream);
 }
 
 int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
@@ -492,7 +500,7 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
   GemmArgs g{};
   g.epi = EPI_QK;
   CUtensorMap ta, tb;
-  int rc = gemm_common(g, ta, tb, a, b, m, n, k, mode, 128);
+  int rc = gemm_common(g, ta, tb, a, b, m, n, k, mode, 128, false);
   if (rc) return rc;
   g.quantized = quant ? 1 : 0;
   g.a_scales = a_scales;
@@ -504,7 +512,7 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
   g.sin = sin;
   g.rope_half = rope_half;
   g.eps = epsilon;
-  return gemm_launch(ta, tb, g, 128, stream);
+  return gemm_launch(ta, tb, g, 128, false, stream);
 }
 
 }  // extern "C"

@@ -7,7 +7,7 @@
 // src/m5kernels/qk_rope.py:120-182 (shaders/qk_rope_projection.metal,
 // shaders/qk_rope_body.metal).
 //
-// Structure (one CTA per SM, 6 warps):
+// Structure (one CTA per SM, 6 warps; optionally CTA pairs, see PAIR below):
 //   warp 0     TMA producer: 128-byte K slices of A (128 rows) and B (BN rows)
 //              into a STAGES-deep ring of 128B-swizzled shared-memory tiles.
 //   warp 1     TMEM allocator + single-thread tcgen05.mma issuer
@@ -20,6 +20,13 @@
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
 // the MMAs of tile i+1.  Tiles are walked in grouped-M order, CTA b taking
 // tiles b, b + grid, ...  No TMA multicast is used anywhere.
+//
+// PAIR (cluster of two CTAs on neighbouring SMs, tcgen05 cta_group::2): the
+// tile is 256 x BN.  Each CTA loads its own 128 rows of A and its own BN/2
+// rows of B (plain TMA loads, transaction bytes counted on the even CTA's
+// barrier); the even CTA's MMA warp issues M=256 MMAs that read both CTAs'
+// shared memory and write 128 accumulator rows into each CTA's TMEM.  Per SM
+// this halves the B traffic into shared memory, so a 6-deep ring fits.
 //
 // Rounding contract (bit-reproducible, mirrored by the C oracle):
 //   quantized:  v = fp32(acc) * sa[m] * sb[n]   (int32 -> fp32 RNE, then two
@@ -35,12 +42,14 @@ namespace m5b {
 constexpr int kBM = 128;
 constexpr int kQKStride = 130;  // bf16 elements per staged Q/K row (conflict-free)
 
-template <int BN, bool QK>
+template <int BN, bool QK, bool PAIR>
 struct GemmCfg {
-  static constexpr int A_BYTES = kBM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int A_BYTES = kBM * 128;                 // this CTA's A rows
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;         // this CTA's B rows
+  static constexpr int B_BYTES = B_ROWS * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = QK ? 5 : (BN == 256 ? 4 : 6);
+  static constexpr int TILE_M = PAIR ? 2 * kBM : kBM;
+  static constexpr int STAGES = QK ? 5 : (STAGE_BYTES <= 32 * 1024 ? 6 : 4);
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
   static constexpr int QK_BYTES = QK ? kBM * kQKStride * 2 : 0;
@@ -48,6 +57,7 @@ struct GemmCfg {
 };
 
 __device__ __forceinline__ void tile_coords(int t, const GemmArgs& g, int& m_blk, int& n_blk) {
+  // m_blk indexes tiles of TILE_M rows (128, or 256 for a CTA pair).
   const int group_size = g.group_m * g.num_n_blocks;
   const int group = t / group_size;
   const int first_m = group * g.group_m;
@@ -170,14 +180,14 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
   }
 }
 
-template <int KIND, int BN, bool QK>
+template <int KIND, int BN, bool QK, bool PAIR>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, const GemmArgs g) {
-  using Cfg = GemmCfg<BN, QK>;
+  using Cfg = GemmCfg<BN, QK, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int K_ELEMS = (KIND == KIND_BF16 || KIND == KIND_F16) ? 64 : 128;
-  constexpr uint32_t IDESC = make_idesc(KIND, BN);
+  constexpr uint32_t IDESC = make_idesc(KIND, Cfg::TILE_M, BN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -196,6 +206,10 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_rank() : 0;  // position in the CTA pair
+  const bool leader = rank == 0;
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -204,7 +218,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], PAIR ? 8 : 4);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -215,11 +229,17 @@ __global__ void __launch_bounds__(192, 1)
     tma_prefetch_desc(&tmap_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -232,18 +252,27 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      for (int t = unit; t < num_tiles && !*abort_flag; t += units) {
         int m_blk, n_blk;
         tile_coords(t, g, m_blk, n_blk);
+        const int a_row = m_blk * Cfg::TILE_M + static_cast<int>(rank) * kBM;
+        const int b_row = n_blk * BN + static_cast<int>(rank) * Cfg::B_ROWS;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, g.status,
                                  DEV_TIMEOUT_PRODUCER))
             break;
-          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmap_a, &full[stage], kb * K_ELEMS,
-                      m_blk * kBM);
-          tma_load_2d(sB + stage * Cfg::B_BYTES, &tmap_b, &full[stage], kb * K_ELEMS,
-                      n_blk * BN);
+          if constexpr (PAIR) {
+            // The even CTA expects both CTAs' bytes; each CTA loads its halves.
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+            tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmap_a, &full[stage], kb * K_ELEMS,
+                             a_row);
+            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmap_b, &full[stage], kb * K_ELEMS,
+                             b_row);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+            tma_load_2d(sA + stage * Cfg::A_BYTES, &tmap_a, &full[stage], kb * K_ELEMS, a_row);
+            tma_load_2d(sB + stage * Cfg::B_BYTES, &tmap_b, &full[stage], kb * K_ELEMS, b_row);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -251,9 +280,11 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      if (*abort_flag) {
+      if (*abort_flag && (!PAIR || leader)) {
         // Drain: wait (bounded) until the copies already issued into the
         // ring have landed, so no TMA write targets this CTA after it exits.
+        // (In a pair the even CTA's barriers count both CTAs' copies; the
+        // closing cluster barrier keeps the odd CTA alive until then.)
         int s = stage, ph = phase;
         for (int i = 0; i < STAGES && i < issued; ++i) {
           s = (s == 0) ? STAGES - 1 : s - 1;
@@ -270,12 +301,12 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
+    if ((!PAIR || leader) && elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+      for (int t = unit; t < num_tiles && ok; t += units, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, abort_flag, g.status,
@@ -295,21 +326,34 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            tc_mma<KIND>(d_tmem, smem_desc_k128(a_base + k * 32), smem_desc_k128(b_base + k * 32),
-                         IDESC, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (PAIR)
+              tc_mma_pair<KIND>(d_tmem, smem_desc_k128(a_base + k * 32),
+                                smem_desc_k128(b_base + k * 32), IDESC, (kb | k) != 0 ? 1u : 0u);
+            else
+              tc_mma<KIND>(d_tmem, smem_desc_k128(a_base + k * 32),
+                           smem_desc_k128(b_base + k * 32), IDESC, (kb | k) != 0 ? 1u : 0u);
           }
-          tc_commit(&empty[stage]);
+          if constexpr (PAIR)
+            tc_commit_pair(&empty[stage]);
+          else
+            tc_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(&acc_full[acc]);
+        if constexpr (PAIR)
+          tc_commit_pair(&acc_full[acc]);
+        else
+          tc_commit(&acc_full[acc]);
       }
       if (!ok) {
         // Aborted: let every MMA already issued retire before TMEM is freed.
-        tc_commit(drain);
+        if constexpr (PAIR)
+          tc_commit_pair(drain);
+        else
+          tc_commit(drain);
         const unsigned long long t0 = globaltimer_ns();
         while (!mbar_try_wait(drain, 0)) {
           if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -322,9 +366,18 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
-    const int row_in_tile = quarter * 32 + lane;
+    const int row_in_tile = static_cast<int>(rank) * kBM + quarter * 32 + lane;
+    // acc_empty lives in the even CTA of a pair: the odd CTA arrives remotely.
+    const uint32_t acc_empty_remote0 = PAIR ? map_to_rank(&acc_empty[0], 0) : 0u;
+    const uint32_t acc_empty_remote1 = PAIR ? map_to_rank(&acc_empty[1], 0) : 0u;
+    auto release_acc = [&](int acc) {
+      if constexpr (PAIR)
+        mbar_arrive_cluster(acc == 0 ? acc_empty_remote0 : acc_empty_remote1);
+      else
+        mbar_arrive(&acc_empty[acc]);
+    };
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    for (int t = unit; t < num_tiles; t += units, ++local) {
       int m_blk, n_blk;
       tile_coords(t, g, m_blk, n_blk);
       const int acc = local & 1;
@@ -334,7 +387,7 @@ __global__ void __launch_bounds__(192, 1)
         break;
       __syncwarp();
       tc_fence_after();
-      const int64_t row = int64_t(m_blk) * kBM + row_in_tile;
+      const int64_t row = int64_t(m_blk) * Cfg::TILE_M + row_in_tile;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const float sa = (g.quantized && row < g.M) ? __ldg(g.a_scales + row) : 1.0f;
@@ -348,11 +401,11 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (lane == 0) release_acc(acc);
       } else {
         // Pass 1: BF16 projection z, its square sum (sequential over the 128
         // head channels) and a private staged copy of this row.
-        __nv_bfloat16* zrow = qk_stage + row_in_tile * kQKStride;
+        __nv_bfloat16* zrow = qk_stage + (quarter * 32 + lane) * kQKStride;
         float sumsq = 0.0f;
         const int head = n_blk;
 #pragma unroll 1
@@ -378,7 +431,7 @@ __global__ void __launch_bounds__(192, 1)
         // The accumulator is no longer needed: hand it back to the MMA warp.
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (lane == 0) release_acc(acc);
         if (row < g.M) {
           const float inv =
               __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, 128.0f), g.eps)));
@@ -420,26 +473,41 @@ __global__ void __launch_bounds__(192, 1)
   // ------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer no longer touches this CTA
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
-template <int KIND, int BN, bool QK>
+template <int KIND, int BN, bool QK, bool PAIR>
 static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
                             int grid, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN, QK>;
-  auto kern = gemm_tc_kernel<KIND, BN, QK>;
-  static bool configured = false;  // attribute is per function, idempotent
-  if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    configured = true;
+  using Cfg = GemmCfg<BN, QK, PAIR>;
+  auto kern = gemm_tc_kernel<KIND, BN, QK, PAIR>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (PAIR) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
   }
-  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ta, tb, g);
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, g);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -449,13 +517,14 @@ int gemm_block_n(const GemmArgs& g) {
 }
 
 cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, int bn,
-                        int grid, cudaStream_t stream) {
+                        int grid, bool pair, cudaStream_t stream) {
   const bool qk = g.epi == EPI_QK;
-#define M5B_KIND_CASE(KIND_)                                                   \
-  case KIND_:                                                                  \
-    if (qk) return launch_k<KIND_, 128, true>(ta, tb, g, grid, stream);        \
-    if (bn == 128) return launch_k<KIND_, 128, false>(ta, tb, g, grid, stream); \
-    return launch_k<KIND_, 256, false>(ta, tb, g, grid, stream);
+#define M5B_KIND_CASE(KIND_)                                                          \
+  case KIND_:                                                                         \
+    if (qk) return launch_k<KIND_, 128, true, false>(ta, tb, g, grid, stream);        \
+    if (pair) return launch_k<KIND_, 256, false, true>(ta, tb, g, grid, stream);      \
+    if (bn == 128) return launch_k<KIND_, 128, false, false>(ta, tb, g, grid, stream); \
+    return launch_k<KIND_, 256, false, false>(ta, tb, g, grid, stream);
   switch (g.kind) {
     M5B_KIND_CASE(KIND_I8)
     M5B_KIND_CASE(KIND_F8)

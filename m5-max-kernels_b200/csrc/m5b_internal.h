@@ -85,7 +85,7 @@ struct GemmArgs {
 };
 
 cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, int bn,
-                        int grid, cudaStream_t stream);
+                        int grid, bool pair, cudaStream_t stream);
 int gemm_block_n(const GemmArgs& g);
 
 }  // namespace m5b

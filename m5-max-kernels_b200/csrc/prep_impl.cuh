@@ -27,10 +27,12 @@
 // elements [64 t, 64 t + 64) of the row, held in registers.  Hence Hadamard
 // strides 1..32 are register butterflies and strides 64..B/2 are warp
 // shuffles (lane xor 1 .. B/128).  Row reductions have one canonical order,
-// mirrored by the C oracle: each thread sums its chunk sequentially; lanes
-// combine with a xor butterfly of increasing offset (1, 2, 4, 8, 16 — a
-// pairwise tree over chunk index); warps combine pairwise in index order
-// (w0+w1, w2+w3, ... then pairs of pairs).
+// mirrored by the C oracle: within a chunk, eight accumulators a[e] collect
+// elements e, e+8, ..., e+56 in order and combine pairwise
+// ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)); lanes combine with a xor butterfly of
+// increasing offset (1, 2, 4, 8, 16 — a pairwise tree over chunk index);
+// warps combine pairwise in index order (w0+w1, w2+w3, ... then pairs of
+// pairs).
 #pragma once
 #include "common.cuh"
 #include "m5b_internal.h"
@@ -69,6 +71,33 @@ __device__ __forceinline__ uint32_t quant_e4m3(float v, float scale, float inv, 
       __nv_cvt_float_to_fp8(__fdiv_rn(v, scale), __NV_SATFINITE, __NV_E4M3));
 }
 
+// Round-to-nearest-even of |t| < 2^22 by the 1.5 * 2^23 magic constant: the
+// low byte of the sum's bit pattern is the two's-complement int8 of rint(t).
+constexpr float kRoundMagic = 12582912.0f;
+
+// Quantize n (multiple of 4) values to int8 codes packed four per word.
+// Fast path only; returns true if any value needs the exact re-check (its
+// product lies within 2^-14 of a half-integer, see quant_i8).
+template <int N>
+__device__ __forceinline__ bool quant_i8_fast(const float* v, float inv, uint32_t* words) {
+  bool near_tie = false;
+#pragma unroll
+  for (int w = 0; w < N / 4; ++w) {
+    uint32_t u[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float t = __fmul_rn(v[4 * w + e], inv);
+      const float m = __fadd_rn(t, kRoundMagic);
+      const float r = __fsub_rn(m, kRoundMagic);
+      near_tie |= fabsf(__fsub_rn(t, r)) > 0.5f - 0x1p-14f;
+      u[e] = __float_as_uint(m);
+    }
+    words[w] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040),
+                           0x5410);
+  }
+  return near_tie;
+}
+
 // ---------------------------------------------------------------- loads
 template <typename T>
 __device__ __forceinline__ void cvt8(const uint4& raw, float* out) {
@@ -103,6 +132,46 @@ __device__ __forceinline__ void param8(const void* base, int dtype, int64_t j, b
 }
 
 // ---------------------------------------------------------------- reductions
+// Canonical chunk sum: eight interleaved accumulators, combined pairwise.
+template <int KIND>  // 0: sum v, 1: sum v*v, 2: sum (v-mean)^2
+__device__ __forceinline__ float chunk_sum(const float* v, int cnt, float mean) {
+  float a[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) a[e] = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 64; i += 8) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (i + e < cnt) {
+        const float x = v[i + e];
+        if constexpr (KIND == 0) {
+          a[e] = __fadd_rn(a[e], x);
+        } else if constexpr (KIND == 1) {
+          a[e] = __fmaf_rn(x, x, a[e]);
+        } else {
+          const float d = __fsub_rn(x, mean);
+          a[e] = __fmaf_rn(d, d, a[e]);
+        }
+      }
+    }
+  }
+  return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
+                   __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
+}
+
+// max |v| over a chunk as a balanced tree (exact in any order)
+__device__ __forceinline__ float chunk_absmax(const float* v, int cnt) {
+  float m[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) m[e] = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 64; i += 8)
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (i + e < cnt) m[e] = fmaxf(m[e], fabsf(v[i + e]));
+  return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])),
+               fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+}
 __device__ __forceinline__ float warp_sum_tree(float v) {
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
@@ -310,30 +379,14 @@ __global__ void __launch_bounds__(512)
     // ---- normalization statistics ----------------------------------------
     float mean = 0.0f, inv = 1.0f;
     if (a.norm != NORM_NONE) {
-      float acc = 0.0f;
-      if (a.norm == NORM_LAYER) {
-#pragma unroll
-        for (int i = 0; i < kChunk; ++i)
-          if (i < cnt) acc = __fadd_rn(acc, v[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < kChunk; ++i)
-          if (i < cnt) acc = __fmaf_rn(v[i], v[i], acc);
-      }
+      const float acc = (a.norm == NORM_LAYER) ? chunk_sum<0>(v, cnt, 0.0f)
+                                               : chunk_sum<1>(v, cnt, 0.0f);
       const float kf = static_cast<float>(K);
       const float first = __fdiv_rn(cta_sum(acc, red, W), kf);
       float moment = first;
       if (a.norm == NORM_LAYER) {
         mean = first;
-        float acc2 = 0.0f;
-#pragma unroll
-        for (int i = 0; i < kChunk; ++i) {
-          if (i < cnt) {
-            const float d = __fsub_rn(v[i], mean);
-            acc2 = __fmaf_rn(d, d, acc2);
-          }
-        }
-        moment = __fdiv_rn(cta_sum(acc2, red, W), kf);
+        moment = __fdiv_rn(cta_sum(chunk_sum<2>(v, cnt, mean), red, W), kf);
       }
       inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(moment, a.eps)));
 
@@ -417,11 +470,7 @@ __global__ void __launch_bounds__(512)
       }
     } else {
       // ---- row peak, per-row scale, codes ----------------------------------
-      float peak = 0.0f;
-#pragma unroll
-      for (int i = 0; i < kChunk; ++i)
-        if (i < cnt) peak = fmaxf(peak, fabsf(v[i]));
-      peak = cta_max(peak, red, W);
+      const float peak = cta_max(chunk_absmax(v, cnt), red, W);
       const float qmax = (OUT == OUT_E4M3) ? 448.0f : 127.0f;
       const float scale = (peak == 0.0f) ? 1.0f : __fdiv_rn(peak, qmax);
       const float rinv = __frcp_rn(scale);
@@ -429,26 +478,48 @@ __global__ void __launch_bounds__(512)
       if (tid == 0) a.s[row] = scale;
       uint8_t* qrow = reinterpret_cast<uint8_t*>(a.q) + row * K;
       if (fullchunk && vec && (K % 16) == 0) {
+        if constexpr (OUT == OUT_E4M3) {
 #pragma unroll
-        for (int i = 0; i < kChunk; i += 16) {
-          uint32_t w[4];
+          for (int w0 = 0; w0 < kChunk / 4; w0 += 4) {
+            uint32_t words[4];
 #pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            uint32_t b0, b1, b2, b3;
-            if constexpr (OUT == OUT_E4M3) {
-              b0 = quant_e4m3(v[i + 4 * p + 0], scale, rinv, fast);
-              b1 = quant_e4m3(v[i + 4 * p + 1], scale, rinv, fast);
-              b2 = quant_e4m3(v[i + 4 * p + 2], scale, rinv, fast);
-              b3 = quant_e4m3(v[i + 4 * p + 3], scale, rinv, fast);
-            } else {
-              b0 = quant_i8(v[i + 4 * p + 0], scale, rinv, fast) & 0xFF;
-              b1 = quant_i8(v[i + 4 * p + 1], scale, rinv, fast) & 0xFF;
-              b2 = quant_i8(v[i + 4 * p + 2], scale, rinv, fast) & 0xFF;
-              b3 = quant_i8(v[i + 4 * p + 3], scale, rinv, fast) & 0xFF;
+            for (int w = 0; w < 4; ++w) {
+              const float* p = v + 4 * (w0 + w);
+              words[w] = quant_e4m3(p[0], scale, rinv, fast) |
+                         (quant_e4m3(p[1], scale, rinv, fast) << 8) |
+                         (quant_e4m3(p[2], scale, rinv, fast) << 16) |
+                         (quant_e4m3(p[3], scale, rinv, fast) << 24);
             }
-            w[p] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+            *reinterpret_cast<uint4*>(qrow + j0 + 4 * w0) =
+                make_uint4(words[0], words[1], words[2], words[3]);
           }
-          *reinterpret_cast<uint4*>(qrow + j0 + i) = make_uint4(w[0], w[1], w[2], w[3]);
+        } else {
+          bool redo = !fast;
+#pragma unroll
+          for (int w0 = 0; w0 < kChunk / 4; w0 += 4) {
+            uint32_t words[4];
+            redo |= quant_i8_fast<16>(v + 4 * w0, rinv, words);
+            *reinterpret_cast<uint4*>(qrow + j0 + 4 * w0) =
+                make_uint4(words[0], words[1], words[2], words[3]);
+          }
+          if (redo) {
+            // rare: some product sits within 2^-14 of a half-integer; the
+            // exact codes overwrite the chunk just written by this thread
+#pragma unroll
+            for (int w0 = 0; w0 < kChunk / 4; w0 += 4) {
+              uint32_t words[4];
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                const float* p = v + 4 * (w0 + w);
+                words[w] = (quant_i8(p[0], scale, rinv, fast) & 0xFF) |
+                           ((quant_i8(p[1], scale, rinv, fast) & 0xFF) << 8) |
+                           ((quant_i8(p[2], scale, rinv, fast) & 0xFF) << 16) |
+                           ((quant_i8(p[3], scale, rinv, fast) & 0xFF) << 24);
+              }
+              *reinterpret_cast<uint4*>(qrow + j0 + 4 * w0) =
+                  make_uint4(words[0], words[1], words[2], words[3]);
+            }
+          }
         }
       } else {
 #pragma unroll

@@ -23,7 +23,8 @@
  * one-code difference.  This restatement instead fixes the FP32 order so it is
  * bit-comparable with the CUDA kernels:
  *   - row reductions: thread t of the row owns the contiguous 64-element chunk
- *     [64 t, 64 t + 64) and sums it sequentially; the 32 lanes of a warp
+ *     [64 t, 64 t + 64); eight accumulators a[e] take elements e, e+8, ...,
+ *     e+56 in order and combine ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)); the 32 lanes of a warp
  *     combine with a xor butterfly of increasing offset (1, 2, 4, 8, 16), i.e.
  *     a pairwise tree over chunk index; the W = ceil(K / 2048) warp partials
  *     (padded with zeros to 16) combine pairwise (w0+w1, w2+w3, ...);
@@ -154,20 +155,23 @@ static float row_reduce(const float* v, int64_t K, int W, int kind, float mean) 
     float lane_acc[32];
     for (int l = 0; l < 32; ++l) {
       const int64_t j0 = ((int64_t)w * 32 + l) * CHUNK;
-      float acc = 0.0f;
-      for (int i = 0; i < CHUNK; ++i) {
-        const int64_t j = j0 + i;
-        if (j >= K) break;
-        const float x = v[j];
-        if (kind == 0) {
-          acc = acc + x;
-        } else if (kind == 1) {
-          acc = fmaf(x, x, acc);
-        } else {
-          const float d = x - mean;
-          acc = fmaf(d, d, acc);
+      float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int i = 0; i < CHUNK; i += 8) {
+        for (int e = 0; e < 8; ++e) {
+          const int64_t j = j0 + i + e;
+          if (j >= K) continue;
+          const float x = v[j];
+          if (kind == 0) {
+            a[e] = a[e] + x;
+          } else if (kind == 1) {
+            a[e] = fmaf(x, x, a[e]);
+          } else {
+            const float d = x - mean;
+            a[e] = fmaf(d, d, a[e]);
+          }
         }
       }
+      const float acc = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
       lane_acc[l] = acc;
     }
     for (int off = 1; off < 32; off <<= 1) {

@@ -42,7 +42,8 @@ def ops():
 @pytest.mark.parametrize("mode", ["int8", "fp8"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("kind", ["normal", "zeros", "outliers", "rowzero"])
-@pytest.mark.parametrize("shape", [(7, 256), (3, 257), (1, 33), (9, 5376), (4, 16384)])
+@pytest.mark.parametrize("shape", [(7, 256), (3, 257), (1, 33), (9, 5376), (4, 16384), (5, 5384),
+                                   (3, 200), (2, 32768), (300, 1024)])
 def test_quantize_matches_reference_bit_exact(ops, mode, dtype, kind, shape):
     x = _x(*shape, dtype, kind)
     q, s = ops.quantize(x.to(DEV), mode)
@@ -233,3 +234,49 @@ def test_contract_rejections(ops):
         ops.rotate(torch.ones(2, 16, device=DEV), 16, torch.ones(16, dtype=torch.int8, device=DEV))
     with pytest.raises(ValueError, match="signs"):
         ops.rotate(x, 32, signs.float())
+
+
+@pytest.mark.parametrize("mode", ["int8", "fp8"])
+def test_quantize_misaligned_base(ops, mode):
+    rows, k = 6, 4096
+    store = torch.randn(rows * k + 16).to(torch.bfloat16)
+    x = store[3:3 + rows * k].view(rows, k)  # contiguous, base not 16-byte aligned
+    xd = store.to(DEV)[3:3 + rows * k].view(rows, k)
+    q, s = ops.quantize(xd, mode)
+    rq, rs = ref.quantize_reference(x.float().numpy(), mode)
+    np.testing.assert_array_equal(q.cpu().numpy().view(np.uint8), rq.view(np.uint8))
+    np.testing.assert_array_equal(s.cpu().numpy(), rs)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("k", [5376, 16384, 32768])
+def test_gated_prep_wide_rows_and_padded_ring(ops, dtype, k):
+    m = 9
+    g = torch.Generator().manual_seed(k)
+    res = torch.randn(m, k, generator=g).to(dtype)
+    br = torch.randn(m, k, generator=g).to(dtype)
+    gate = (0.1 * torch.randn(k, generator=g)).to(torch.bfloat16)
+    gamma, scale, shift = _mod_params(k, torch.bfloat16)
+    signs = torch.from_numpy(ref.hadamard_signs(k, 3))
+    q, s, r2 = ops.fused_gated_residual_norm_hadamard_quantize(
+        res.to(DEV), br.to(DEV), gate.to(DEV), gamma.to(DEV), scale.to(DEV), shift.to(DEV),
+        signs.to(DEV), 256, norm="rms")
+    o = co.row_prep(res, block=256, norm="rms", eps=1e-5, round_output=True, gamma=gamma,
+                    scale=scale, shift=shift, signs=signs, branch=br, gate=gate)
+    assert torch.equal(r2.cpu(), o["residual"])
+    assert torch.equal(q.cpu(), o["q"]) and torch.equal(s.cpu(), o["s"])
+
+
+@pytest.mark.parametrize("block", [64, 1024])
+def test_many_rows_persistent_ring(ops, block):
+    """More rows than resident CTAs: every ring slot is reused many times."""
+    m, k = 3000, 2048
+    x = _x(m, k, torch.bfloat16, "outliers", seed=77)
+    signs = torch.from_numpy(ref.hadamard_signs(k, 21))
+    gamma, scale, shift = _mod_params(k, torch.bfloat16, table=3)
+    rm = (torch.arange(m, dtype=torch.int32) * 7) % 3
+    q, s = ops.fused_norm_hadamard_quantize(x.to(DEV), gamma.to(DEV), scale.to(DEV), shift.to(DEV),
+                                            signs.to(DEV), block, norm="layer", row_map=rm.to(DEV))
+    o = co.row_prep(x, block=block, norm="layer", eps=1e-5, round_output=True, gamma=gamma,
+                    scale=scale, shift=shift, row_map=rm, signs=signs)
+    assert torch.equal(q.cpu(), o["q"]) and torch.equal(s.cpu(), o["s"])
