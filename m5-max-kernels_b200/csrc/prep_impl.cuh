@@ -292,9 +292,14 @@ __global__ void __launch_bounds__(512)
     const T* xg = reinterpret_cast<const T*>(a.x) + row * K;  // ... or the row in HBM
     const T* bg = gated ? reinterpret_cast<const T*>(a.branch) + row * K : nullptr;
     if (stages > 0) {
+      // One thread waits (bounded); the barrier then releases the CTA and a
+      // single non-blocking probe gives every thread the acquire on the data.
       const uint32_t parity = static_cast<uint32_t>((it / stages) & 1);
-      if (!mbar_wait_bounded(&full_bar[s], parity, &abort_flag, a.status, DEV_TIMEOUT_PRODUCER))
-        break;
+      if (tid == 0)
+        mbar_wait_bounded(&full_bar[s], parity, &abort_flag, a.status, DEV_TIMEOUT_PRODUCER);
+      __syncthreads();
+      if (abort_flag) break;
+      (void)mbar_try_wait(&full_bar[s], parity);
       xs = dsmem + int64_t(s) * inputs * buf_stride;
       if (gated) bs = xs + buf_stride;
     }
@@ -494,20 +499,12 @@ __global__ void __launch_bounds__(512)
                 make_uint4(words[0], words[1], words[2], words[3]);
           }
         } else {
-          bool redo = !fast;
 #pragma unroll
           for (int w0 = 0; w0 < kChunk / 4; w0 += 4) {
             uint32_t words[4];
-            redo |= quant_i8_fast<16>(v + 4 * w0, rinv, words);
-            *reinterpret_cast<uint4*>(qrow + j0 + 4 * w0) =
-                make_uint4(words[0], words[1], words[2], words[3]);
-          }
-          if (redo) {
-            // rare: some product sits within 2^-14 of a half-integer; the
-            // exact codes overwrite the chunk just written by this thread
-#pragma unroll
-            for (int w0 = 0; w0 < kChunk / 4; w0 += 4) {
-              uint32_t words[4];
+            const bool redo = quant_i8_fast<16>(v + 4 * w0, rinv, words) || !fast;
+            if (redo) {
+              // rare: a product within 2^-14 of a half-integer; divide exactly
 #pragma unroll
               for (int w = 0; w < 4; ++w) {
                 const float* p = v + 4 * (w0 + w);
@@ -516,9 +513,9 @@ __global__ void __launch_bounds__(512)
                            ((quant_i8(p[2], scale, rinv, fast) & 0xFF) << 16) |
                            ((quant_i8(p[3], scale, rinv, fast) & 0xFF) << 24);
               }
-              *reinterpret_cast<uint4*>(qrow + j0 + 4 * w0) =
-                  make_uint4(words[0], words[1], words[2], words[3]);
             }
+            *reinterpret_cast<uint4*>(qrow + j0 + 4 * w0) =
+                make_uint4(words[0], words[1], words[2], words[3]);
           }
         }
       } else {

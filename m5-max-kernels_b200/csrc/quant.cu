@@ -1,0 +1,211 @@
+// Per-token symmetric quantization of plain rows (no normalization, no
+// rotation): the online activation quantization of the W8A8 / FP8 GEMM.
+//
+// Reference contract: src/m5kernels/metal.py:106-123 (quantize) with the
+// arithmetic of src/m5kernels/numerics.py:29-46 (quantize_reference):
+//   scale = peak / 127 (int8) or peak / 448 (E4M3), 1 for an all-zero row;
+//   code  = clip(rint(x / scale), +-127) or E4M3_RNE_saturating(x / scale).
+//
+// Two passes per row, no register-resident row: pass 1 streams the row from
+// HBM and reduces max |x| (on packed bf16 / fp16 pairs where possible); pass 2
+// streams it again - from L2, which still holds the row the CTA just read -
+// and writes the codes.  Each thread keeps only one 16-byte vector per
+// in-flight load, so eight 256-thread CTAs fit per SM and the loads of all of
+// them overlap.  Loads are 16 bytes per lane, 512 contiguous bytes per warp
+// instruction; codes are stored 8 bytes per lane.  HBM traffic per row:
+// K * sizeof(T) read, K written, 4 for the scale.
+#include "common.cuh"
+#include "m5b_internal.h"
+
+namespace m5b {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: RNE to integer for |t| < 2^22
+
+template <typename T>
+__device__ __forceinline__ float vec_absmax(const uint4& raw) {
+  if constexpr (sizeof(T) == 2) {
+    // |x| of a 16-bit float is its bit pattern with the sign cleared, and for
+    // finite values that pattern orders like the value: integer max suffices.
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&raw);
+    uint32_t m = __vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu);
+    m = __vmaxu2(m, __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
+    const uint32_t hi = m >> 16, lo = m & 0xFFFFu;
+    const uint16_t best = static_cast<uint16_t>(hi > lo ? hi : lo);
+    return to_f32(*reinterpret_cast<const T*>(&best));
+  } else {
+    const float* f = reinterpret_cast<const float*>(&raw);
+    return fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
+  }
+}
+
+// Elements per 16-byte vector.
+template <typename T>
+constexpr int kVec = 16 / sizeof(T);
+
+template <typename T>
+__device__ __forceinline__ void unpack(const uint4& raw, float* out) {
+  if constexpr (sizeof(T) == 2) {
+    const T* h = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) out[e] = to_f32(h[e]);
+  } else {
+    const float* f = reinterpret_cast<const float*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) out[e] = f[e];
+  }
+}
+
+// INT8 codes of n values packed into n/4 words; sets *near when any product
+// lies within 2^-14 of a half-integer (then the exact quotient decides).
+template <int N>
+__device__ __forceinline__ void pack_i8(const float* v, float inv, uint32_t* words, bool* near) {
+#pragma unroll
+  for (int w = 0; w < N / 4; ++w) {
+    uint32_t u[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float t = __fmul_rn(v[4 * w + e], inv);
+      const float m = __fadd_rn(t, kMagic);
+      *near |= fabsf(__fsub_rn(t, __fsub_rn(m, kMagic))) > 0.5f - 0x1p-14f;
+      u[e] = __float_as_uint(m);
+    }
+    words[w] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040),
+                           0x5410);
+  }
+}
+
+__device__ __forceinline__ uint32_t code_i8_exact(float v, float scale) {
+  float r = rintf(__fdiv_rn(v, scale));
+  r = fminf(fmaxf(r, -127.0f), 127.0f);
+  return static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu;
+}
+
+__device__ __forceinline__ uint32_t code_e4m3(float v, float scale, float inv, bool fast) {
+  if (fast) {
+    const float t = __fmul_rn(v, inv);
+    const __nv_fp8x2_storage_t two = __nv_cvt_float2_to_fp8x2(
+        make_float2(__fmul_rn(t, 1.0f - 0x1p-18f), __fmul_rn(t, 1.0f + 0x1p-18f)), __NV_SATFINITE,
+        __NV_E4M3);
+    if ((two & 0xFFu) == (two >> 8)) return two & 0xFFu;
+  }
+  return static_cast<uint32_t>(
+      __nv_cvt_float_to_fp8(__fdiv_rn(v, scale), __NV_SATFINITE, __NV_E4M3));
+}
+
+template <typename T, int OUT>
+__global__ void __launch_bounds__(kThreads)
+    quant_rows_kernel(const T* __restrict__ x, int64_t rows, int64_t K, uint8_t* __restrict__ q,
+                      float* __restrict__ s) {
+  constexpr int V = kVec<T>;
+  __shared__ float red[kThreads / 32];
+  const int tid = threadIdx.x;
+  const int64_t nvec = K / V;  // K % V == 0 on this path
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
+    // ---- pass 1: peak -----------------------------------------------------
+    float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f, p3 = 0.0f;
+    int64_t i = tid;
+    for (; i + 3 * kThreads < nvec; i += 4 * kThreads) {
+      const uint4 a = __ldg(xr + i), b = __ldg(xr + i + kThreads);
+      const uint4 c = __ldg(xr + i + 2 * kThreads), d = __ldg(xr + i + 3 * kThreads);
+      p0 = fmaxf(p0, vec_absmax<T>(a));
+      p1 = fmaxf(p1, vec_absmax<T>(b));
+      p2 = fmaxf(p2, vec_absmax<T>(c));
+      p3 = fmaxf(p3, vec_absmax<T>(d));
+    }
+    for (; i < nvec; i += kThreads) p0 = fmaxf(p0, vec_absmax<T>(__ldg(xr + i)));
+    float peak = fmaxf(fmaxf(p0, p1), fmaxf(p2, p3));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, off));
+    if ((tid & 31) == 0) red[tid >> 5] = peak;
+    __syncthreads();
+    peak = red[0];
+#pragma unroll
+    for (int w = 1; w < kThreads / 32; ++w) peak = fmaxf(peak, red[w]);
+    __syncthreads();
+    const float qmax = OUT == OUT_E4M3 ? 448.0f : 127.0f;
+    const float scale = peak == 0.0f ? 1.0f : __fdiv_rn(peak, qmax);
+    const float inv = __frcp_rn(scale);
+    const bool fast = scale >= 0x1p-100f;
+    if (tid == 0) s[row] = scale;
+    // ---- pass 2: codes ----------------------------------------------------
+    uint8_t* qr = q + row * K;
+    for (int64_t j = tid; j < nvec; j += kThreads) {
+      float v[V];
+      unpack<T>(__ldg(xr + j), v);
+      uint32_t words[V / 4];
+      if constexpr (OUT == OUT_E4M3) {
+#pragma unroll
+        for (int w = 0; w < V / 4; ++w)
+          words[w] = code_e4m3(v[4 * w], scale, inv, fast) |
+                     (code_e4m3(v[4 * w + 1], scale, inv, fast) << 8) |
+                     (code_e4m3(v[4 * w + 2], scale, inv, fast) << 16) |
+                     (code_e4m3(v[4 * w + 3], scale, inv, fast) << 24);
+      } else {
+        bool near = !fast;
+        pack_i8<V>(v, inv, words, &near);
+        if (near) {
+#pragma unroll
+          for (int w = 0; w < V / 4; ++w)
+            words[w] = code_i8_exact(v[4 * w], scale) | (code_i8_exact(v[4 * w + 1], scale) << 8) |
+                       (code_i8_exact(v[4 * w + 2], scale) << 16) |
+                       (code_i8_exact(v[4 * w + 3], scale) << 24);
+        }
+      }
+      if constexpr (V == 8)
+        *reinterpret_cast<uint2*>(qr + j * 8) = make_uint2(words[0], words[1]);
+      else
+        *reinterpret_cast<uint32_t*>(qr + j * 4) = words[0];
+    }
+  }
+}
+
+template <typename T, int OUT>
+cudaError_t launch_quant_t(const RowPrepArgs& a, cudaStream_t stream) {
+  auto kern = quant_rows_kernel<T, OUT>;
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0);
+  if (e != cudaSuccess) return e;
+  int64_t grid = int64_t(sms) * (per_sm > 0 ? per_sm : 1);
+  if (grid > a.rows) grid = a.rows;
+  kern<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
+      reinterpret_cast<const T*>(a.x), a.rows, a.K, reinterpret_cast<uint8_t*>(a.q), a.s);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// True when the lean kernel applies: plain quantization of aligned rows whose
+// width is a whole number of 16-byte vectors and whose codes can be stored
+// 8 (fp32: 4) bytes at a time.
+bool quant_rows_applicable(const RowPrepArgs& a, int x_dtype, int block, int out) {
+  if (block != 0 || a.norm != NORM_NONE || a.branch || a.signs || out == OUT_F32) return false;
+  const int vec = x_dtype == DT_F32 ? 4 : 8;
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(a.x), qa = reinterpret_cast<uintptr_t>(a.q);
+  return (a.K % vec) == 0 && (xa % 16) == 0 && (qa % vec) == 0;
+}
+
+cudaError_t launch_quant_rows(const RowPrepArgs& a, int x_dtype, int out, cudaStream_t stream) {
+  const bool e4 = out == OUT_E4M3;
+  switch (x_dtype) {
+    case DT_BF16:
+      return e4 ? launch_quant_t<__nv_bfloat16, OUT_E4M3>(a, stream)
+                : launch_quant_t<__nv_bfloat16, OUT_INT8>(a, stream);
+    case DT_F16:
+      return e4 ? launch_quant_t<__half, OUT_E4M3>(a, stream)
+                : launch_quant_t<__half, OUT_INT8>(a, stream);
+    case DT_F32:
+      return e4 ? launch_quant_t<float, OUT_E4M3>(a, stream)
+                : launch_quant_t<float, OUT_INT8>(a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace m5b

@@ -1,0 +1,116 @@
+"""m5bench-style command line for the cuda-b200 backends.
+
+    python -m m5kernels_b200.cli doctor
+    python -m m5kernels_b200.cli shapes [--suite baseline]
+    python -m m5kernels_b200.cli bench --suite baseline --backends cuda-b200 \\
+        --precisions int8 [--cases id,...] [--seed 17] [--distribution normal] \\
+        [--warmup 3] [--repeat 10] [--out results/run.json]
+    python -m m5kernels_b200.cli report results/run.json
+
+Mirrors the reference CLI (src/m5kernels/cli.py:188-245): suites are
+workload manifests (schema v1), every (case, precision, backend) goes
+through engine.run_case, and results are written with exclusive create.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+from . import engine, workloads
+
+
+def _doctor(_args) -> int:
+    import torch
+
+    from . import _lib
+
+    info = engine.environment()
+    try:
+        _lib.lib()
+        info["library_loaded"] = True
+    except _lib.ExtensionMissing as e:
+        info["library_loaded"] = False
+        info["library_error"] = str(e)
+    info["cuda_available"] = torch.cuda.is_available()
+    print(json.dumps(info, indent=2))
+    return 0 if info["library_loaded"] and info["cuda_available"] else 1
+
+
+def _shapes(args) -> int:
+    data = workloads.load(args.suite)
+    for c in data["cases"]:
+        extra = {k: v for k, v in c.items() if k not in ("id", "op", "m", "n", "k")}
+        print(f"{c['id']:32s} {c['op']:26s} m={c['m']:<6d} n={c['n']:<6d} k={c['k']:<6d} {extra}")
+    return 0
+
+
+def _bench(args) -> int:
+    data = workloads.load(args.suite)
+    cases = data["cases"]
+    if args.cases:
+        wanted = set(args.cases.split(","))
+        cases = [c for c in cases if c["id"] in wanted]
+    results = []
+    for c in cases:
+        for precision in args.precisions.split(","):
+            for backend in args.backends.split(","):
+                if backend == "auto":  # the first cuda-b200 backend of the case's op
+                    backend = engine.BACKENDS.get(c["op"], ("cuda-b200",))[0]
+                    if c["op"] == "gemm" and "hadamard" in c:
+                        backend = "cuda-b200-hadamard"
+                r = engine.run_case(c, backend, precision, seed=args.seed,
+                                    distribution=args.distribution, warmup=args.warmup,
+                                    repeat=args.repeat)
+                results.append(r)
+                line = f"{c['id']:30s} {backend:26s} {precision:5s} {r['status']:11s}"
+                if r["status"] == "ok":
+                    line += (f" {r['timing']['median_ms']:.4f} ms  {r['effective_tops']:.1f} TOPS"
+                             f"  online {r['stages']['online_activation_plus_gemm']['median_ms']:.4f} ms")
+                else:
+                    line += f" {r.get('reason', '')[:80]}"
+                print(line, flush=True)
+    document = {"schema_version": 1, "environment": engine.environment(), "suite": args.suite,
+                "results": results}
+    if args.out:
+        engine.write_result(args.out, document)
+    bad = [r for r in results if r["status"] in ("incorrect", "error")]
+    return 1 if bad else 0
+
+
+def _report(args) -> int:
+    doc = json.loads(open(args.path).read())
+    for r in doc["results"]:
+        t = r.get("timing", {}).get("median_ms")
+        print(f"{r['case']['id']:30s} {r['backend']:26s} {r['precision']:5s} {r['status']:11s} "
+              f"{'' if t is None else f'{t:.4f} ms'}")
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(prog="m5bench-b200")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    sub.add_parser("doctor")
+    p = sub.add_parser("shapes")
+    p.add_argument("--suite", default="baseline")
+    p = sub.add_parser("bench")
+    p.add_argument("--suite", default="baseline")
+    p.add_argument("--cases", default="")
+    p.add_argument("--backends", default="auto")
+    p.add_argument("--precisions", default="int8")
+    p.add_argument("--seed", type=int, default=17)
+    p.add_argument("--distribution", default="normal", choices=["normal", "outliers", "zeros"])
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--repeat", type=int, default=10)
+    p.add_argument("--out", default="")
+    p = sub.add_parser("report")
+    p.add_argument("path")
+    args = ap.parse_args(argv)
+    if getattr(args, "warmup", 1) < 0 or getattr(args, "repeat", 1) < 1:
+        ap.error("warmup must be >= 0 and repeat >= 1")
+    return {"doctor": _doctor, "shapes": _shapes, "bench": _bench, "report": _report}[args.cmd](args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
