@@ -353,9 +353,9 @@ int m5b_fused_gated_residual_norm_hadamard_quantize(
 // one full pair tile of rows and more than 128 output columns.
 static bool use_pair(int epi, int64_t m, int64_t n) { return epi != EPI_QK && m >= 256 && n > 128; }
 
-static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, const void* a,
-                       const void* b, int64_t m, int64_t n, int64_t k, int mode, int bn,
-                       bool pair) {
+static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMap& tbh,
+                       const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
+                       int bn, bool pair) {
   if (m <= 0 || n <= 0 || k <= 0) return fail(M5B_EINVAL, "A and B must be nonempty matrices");
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL)
     return fail(M5B_EUNSUPPORTED, "matrix dimensions exceed 2^31-1");
@@ -384,6 +384,11 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, const void
   if (rc) return rc;
   rc = make_kmajor_map(&tb, b, n, k, eb, pair ? bn / 2 : bn);
   if (rc) return rc;
+  tbh = tb;
+  if (pair) {  // half-height B boxes for split tail tiles
+    rc = make_kmajor_map(&tbh, b, n, k, eb, bn / 4);
+    if (rc) return rc;
+  }
   g.M = static_cast<int>(m);
   g.N = static_cast<int>(n);
   g.K = static_cast<int>(k);
@@ -397,17 +402,24 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, const void
   return M5B_OK;
 }
 
-static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, int bn,
-                       bool pair, void* stream) {
+static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
+                       GemmArgs& g, int bn, bool pair, void* stream) {
   unsigned int* status = nullptr;
   int sms = 0;
   int rc = device_state(&status, &sms);
   if (rc) return rc;
   g.status = status;
   const int tiles = g.num_m_blocks * g.num_n_blocks;
-  const int units = pair ? sms / 2 : sms;  // persistent CTAs (pairs)
-  const int grid = (tiles < units ? tiles : units) * (pair ? 2 : 1);
-  cudaError_t e = launch_gemm(ta, tb, g, bn, grid, pair, static_cast<cudaStream_t>(stream));
+  const int slots = pair ? sms / 2 : sms;  // persistent CTAs (pairs)
+  g.num_full = tiles;
+  g.num_units = tiles;
+  const int rem = tiles % slots;
+  if (pair && tiles > slots && rem > 0 && 2 * rem <= slots) {
+    g.num_full = tiles - rem;
+    g.num_units = g.num_full + 2 * rem;
+  }
+  const int grid = (g.num_units < slots ? g.num_units : slots) * (pair ? 2 : 1);
+  cudaError_t e = launch_gemm(ta, tb, tbh, g, bn, grid, pair, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
   return ok();
 }
@@ -422,8 +434,8 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
   g.N = static_cast<int>(n);
   const int bn = gemm_block_n(g);
   const bool pair = use_pair(EPI_PLAIN, m, n);
-  CUtensorMap ta, tb;
-  int rc = gemm_common(g, ta, tb, a, b, m, n, k, mode, bn, pair);
+  CUtensorMap ta, tb, tbh;
+  int rc = gemm_common(g, ta, tb, tbh, a, b, m, n, k, mode, bn, pair);
   if (rc) return rc;
   if (out_dtype == M5B_I32) {
     // Raw INT32 accumulators: INT8 operands, no scales and no epilogue.
@@ -434,7 +446,7 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
     if (!out) return fail(M5B_EINVAL, "output pointer is NULL");
     g.out = out;
     g.out_dtype = DT_I32;
-    return gemm_launch(ta, tb, g, bn, pair, stream);
+    return gemm_launch(ta, tb, tbh, g, bn, pair, stream);
   }
   const bool quant = (mode == M5B_MODE_INT8 || mode == M5B_MODE_FP8);
   if (quant && (!a_scales || !b_scales)) return fail(M5B_EINVAL, "scales required");
@@ -473,7 +485,7 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
     g.bias = bias;
     g.bias_row_map = bias_row_map;
   }
-  return gemm_launch(ta, tb, g, bn, pair, stream);
+  return gemm_launch(ta, tb, tbh, g, bn, pair, stream);
 }
 
 int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
@@ -499,8 +511,8 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
   if (!aligned(out, 16)) return fail(M5B_EINVAL, "output base address must be 16-byte aligned");
   GemmArgs g{};
   g.epi = EPI_QK;
-  CUtensorMap ta, tb;
-  int rc = gemm_common(g, ta, tb, a, b, m, n, k, mode, 128, false);
+  CUtensorMap ta, tb, tbh;
+  int rc = gemm_common(g, ta, tb, tbh, a, b, m, n, k, mode, 128, false);
   if (rc) return rc;
   g.quantized = quant ? 1 : 0;
   g.a_scales = a_scales;
@@ -512,7 +524,7 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
   g.sin = sin;
   g.rope_half = rope_half;
   g.eps = epsilon;
-  return gemm_launch(ta, tb, g, 128, false, stream);
+  return gemm_launch(ta, tb, tbh, g, 128, false, stream);
 }
 
 }  // extern "C"

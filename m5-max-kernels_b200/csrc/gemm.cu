@@ -26,7 +26,10 @@
 // rows of B (plain TMA loads, transaction bytes counted on the even CTA's
 // barrier); the even CTA's MMA warp issues M=256 MMAs that read both CTAs'
 // shared memory and write 128 accumulator rows into each CTA's TMEM.  Per SM
-// this halves the B traffic into shared memory, so a 6-deep ring fits.
+// this halves the B traffic into shared memory, so a 6-deep ring fits.  When
+// the last wave of 256 x BN tiles would leave more than half of the pairs
+// idle, those tiles run as two 256 x BN/2 halves (second B descriptor with
+// half-height boxes, N = BN/2 instruction descriptor).
 //
 // Rounding contract (bit-reproducible, mirrored by the C oracle):
 //   quantized:  v = fp32(acc) * sa[m] * sb[n]   (int32 -> fp32 RNE, then two
@@ -183,11 +186,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
 template <int KIND, int BN, bool QK, bool PAIR>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                   const __grid_constant__ CUtensorMap tmap_b, const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tmap_b,
+                   const __grid_constant__ CUtensorMap tmap_b_half, const GemmArgs g) {
   using Cfg = GemmCfg<BN, QK, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int K_ELEMS = (KIND == KIND_BF16 || KIND == KIND_F16) ? 64 : 128;
   constexpr uint32_t IDESC = make_idesc(KIND, Cfg::TILE_M, BN);
+  constexpr uint32_t IDESC_HALF = make_idesc(KIND, Cfg::TILE_M, BN / 2);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -227,6 +232,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (g.num_units > g.num_full) tma_prefetch_desc(&tmap_b_half);
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -243,8 +249,22 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_tiles = g.num_m_blocks * g.num_n_blocks;
+  const int num_units_total = g.num_units;
   const int nkb = g.num_k_blocks;
+  // Unit -> (tile, N offset within the tile, width): whole tiles first, then halves.
+  auto unit_tile = [&](int u, int& m_blk, int& n_col, bool& whole) {
+    int n_blk;
+    if (u < g.num_full) {
+      tile_coords(u, g, m_blk, n_blk);
+      n_col = n_blk * BN;
+      whole = true;
+    } else {
+      const int h = u - g.num_full;
+      tile_coords(g.num_full + (h >> 1), g, m_blk, n_blk);
+      n_col = n_blk * BN + (h & 1) * (BN / 2);
+      whole = false;
+    }
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -252,26 +272,30 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int t = unit; t < num_tiles && !*abort_flag; t += units) {
-        int m_blk, n_blk;
-        tile_coords(t, g, m_blk, n_blk);
+      for (int t = unit; t < num_units_total && !*abort_flag; t += units) {
+        int m_blk, n_col;
+        bool whole;
+        unit_tile(t, m_blk, n_col, whole);
         const int a_row = m_blk * Cfg::TILE_M + static_cast<int>(rank) * kBM;
-        const int b_row = n_blk * BN + static_cast<int>(rank) * Cfg::B_ROWS;
+        const int b_rows = whole ? Cfg::B_ROWS : Cfg::B_ROWS / 2;
+        const int b_row = n_col + static_cast<int>(rank) * b_rows;
+        const CUtensorMap* bmap = whole ? &tmap_b : &tmap_b_half;
+        const uint32_t stage_bytes = Cfg::A_BYTES + b_rows * 128;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, g.status,
                                  DEV_TIMEOUT_PRODUCER))
             break;
           if constexpr (PAIR) {
             // The even CTA expects both CTAs' bytes; each CTA loads its halves.
-            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * stage_bytes);
             tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmap_a, &full[stage], kb * K_ELEMS,
                              a_row);
-            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmap_b, &full[stage], kb * K_ELEMS,
+            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, bmap, &full[stage], kb * K_ELEMS,
                              b_row);
           } else {
-            mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+            mbar_arrive_expect_tx(&full[stage], stage_bytes);
             tma_load_2d(sA + stage * Cfg::A_BYTES, &tmap_a, &full[stage], kb * K_ELEMS, a_row);
-            tma_load_2d(sB + stage * Cfg::B_BYTES, &tmap_b, &full[stage], kb * K_ELEMS, b_row);
+            tma_load_2d(sB + stage * Cfg::B_BYTES, bmap, &full[stage], kb * K_ELEMS, b_row);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -306,7 +330,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = unit; t < num_tiles && ok; t += units, ++local) {
+      for (int t = unit; t < num_units_total && ok; t += units, ++local) {
+        const uint32_t idesc = t < g.num_full ? IDESC : IDESC_HALF;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, abort_flag, g.status,
@@ -328,10 +353,10 @@ __global__ void __launch_bounds__(192, 1)
           for (int k = 0; k < 4; ++k) {
             if constexpr (PAIR)
               tc_mma_pair<KIND>(d_tmem, smem_desc_k128(a_base + k * 32),
-                                smem_desc_k128(b_base + k * 32), IDESC, (kb | k) != 0 ? 1u : 0u);
+                                smem_desc_k128(b_base + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
             else
               tc_mma<KIND>(d_tmem, smem_desc_k128(a_base + k * 32),
-                           smem_desc_k128(b_base + k * 32), IDESC, (kb | k) != 0 ? 1u : 0u);
+                           smem_desc_k128(b_base + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
           }
           if constexpr (PAIR)
             tc_commit_pair(&empty[stage]);
@@ -377,9 +402,11 @@ __global__ void __launch_bounds__(192, 1)
         mbar_arrive(&acc_empty[acc]);
     };
     int local = 0;
-    for (int t = unit; t < num_tiles; t += units, ++local) {
-      int m_blk, n_blk;
-      tile_coords(t, g, m_blk, n_blk);
+    for (int t = unit; t < num_units_total; t += units, ++local) {
+      int m_blk, n_col;
+      bool whole;
+      unit_tile(t, m_blk, n_col, whole);
+      const int n_blk = n_col / BN;  // Q/K tiles are always whole (one head)
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, g.status,
@@ -392,12 +419,13 @@ __global__ void __launch_bounds__(192, 1)
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const float sa = (g.quantized && row < g.M) ? __ldg(g.a_scales + row) : 1.0f;
       if constexpr (!QK) {
+        const int chunks = whole ? BN / 32 : BN / 64;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < chunks; ++c) {
           uint32_t r[32];
           tmem_ld32(taddr + c * 32, r);
           tmem_wait_ld();
-          epilogue_chunk<KIND>(g, r, row, n_blk * BN + c * 32, sa);
+          epilogue_chunk<KIND>(g, r, row, n_col + c * 32, sa);
         }
         tc_fence_before();
         __syncwarp();
@@ -485,8 +513,8 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 template <int KIND, int BN, bool QK, bool PAIR>
-static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
-                            int grid, cudaStream_t stream) {
+static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
+                            const GemmArgs& g, int grid, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, QK, PAIR>;
   auto kern = gemm_tc_kernel<KIND, BN, QK, PAIR>;
   cudaError_t e =
@@ -506,7 +534,7 @@ static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, g);
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tbh, g);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -516,15 +544,15 @@ int gemm_block_n(const GemmArgs& g) {
   return g.N <= 128 ? 128 : 256;
 }
 
-cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, int bn,
-                        int grid, bool pair, cudaStream_t stream) {
+cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
+                        const GemmArgs& g, int bn, int grid, bool pair, cudaStream_t stream) {
   const bool qk = g.epi == EPI_QK;
-#define M5B_KIND_CASE(KIND_)                                                          \
-  case KIND_:                                                                         \
-    if (qk) return launch_k<KIND_, 128, true, false>(ta, tb, g, grid, stream);        \
-    if (pair) return launch_k<KIND_, 256, false, true>(ta, tb, g, grid, stream);      \
-    if (bn == 128) return launch_k<KIND_, 128, false, false>(ta, tb, g, grid, stream); \
-    return launch_k<KIND_, 256, false, false>(ta, tb, g, grid, stream);
+#define M5B_KIND_CASE(KIND_)                                                               \
+  case KIND_:                                                                              \
+    if (qk) return launch_k<KIND_, 128, true, false>(ta, tb, tbh, g, grid, stream);        \
+    if (pair) return launch_k<KIND_, 256, false, true>(ta, tb, tbh, g, grid, stream);      \
+    if (bn == 128) return launch_k<KIND_, 128, false, false>(ta, tb, tbh, g, grid, stream); \
+    return launch_k<KIND_, 256, false, false>(ta, tb, tbh, g, grid, stream);
   switch (g.kind) {
     M5B_KIND_CASE(KIND_I8)
     M5B_KIND_CASE(KIND_F8)

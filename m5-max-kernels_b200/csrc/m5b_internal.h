@@ -83,11 +83,16 @@ struct GemmArgs {
   float eps;
   int num_m_blocks, num_n_blocks, num_k_blocks;
   int group_m;
+  // Work units: units [0, num_full) are whole tiles; when a CTA-pair launch's
+  // last wave would be at most half full, the remaining tiles are split into
+  // two N-halves each (units [num_full, num_units)), which evens out the wave.
+  int num_full;
+  int num_units;
   unsigned int* status;       // device status word (bounded-wait errors)
 };
 
-cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, int bn,
-                        int grid, bool pair, cudaStream_t stream);
+cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb_half,
+                        const GemmArgs& g, int bn, int grid, bool pair, cudaStream_t stream);
 int gemm_block_n(const GemmArgs& g);
 
 }  // namespace m5b

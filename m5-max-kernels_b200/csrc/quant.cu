@@ -14,6 +14,8 @@
 // them overlap.  Loads are 16 bytes per lane, 512 contiguous bytes per warp
 // instruction; codes are stored 8 bytes per lane.  HBM traffic per row:
 // K * sizeof(T) read, K written, 4 for the scale.
+#include <type_traits>
+
 #include "common.cuh"
 #include "m5b_internal.h"
 
@@ -58,23 +60,48 @@ __device__ __forceinline__ void unpack(const uint4& raw, float* out) {
   }
 }
 
-// INT8 codes of n values packed into n/4 words; sets *near when any product
-// lies within 2^-14 of a half-integer (then the exact quotient decides).
-template <int N>
-__device__ __forceinline__ void pack_i8(const float* v, float inv, uint32_t* words, bool* near) {
+// INT8 codes of one 16-byte vector (8 bf16/fp16 or 4 fp32 values) packed
+// into words, on sm_100 packed-FP32 arithmetic (each lane an IEEE binary32
+// op).  Per pair: t = x * inv, m = t + 1.5*2^23 (RNE to integer, code in the
+// low byte of m), r = m - 1.5*2^23, d = t - r (both exact).  Returns max |d|;
+// max |d| > 0.5 - 2^-14 flags a product near a half-integer.
+template <typename T>
+__device__ __forceinline__ float pack_i8_vec(const uint4& raw, float inv, uint32_t* words) {
+  const float2 inv2 = make_float2(inv, inv);
+  const float2 mag2 = make_float2(kMagic, kMagic);
+  const float2 nmag2 = make_float2(-kMagic, -kMagic);
+  const float2 neg1 = make_float2(-1.0f, -1.0f);
+  float dmax = 0.0f;
+  constexpr int PAIRS = sizeof(T) == 2 ? 4 : 2;
+  uint32_t u[2 * PAIRS];
 #pragma unroll
-  for (int w = 0; w < N / 4; ++w) {
-    uint32_t u[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float t = __fmul_rn(v[4 * w + e], inv);
-      const float m = __fadd_rn(t, kMagic);
-      *near |= fabsf(__fsub_rn(t, __fsub_rn(m, kMagic))) > 0.5f - 0x1p-14f;
-      u[e] = __float_as_uint(m);
+  for (int p = 0; p < PAIRS; ++p) {
+    float2 v;
+    if constexpr (sizeof(T) == 2) {
+      const uint32_t w = reinterpret_cast<const uint32_t*>(&raw)[p];
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        v = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+      } else {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w);
+        v = __half22float2(h);
+      }
+    } else {
+      v = make_float2(reinterpret_cast<const float*>(&raw)[2 * p],
+                      reinterpret_cast<const float*>(&raw)[2 * p + 1]);
     }
-    words[w] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040),
-                           0x5410);
+    const float2 t = __fmul2_rn(v, inv2);
+    const float2 m = __fadd2_rn(t, mag2);
+    const float2 r = __fadd2_rn(m, nmag2);
+    const float2 d = __ffma2_rn(r, neg1, t);
+    dmax = fmaxf(dmax, fmaxf(fabsf(d.x), fabsf(d.y)));
+    u[2 * p] = __float_as_uint(m.x);
+    u[2 * p + 1] = __float_as_uint(m.y);
   }
+#pragma unroll
+  for (int w = 0; w < PAIRS / 2; ++w)
+    words[w] = __byte_perm(__byte_perm(u[4 * w], u[4 * w + 1], 0x0040),
+                           __byte_perm(u[4 * w + 2], u[4 * w + 3], 0x0040), 0x5410);
+  return dmax;
 }
 
 __device__ __forceinline__ uint32_t code_i8_exact(float v, float scale) {
@@ -134,10 +161,11 @@ __global__ void __launch_bounds__(kThreads)
     // ---- pass 2: codes ----------------------------------------------------
     uint8_t* qr = q + row * K;
     for (int64_t j = tid; j < nvec; j += kThreads) {
+      const uint4 raw = __ldg(xr + j);
       float v[V];
-      unpack<T>(__ldg(xr + j), v);
       uint32_t words[V / 4];
       if constexpr (OUT == OUT_E4M3) {
+        unpack<T>(raw, v);
 #pragma unroll
         for (int w = 0; w < V / 4; ++w)
           words[w] = code_e4m3(v[4 * w], scale, inv, fast) |
@@ -145,9 +173,9 @@ __global__ void __launch_bounds__(kThreads)
                      (code_e4m3(v[4 * w + 2], scale, inv, fast) << 16) |
                      (code_e4m3(v[4 * w + 3], scale, inv, fast) << 24);
       } else {
-        bool near = !fast;
-        pack_i8<V>(v, inv, words, &near);
-        if (near) {
+        const float dmax = pack_i8_vec<T>(raw, inv, words);
+        if (!fast || dmax > 0.5f - 0x1p-14f) {
+          unpack<T>(raw, v);
 #pragma unroll
           for (int w = 0; w < V / 4; ++w)
             words[w] = code_i8_exact(v[4 * w], scale) | (code_i8_exact(v[4 * w + 1], scale) << 8) |

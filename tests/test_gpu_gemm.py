@@ -169,3 +169,18 @@ def test_gemm_contract_rejections(ops):
                  gate=torch.zeros(4, device=DEV, dtype=torch.bfloat16))
     with pytest.raises(ValueError, match="K mismatch"):
         ops.gemm(qa, qa[:, :32], "int8", a_scales=qsa, b_scales=qsa)
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096, 256), (4000, 4000, 384), (9914, 4096, 128),
+                                   (2304, 8448, 128)])
+def test_pair_split_tail_bit_exact(ops, shape):
+    """Shapes whose last wave of 256x256 CTA-pair tiles is split into halves."""
+    m, n, k = shape
+    a, b = _operands(m, n, k, seed=21)
+    aq, sa = _q(ops, a)
+    bq, sb = _q(ops, b)
+    acc = ops.gemm(aq, bq, "int8", output_dtype=torch.int32).cpu()
+    expect = co.gemm_i8_acc_fast(aq.cpu(), bq.cpu())
+    assert torch.equal(acc, expect)
+    y = ops.gemm(aq, bq, "int8", a_scales=sa, b_scales=sb, output_dtype=torch.bfloat16).cpu()
+    assert torch.equal(y, co.gemm_epilogue(expect, sa.cpu(), sb.cpu()))
