@@ -117,6 +117,19 @@ class ClockSampler:
                 "reasons": sorted(seen), "samples": len(self.samples)}
 
 
+def _profiled_traffic():
+    """DRAM bytes per GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum)
+    from the committed ncu summary of this workload, or None."""
+    import re
+
+    p = ROOT / "profiles" / "gemm_tc_i8_ffn_down_m4096.md"
+    try:
+        m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", p.read_text(), re.M)
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
 def _dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -221,43 +234,34 @@ def run_b200(args, world, rank, local):
     barrier()
 
     stream = torch.cuda.current_stream(dev)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
+    # Events around each kernel of every timed step: the per-kernel averages
+    # come from the same timed region as the headline number.
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+
+    def timed_step(i):
+        a, wq, ws = sets[i % SETS]
+        ev[i][0].record(stream)
+        q, s = m5.quantize(a, "int8")
+        ev[i][1].record(stream)
+        m5.gemm(q, wq, "int8", a_scales=s, b_scales=ws, output_dtype=torch.bfloat16)
+        ev[i][2].record(stream)
+
     with ClockSampler(local) as clocks:
         barrier()
         torch.cuda.synchronize()
-        t0.record(stream)
         for i in range(args.steps):
-            step(i)
-        t1.record(stream)
+            timed_step(i)
         torch.cuda.synchronize()
         barrier()
-    ms_total = t0.elapsed_time(t1)
+    ms_total = ev[0][0].elapsed_time(ev[-1][2])
+    prep_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    gemm_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
     ms = torch.tensor([ms_total / args.steps], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms_per_step = float(ms.item())
     ops_per_rank = 2.0 * M * N * K
     value = world * ops_per_rank / (ms_per_step * 1e-3) / 1e12
-
-    # Per-kernel device times (same stream, same rotation) for the roofline.
-    def time_kernel(fn, reps):
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        fn(0)
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for i in range(reps):
-            fn(i)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / reps
-
-    prepped = [m5.quantize(a, "int8") for a, _, _ in sets]
-    gemm_ms = time_kernel(lambda i: m5.gemm(prepped[i % SETS][0], sets[i % SETS][1], "int8",
-                                            a_scales=prepped[i % SETS][1], b_scales=sets[i % SETS][2],
-                                            output_dtype=torch.bfloat16), max(args.steps, 10))
-    prep_ms = time_kernel(lambda i: m5.quantize(sets[i % SETS][0], "int8"), max(args.steps, 10))
 
     if args.profile:
         if rank == 0:
@@ -301,14 +305,7 @@ def run_b200(args, world, rank, local):
     gemm_tops = ops_per_rank / (gemm_ms * 1e-3) / 1e12
     prep_bytes = M * (3 * K + 4)
     prep_gbs = prep_bytes / (prep_ms * 1e-3) / 1e9
-    traffic = None
-    tfile = ROOT / "profiles" / "roofline_traffic.json"
-    if tfile.exists():
-        try:
-            traffic = json.loads(tfile.read_text()).get("gemm_dram_bytes_per_launch")
-        except Exception:
-            traffic = None
-
+    traffic = _profiled_traffic()
     out = None
     if rank == 0:
         cb = cpu_reference(1, 0, target_s=10.0) if world == 1 else None
@@ -323,9 +320,9 @@ def run_b200(args, world, rank, local):
                        "l2": f"inputs larger than L2; {SETS} rotating operand sets"},
             "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
                          "unit": "TFLOP/s", "frac": gemm_tops / int8_peak, "traffic": traffic,
-                         "kernel": "gemm_tc_kernel<i8>",
+                         "kernel": "gemm_tc_kernel<i8,256,pair>",
                          "peak_source": f"2 x {peaks['source']} dense bf16 ({peaks['bf16']} TF/s)"},
-            "prep": {"kernel": "row_prep_kernel<bf16,0,int8>", "ms": prep_ms,
+            "prep": {"kernel": "quant_rows_kernel<bf16,int8,VPT=8>", "ms": prep_ms,
                      "achieved_gbs": prep_gbs, "peak_gbs": peaks["hbm_gbs"],
                      "frac": prep_gbs / peaks["hbm_gbs"], "bytes": prep_bytes},
             "gemm_ms": gemm_ms,

@@ -9,6 +9,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -398,7 +399,16 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMa
   g.num_m_blocks = static_cast<int>((m + tile_m - 1) / tile_m);
   g.num_n_blocks = static_cast<int>((n + bn - 1) / bn);
   g.num_k_blocks = static_cast<int>((k + k_elems - 1) / k_elems);
-  g.group_m = 8;
+  // Grouped-M raster: consecutive tiles walk the M-blocks of a group before
+  // the next N-block, so a group's A rows are re-read from L2 while B streams.
+  // A group's A footprint is capped near 48 MB (a little over a third of L2).
+  // M5B_GEMM_GROUP_M overrides the choice (tuning experiments).
+  const int64_t a_block_bytes = int64_t(tile_m) * k * eb;
+  int64_t group = (48ll << 20) / (a_block_bytes > 0 ? a_block_bytes : 1);
+  if (const char* env = std::getenv("M5B_GEMM_GROUP_M")) group = std::atoi(env);
+  if (group < 1) group = 1;
+  if (group > g.num_m_blocks) group = g.num_m_blocks;
+  g.group_m = static_cast<int>(group);
   return M5B_OK;
 }
 

@@ -6,13 +6,13 @@
 //   scale = peak / 127 (int8) or peak / 448 (E4M3), 1 for an all-zero row;
 //   code  = clip(rint(x / scale), +-127) or E4M3_RNE_saturating(x / scale).
 //
-// Two passes per row, no register-resident row: pass 1 streams the row from
-// HBM and reduces max |x| (on packed bf16 / fp16 pairs where possible); pass 2
-// streams it again - from L2, which still holds the row the CTA just read -
-// and writes the codes.  Each thread keeps only one 16-byte vector per
-// in-flight load, so eight 256-thread CTAs fit per SM and the loads of all of
-// them overlap.  Loads are 16 bytes per lane, 512 contiguous bytes per warp
-// instruction; codes are stored 8 bytes per lane.  HBM traffic per row:
+// One HBM read per row: each of the CTA's 256 threads loads its VPT 16-byte
+// vectors of the row at once (lane-interleaved, 512 contiguous bytes per warp
+// instruction) and keeps them packed in registers (a bf16 row of 16384 is 32
+// registers per thread), reduces max |x| on the packed 16-bit pairs, then
+// quantizes the same registers with packed-FP32 arithmetic and stores the
+// codes 8 bytes per lane.  Rows wider than 256 x 16 vectors stream twice
+// (peak pass from HBM, code pass from L2).  HBM traffic per row:
 // K * sizeof(T) read, K written, 4 for the scale.
 #include <type_traits>
 
@@ -122,78 +122,120 @@ __device__ __forceinline__ uint32_t code_e4m3(float v, float scale, float inv, b
       __nv_cvt_float_to_fp8(__fdiv_rn(v, scale), __NV_SATFINITE, __NV_E4M3));
 }
 
+// Codes of one 16-byte vector into `words` (V/4 words).
 template <typename T, int OUT>
+__device__ __forceinline__ void vec_codes(const uint4& raw, float scale, float inv, bool fast,
+                                          uint32_t* words) {
+  constexpr int V = kVec<T>;
+  float v[V];
+  if constexpr (OUT == OUT_E4M3) {
+    unpack<T>(raw, v);
+#pragma unroll
+    for (int w = 0; w < V / 4; ++w)
+      words[w] = code_e4m3(v[4 * w], scale, inv, fast) |
+                 (code_e4m3(v[4 * w + 1], scale, inv, fast) << 8) |
+                 (code_e4m3(v[4 * w + 2], scale, inv, fast) << 16) |
+                 (code_e4m3(v[4 * w + 3], scale, inv, fast) << 24);
+  } else {
+    const float dmax = pack_i8_vec<T>(raw, inv, words);
+    if (!fast || dmax > 0.5f - 0x1p-14f) {
+      unpack<T>(raw, v);
+#pragma unroll
+      for (int w = 0; w < V / 4; ++w)
+        words[w] = code_i8_exact(v[4 * w], scale) | (code_i8_exact(v[4 * w + 1], scale) << 8) |
+                   (code_i8_exact(v[4 * w + 2], scale) << 16) |
+                   (code_i8_exact(v[4 * w + 3], scale) << 24);
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_codes(uint8_t* qr, int64_t j, const uint32_t* words) {
+  if constexpr (kVec<T> == 8)
+    *reinterpret_cast<uint2*>(qr + j * 8) = make_uint2(words[0], words[1]);
+  else
+    *reinterpret_cast<uint32_t*>(qr + j * 4) = words[0];
+}
+
+__device__ __forceinline__ float cta_peak(float peak, float* red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = peak;
+  __syncthreads();
+  peak = red[0];
+#pragma unroll
+  for (int w = 1; w < kThreads / 32; ++w) peak = fmaxf(peak, red[w]);
+  __syncthreads();
+  return peak;
+}
+
+// VPT > 0: each thread holds VPT vectors of the row in registers (one HBM
+// read).  VPT == 0: two streaming passes for very wide rows.
+template <typename T, int OUT, int VPT>
 __global__ void __launch_bounds__(kThreads)
     quant_rows_kernel(const T* __restrict__ x, int64_t rows, int64_t K, uint8_t* __restrict__ q,
                       float* __restrict__ s) {
   constexpr int V = kVec<T>;
   __shared__ float red[kThreads / 32];
   const int tid = threadIdx.x;
-  const int64_t nvec = K / V;  // K % V == 0 on this path
+  const int nvec = static_cast<int>(K / V);  // K % V == 0 on this path
+  const float qmax = OUT == OUT_E4M3 ? 448.0f : 127.0f;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
-    // ---- pass 1: peak -----------------------------------------------------
-    float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f, p3 = 0.0f;
-    int64_t i = tid;
-    for (; i + 3 * kThreads < nvec; i += 4 * kThreads) {
-      const uint4 a = __ldg(xr + i), b = __ldg(xr + i + kThreads);
-      const uint4 c = __ldg(xr + i + 2 * kThreads), d = __ldg(xr + i + 3 * kThreads);
-      p0 = fmaxf(p0, vec_absmax<T>(a));
-      p1 = fmaxf(p1, vec_absmax<T>(b));
-      p2 = fmaxf(p2, vec_absmax<T>(c));
-      p3 = fmaxf(p3, vec_absmax<T>(d));
-    }
-    for (; i < nvec; i += kThreads) p0 = fmaxf(p0, vec_absmax<T>(__ldg(xr + i)));
-    float peak = fmaxf(fmaxf(p0, p1), fmaxf(p2, p3));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, off));
-    if ((tid & 31) == 0) red[tid >> 5] = peak;
-    __syncthreads();
-    peak = red[0];
-#pragma unroll
-    for (int w = 1; w < kThreads / 32; ++w) peak = fmaxf(peak, red[w]);
-    __syncthreads();
-    const float qmax = OUT == OUT_E4M3 ? 448.0f : 127.0f;
-    const float scale = peak == 0.0f ? 1.0f : __fdiv_rn(peak, qmax);
-    const float inv = __frcp_rn(scale);
-    const bool fast = scale >= 0x1p-100f;
-    if (tid == 0) s[row] = scale;
-    // ---- pass 2: codes ----------------------------------------------------
     uint8_t* qr = q + row * K;
-    for (int64_t j = tid; j < nvec; j += kThreads) {
-      const uint4 raw = __ldg(xr + j);
-      float v[V];
-      uint32_t words[V / 4];
-      if constexpr (OUT == OUT_E4M3) {
-        unpack<T>(raw, v);
+    if constexpr (VPT > 0) {
+      uint4 raw[VPT];
 #pragma unroll
-        for (int w = 0; w < V / 4; ++w)
-          words[w] = code_e4m3(v[4 * w], scale, inv, fast) |
-                     (code_e4m3(v[4 * w + 1], scale, inv, fast) << 8) |
-                     (code_e4m3(v[4 * w + 2], scale, inv, fast) << 16) |
-                     (code_e4m3(v[4 * w + 3], scale, inv, fast) << 24);
-      } else {
-        const float dmax = pack_i8_vec<T>(raw, inv, words);
-        if (!fast || dmax > 0.5f - 0x1p-14f) {
-          unpack<T>(raw, v);
+      for (int i = 0; i < VPT; ++i) {
+        const int j = tid + i * kThreads;
+        raw[i] = j < nvec ? __ldg(xr + j) : make_uint4(0, 0, 0, 0);
+      }
+      float peak = 0.0f;
 #pragma unroll
-          for (int w = 0; w < V / 4; ++w)
-            words[w] = code_i8_exact(v[4 * w], scale) | (code_i8_exact(v[4 * w + 1], scale) << 8) |
-                       (code_i8_exact(v[4 * w + 2], scale) << 16) |
-                       (code_i8_exact(v[4 * w + 3], scale) << 24);
+      for (int i = 0; i < VPT; ++i) peak = fmaxf(peak, vec_absmax<T>(raw[i]));
+      peak = cta_peak(peak, red);
+      const float scale = peak == 0.0f ? 1.0f : __fdiv_rn(peak, qmax);
+      const float inv = __frcp_rn(scale);
+      const bool fast = scale >= 0x1p-100f;
+      if (tid == 0) s[row] = scale;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int j = tid + i * kThreads;
+        if (j < nvec) {
+          uint32_t words[V / 4];
+          vec_codes<T, OUT>(raw[i], scale, inv, fast, words);
+          store_codes<T>(qr, j, words);
         }
       }
-      if constexpr (V == 8)
-        *reinterpret_cast<uint2*>(qr + j * 8) = make_uint2(words[0], words[1]);
-      else
-        *reinterpret_cast<uint32_t*>(qr + j * 4) = words[0];
+    } else {
+      float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f, p3 = 0.0f;
+      int j = tid;
+      for (; j + 3 * kThreads < nvec; j += 4 * kThreads) {
+        const uint4 a = __ldg(xr + j), b = __ldg(xr + j + kThreads);
+        const uint4 c = __ldg(xr + j + 2 * kThreads), d = __ldg(xr + j + 3 * kThreads);
+        p0 = fmaxf(p0, vec_absmax<T>(a));
+        p1 = fmaxf(p1, vec_absmax<T>(b));
+        p2 = fmaxf(p2, vec_absmax<T>(c));
+        p3 = fmaxf(p3, vec_absmax<T>(d));
+      }
+      for (; j < nvec; j += kThreads) p0 = fmaxf(p0, vec_absmax<T>(__ldg(xr + j)));
+      const float peak = cta_peak(fmaxf(fmaxf(p0, p1), fmaxf(p2, p3)), red);
+      const float scale = peak == 0.0f ? 1.0f : __fdiv_rn(peak, qmax);
+      const float inv = __frcp_rn(scale);
+      const bool fast = scale >= 0x1p-100f;
+      if (tid == 0) s[row] = scale;
+      for (j = tid; j < nvec; j += kThreads) {
+        uint32_t words[V / 4];
+        vec_codes<T, OUT>(__ldg(xr + j), scale, inv, fast, words);
+        store_codes<T>(qr, j, words);
+      }
     }
   }
 }
 
-template <typename T, int OUT>
-cudaError_t launch_quant_t(const RowPrepArgs& a, cudaStream_t stream) {
-  auto kern = quant_rows_kernel<T, OUT>;
+template <typename T, int OUT, int VPT>
+cudaError_t launch_quant_v(const RowPrepArgs& a, cudaStream_t stream) {
+  auto kern = quant_rows_kernel<T, OUT, VPT>;
   int dev = 0, sms = 0, per_sm = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -206,6 +248,17 @@ cudaError_t launch_quant_t(const RowPrepArgs& a, cudaStream_t stream) {
   kern<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
       reinterpret_cast<const T*>(a.x), a.rows, a.K, reinterpret_cast<uint8_t*>(a.q), a.s);
   return cudaGetLastError();
+}
+
+template <typename T, int OUT>
+cudaError_t launch_quant_t(const RowPrepArgs& a, cudaStream_t stream) {
+  const int64_t nvec = a.K / kVec<T>;
+  if (nvec <= 1 * kThreads) return launch_quant_v<T, OUT, 1>(a, stream);
+  if (nvec <= 2 * kThreads) return launch_quant_v<T, OUT, 2>(a, stream);
+  if (nvec <= 4 * kThreads) return launch_quant_v<T, OUT, 4>(a, stream);
+  if (nvec <= 8 * kThreads) return launch_quant_v<T, OUT, 8>(a, stream);
+  if (nvec <= 16 * kThreads) return launch_quant_v<T, OUT, 16>(a, stream);
+  return launch_quant_v<T, OUT, 0>(a, stream);
 }
 
 }  // namespace
