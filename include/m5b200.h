@@ -141,6 +141,24 @@ M5B_API int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t
              const void* residual, const void* gate, const int32_t* gate_row_map,
              int64_t gate_rows, void* stream);
 
+/* Workspace bytes m5b_linear needs for activations [m, k]: the per-token
+ * codes (m * k bytes, 256-byte aligned) followed by the fp32 scales. */
+M5B_API int64_t m5b_linear_workspace_bytes(int64_t m, int64_t k);
+
+/* One call for the online projection y = gemm(quantize([rotate](x)), wq):
+ *   codes, scales = quantize(x D H) (block_size > 0, signs as in m5b_rotate)
+ *                 or quantize(x)     (block_size == 0)
+ *   y[m, n] = (float(acc) * scales[m]) * w_scales[n] -> out_dtype (bf16/f16/f32)
+ * x: [m, k] bf16 / fp16 / fp32; wq: [n, k] codes prepared offline with the
+ * same mode (and rotation); k % 16 == 0 (mode FP8: k % 128 == 0).  The codes
+ * and scales live in the caller's workspace (m5b_linear_workspace_bytes).
+ * Replaces the reference's online stage quantize -> gemm
+ * (src/m5kernels/engine.py:180-182, hadamard_gemm.py:65-69). */
+M5B_API int m5b_linear(const void* x, int x_dtype, int64_t m, int64_t k, int block_size,
+                       const int8_t* signs, const void* wq, const float* w_scales, int64_t n,
+                       int mode, void* out, int out_dtype, void* workspace,
+                       int64_t workspace_bytes, void* stream);
+
 /* Q or K projection with per-head RMSNorm and split-half RoPE, head-major:
  *   z = bf16(v)  (v as in m5b_gemm), per (row, head): r = 1/sqrt(mean(z^2) + eps)
  *   u_j = z_j * r * gamma_j; for j < R: (u_j, u_{j+R}) rotated by

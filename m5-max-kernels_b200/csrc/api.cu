@@ -537,4 +537,33 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
   return gemm_launch(ta, tb, tbh, g, 128, false, stream);
 }
 
+int64_t m5b_linear_workspace_bytes(int64_t m, int64_t k) {
+  if (m <= 0 || k <= 0) return 0;
+  const int64_t codes = (m * k + 255) & ~int64_t(255);
+  return codes + m * int64_t(sizeof(float));
+}
+
+int m5b_linear(const void* x, int x_dtype, int64_t m, int64_t k, int block_size,
+               const int8_t* signs, const void* wq, const float* w_scales, int64_t n, int mode,
+               void* out, int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (mode != M5B_MODE_INT8 && mode != M5B_MODE_FP8)
+    return fail(M5B_EUNSUPPORTED, "the online projection supports int8 and fp8 (E4M3)");
+  if (m <= 0 || k <= 0 || n <= 0) return fail(M5B_EINVAL, "A and B must be nonempty matrices");
+  if (k % 16)
+    return fail(M5B_EUNSUPPORTED, "the online projection needs K %% 16 == 0 (16-byte code rows)");
+  const int64_t need = m5b_linear_workspace_bytes(m, k);
+  if (!workspace || workspace_bytes < need)
+    return fail(M5B_EINVAL, "workspace of %lld bytes required", static_cast<long long>(need));
+  if (!aligned(workspace, 256)) return fail(M5B_EINVAL, "workspace must be 256-byte aligned");
+  uint8_t* codes = static_cast<uint8_t*>(workspace);
+  float* scales = reinterpret_cast<float*>(codes + ((m * k + 255) & ~int64_t(255)));
+  int rc = block_size > 0
+               ? m5b_hadamard_quantize(x, x_dtype, m, k, block_size, signs, mode, codes, scales,
+                                       stream)
+               : m5b_quantize(x, x_dtype, m, k, mode, codes, scales, stream);
+  if (rc) return rc;
+  return m5b_gemm(codes, wq, m, n, k, mode, scales, w_scales, out, out_dtype, nullptr, nullptr, 0,
+                  nullptr, nullptr, nullptr, 0, stream);
+}
+
 }  // extern "C"

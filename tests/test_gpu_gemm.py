@@ -184,3 +184,28 @@ def test_pair_split_tail_bit_exact(ops, shape):
     assert torch.equal(acc, expect)
     y = ops.gemm(aq, bq, "int8", a_scales=sa, b_scales=sb, output_dtype=torch.bfloat16).cpu()
     assert torch.equal(y, co.gemm_epilogue(expect, sa.cpu(), sb.cpu()))
+
+
+@pytest.mark.parametrize("mode", ["int8", "fp8"])
+@pytest.mark.parametrize("block", [0, 128])
+def test_linear_one_call_equals_two_calls(ops, mode, block):
+    m, n, k = 300, 520, 1024
+    a, b = _operands(m, n, k, seed=31)
+    signs = torch.from_numpy(ref.hadamard_signs(k, 9)).to(DEV) if block else None
+    if block:
+        wq, ws = ops.hadamard_quantize(b.to(DEV), block, signs, mode)
+        aq, sa = ops.hadamard_quantize(a.to(DEV), block, signs, mode)
+    else:
+        wq, ws = _q(ops, b, mode)
+        aq, sa = _q(ops, a, mode)
+    two = ops.gemm(aq, wq, mode, a_scales=sa, b_scales=ws, output_dtype=torch.bfloat16)
+    one = ops.linear(a.to(DEV), wq, ws, mode, block_size=block, signs=signs)
+    one_again = ops.linear(a.to(DEV), wq, ws, mode, block_size=block, signs=signs)
+    assert torch.equal(one, two) and torch.equal(one_again, two)
+
+
+def test_linear_rejects_bad_k(ops):
+    x = torch.ones(4, 40, device=DEV, dtype=torch.bfloat16)
+    wq = torch.ones(8, 40, device=DEV, dtype=torch.int8)
+    with pytest.raises(NotImplementedError, match="16"):
+        ops.linear(x, wq, torch.ones(8, device=DEV))
