@@ -87,7 +87,12 @@ def _f64(t) -> np.ndarray:
 
 
 def timed(fn, warmup: int, repeat: int) -> dict:
-    """Per-sample device time (CUDA events on the current stream) and host wall time."""
+    """Per-sample device time (CUDA events on the current stream) and host wall time.
+
+    Before each sample a short device spin is queued ahead of the start event,
+    so the host-side launch latency of `fn` overlaps the spin instead of being
+    counted as device time.
+    """
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -97,6 +102,7 @@ def timed(fn, warmup: int, repeat: int) -> dict:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         start = time.perf_counter_ns()
+        torch.cuda._sleep(200_000)  # ~0.1 ms at 2 GHz: covers the launch overhead of fn
         e0.record(stream)
         fn()
         e1.record(stream)
