@@ -159,6 +159,20 @@ M5B_API int m5b_linear(const void* x, int x_dtype, int64_t m, int64_t k, int blo
                        int mode, void* out, int out_dtype, void* workspace,
                        int64_t workspace_bytes, void* stream);
 
+/* m5b_linear for callers that cannot allocate device memory (a host whose
+ * device memory is already committed to its own pool, a plugin host that
+ * forbids extension allocations, a hot path that must not take cudaMalloc's
+ * device synchronisation).  Same arguments and result as m5b_linear minus the
+ * workspace: the codes and scales live in a fixed 64 MiB + 64 KiB device array
+ * inside the library, reserved on every GPU that loads it.  Limits:
+ * m * k <= 67,108,864 and m <= 16,384 (else M5B_EINVAL).  Calls share that
+ * array: calls whose kernels overlap on the GPU race and must be ordered.
+ * The first call on a device looks the array's address up (make it before
+ * any stream capture).  Allocates nothing.  No counterpart in the reference. */
+M5B_API int m5b_linear_noalloc(const void* x, int x_dtype, int64_t m, int64_t k, int block_size,
+                               const int8_t* signs, const void* wq, const float* w_scales,
+                               int64_t n, int mode, void* out, int out_dtype, void* stream);
+
 /* Q or K projection with per-head RMSNorm and split-half RoPE, head-major:
  *   z = bf16(v)  (v as in m5b_gemm), per (row, head): r = 1/sqrt(mean(z^2) + eps)
  *   u_j = z_j * r * gamma_j; for j < R: (u_j, u_{j+R}) rotated by

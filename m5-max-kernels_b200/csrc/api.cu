@@ -225,6 +225,8 @@ int norm_setup(RowPrepArgs& a, const void* gamma, int gamma_dtype, const void* s
 
 }  // namespace
 
+int m5b::set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 extern "C" {
 
 int m5b_version(void) { return 100; }

@@ -46,6 +46,9 @@ struct RowMaps {
   int box_rows;   // 128-byte box rows per TMA load
 };
 
+// Record `msg` as this thread's m5b_last_error() text and return `code`.
+int set_last_error(int code, const char* msg);
+
 int row_prep_warps(int64_t K, int block);
 bool quant_rows_applicable(const RowPrepArgs& a, int x_dtype, int block, int out);
 cudaError_t launch_quant_rows(const RowPrepArgs& a, int x_dtype, int out, cudaStream_t stream);
