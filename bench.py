@@ -178,6 +178,87 @@ def cpu_reference(steps: int, warmup: int, target_s: float = 12.0):
             "seconds_per_step": per}
 
 
+def run_secondary(args, world, rank, local):
+    """Other BASELINE configurations (not the headline line): time one workload.
+
+    prep_c3: online H128 rotation + per-token INT8 of the FFN-down activations
+             (M=4096, K=16384; outlier distribution), HBM bytes 3K+4 per row.
+    prep_c4: gated residual + LayerNorm (eps 1e-6, no affine) + AdaLN (2 samples
+             of 2048 tokens) + H128 + INT8 (M=4096, K=4096), bytes 7K+4 per row.
+    qk_c5:   H256 + INT8 online prep and the Q/K projection with RMSNorm + RoPE
+             (M=9914, K=4096, 32 heads x 128, theta 10000, R=64).
+    """
+    import torch
+
+    import m5kernels_b200 as m5
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    stream = torch.cuda.current_stream(dev)
+    peaks = _peaks()
+    if args.workload == "prep_c3":
+        m, k = 4096, 16384
+        x = torch.randn(m, k, device=dev, generator=g)
+        cols = torch.randperm(k, device=dev, generator=g)[: k // 100]
+        x[:, cols] *= 50
+        x = x.to(torch.bfloat16)
+        signs = torch.ones(k, dtype=torch.int8, device=dev)
+        fn = lambda: m5.hadamard_quantize(x, 128, signs, "int8")  # noqa: E731
+        nbytes, unit = m * (3 * k + 4), "GB/s"
+        kernel = "row_prep_kernel<bf16,128,int8>"
+    elif args.workload == "prep_c4":
+        m, k, p = 4096, 4096, 2
+        res = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+        br = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+        tab = lambda: (0.1 * torch.randn(p, k, device=dev, generator=g)).to(torch.bfloat16)  # noqa: E731
+        gate, scale, shift = tab(), tab(), tab()
+        gamma = torch.ones(k, dtype=torch.bfloat16, device=dev)
+        rmap = (torch.arange(m, device=dev, dtype=torch.int32) // (m // p)).to(torch.int32)
+        signs = torch.ones(k, dtype=torch.int8, device=dev)
+        fn = lambda: m5.fused_gated_residual_norm_hadamard_quantize(  # noqa: E731
+            res, br, gate, gamma, scale, shift, signs, 128, norm="layer", epsilon=1e-6,
+            gate_row_map=rmap, row_map=rmap)
+        nbytes, unit = m * (7 * k + 4), "GB/s"
+        kernel = "row_prep_kernel<bf16,128,int8> (gated)"
+    else:  # qk_c5
+        m, k, n = 9914, 4096, 4096
+        x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+        w = (0.02 * torch.randn(n, k, device=dev, generator=g)).to(torch.bfloat16)
+        signs = torch.ones(k, dtype=torch.int8, device=dev)
+        wq, ws = m5.hadamard_quantize(w, 256, signs, "int8")
+        gamma = (1 + 0.02 * torch.randn(128, device=dev, generator=g)).to(torch.bfloat16)
+        cos, sin = m5.rope_tables(m, 64, 10000.0, device=dev)
+
+        def fn():
+            q, s = m5.hadamard_quantize(x, 256, signs, "int8")
+            return m5.projection_qk_rope(q, wq, gamma, cos, sin, "int8", a_scales=s, b_scales=ws)
+
+        nbytes, unit = 2.0 * m * n * k, "TOPS"
+        kernel = "row_prep_kernel<bf16,256,int8> + gemm_tc_kernel<i8,128,qk>"
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if unit == "GB/s":
+        value = nbytes / (ms * 1e-3) / 1e9
+        frac = value / peaks["hbm_gbs"]
+    else:
+        value = nbytes / (ms * 1e-3) / 1e12
+        frac = value / (2.0 * peaks["bf16"])
+    if rank == 0:
+        print(json.dumps({"workload": args.workload, "kernel": kernel, "ms": ms, "value": value,
+                          "unit": unit, "frac_of_measured_peak": frac, "steps": args.steps}),
+              flush=True)
+    return 0
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return 0
@@ -346,6 +427,9 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="ffn_down",
+                    choices=["ffn_down", "prep_c3", "prep_c4", "qk_c5"],
+                    help="ffn_down is the headline; the others time one other BASELINE config")
     ap.add_argument("--profile", action="store_true",
                     help="profiling run: timed steps and per-kernel timing only (no e2e, no CPU leg)")
     args = ap.parse_args(argv)
@@ -354,6 +438,8 @@ def main(argv=None):
     world, rank, local = _dist()
     if args.impl == "reference":
         return run_reference(args, world, rank)
+    if args.workload != "ffn_down":
+        return run_secondary(args, world, rank, local)
     return run_b200(args, world, rank, local)
 
 
