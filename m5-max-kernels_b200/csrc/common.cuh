@@ -60,6 +60,29 @@ __device__ __forceinline__ int8_t int8_code(float v, float scale) {
   return static_cast<int8_t>(static_cast<int>(z));
 }
 
+// rint(RN(x / s)) for a value whose reciprocal product t = RN(x * RN(1/s))
+// lies within 2^-14 of the half-integer h next to r = RNE(t).  Division-free:
+//   e = RN(x - h*s) (one FMA) has the exact sign of x/s - h and is zero iff
+//   x/s == h; RN(x/s) == h exactly when |x - h*s| < s * ulp(h)/2, and RN(x/s)
+//   lies past h (on e's side) when it is larger.  Only |e| == s*ulp(h)/2,
+//   where e's own rounding hides which case holds, falls back to an IEEE
+//   division.  Requires s >= 2^-100 and |x| <= 127.0001 * s.
+__device__ __forceinline__ float int8_code_near_tie(float x, float s, float t, float r) {
+  const float h = __fadd_rn(r, copysignf(0.5f, __fsub_rn(t, r)));
+  const float e = __fmaf_rn(-h, s, x);
+  const uint32_t biased = (__float_as_uint(h) >> 23) & 0xFFu;  // |h| >= 0.5
+  const float half_ulp_s = __fmul_rn(s, __uint_as_float((biased - 24u) << 23));
+  const float ae = fabsf(e);
+  float q;
+  if (ae < half_ulp_s)
+    q = __fsub_rn(__fadd_rn(h, 12582912.0f), 12582912.0f);  // RN(x/s) == h: ties to even
+  else if (ae > half_ulp_s)
+    q = __fadd_rn(h, copysignf(0.5f, e));
+  else
+    q = rintf(__fdiv_rn(x, s));
+  return fminf(fmaxf(q, -127.0f), 127.0f);
+}
+
 // OCP E4M3 code with round-to-nearest-even and saturation to +-448.
 __device__ __forceinline__ uint8_t e4m3_code(float v, float scale) {
   float z = __fdiv_rn(v, scale);

@@ -45,15 +45,14 @@ constexpr int kChunk = 64;  // elements per thread
 // rint(v / scale) clipped to +-127 with the exact semantics of an IEEE divide
 // followed by rint.  t = v * (1/scale) is within 2^-15.6 of the correctly
 // rounded quotient when |v| <= peak; unless t lies within 2^-14 of a
-// half-integer both round to the same integer, and in that rare case the
-// quotient is recomputed with an IEEE division.
+// half-integer both round to the same integer, and in that case the code is
+// decided exactly by int8_code_near_tie.
 __device__ __forceinline__ int quant_i8(float v, float scale, float inv, bool fast) {
-  float r;
+  if (!fast) return static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(v, scale)), -127.0f), 127.0f));
   const float t = __fmul_rn(v, inv);
-  r = rintf(t);
-  if (!fast || fabsf(__fsub_rn(t, r)) > 0.5f - 0x1p-14f) r = rintf(__fdiv_rn(v, scale));
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return static_cast<int>(r);
+  const float r = __fsub_rn(__fadd_rn(t, 12582912.0f), 12582912.0f);
+  if (fabsf(__fsub_rn(t, r)) > 0.5f - 0x1p-14f) return static_cast<int>(int8_code_near_tie(v, scale, t, r));
+  return static_cast<int>(fminf(fmaxf(r, -127.0f), 127.0f));
 }
 
 // E4M3 code of RN(v / scale) (RNE, saturating).  The conversion is monotonic,
@@ -75,27 +74,29 @@ __device__ __forceinline__ uint32_t quant_e4m3(float v, float scale, float inv, 
 // low byte of the sum's bit pattern is the two's-complement int8 of rint(t).
 constexpr float kRoundMagic = 12582912.0f;
 
-// Quantize n (multiple of 4) values to int8 codes packed four per word.
-// Fast path only; returns true if any value needs the exact re-check (its
-// product lies within 2^-14 of a half-integer, see quant_i8).
+// Quantize N (multiple of 4) values to int8 codes packed four per word.
+// Values whose product lies within 2^-14 of a half-integer are decided exactly
+// by int8_code_near_tie (per element).  Requires scale >= 2^-100.
 template <int N>
-__device__ __forceinline__ bool quant_i8_fast(const float* v, float inv, uint32_t* words) {
-  bool near_tie = false;
+__device__ __forceinline__ void quant_i8_fast(const float* v, float scale, float inv,
+                                              uint32_t* words) {
+  constexpr float kNear = 0.5f - 0x1p-14f;
 #pragma unroll
   for (int w = 0; w < N / 4; ++w) {
     uint32_t u[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float t = __fmul_rn(v[4 * w + e], inv);
-      const float m = __fadd_rn(t, kRoundMagic);
+      const float x = v[4 * w + e];
+      const float t = __fmul_rn(x, inv);
+      float m = __fadd_rn(t, kRoundMagic);
       const float r = __fsub_rn(m, kRoundMagic);
-      near_tie |= fabsf(__fsub_rn(t, r)) > 0.5f - 0x1p-14f;
+      if (fabsf(__fsub_rn(t, r)) > kNear)
+        m = __fadd_rn(int8_code_near_tie(x, scale, t, r), kRoundMagic);
       u[e] = __float_as_uint(m);
     }
     words[w] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040),
                            0x5410);
   }
-  return near_tie;
 }
 
 // ---------------------------------------------------------------- loads
@@ -226,7 +227,9 @@ __device__ __forceinline__ const uint4* swz_slot(const uint8_t* base, int br, in
   return reinterpret_cast<const uint4*>(base + br * 128 + ((slot ^ (br & 7)) << 4));
 }
 
-template <typename T, int B, int OUT>
+// FULL: every chunk that exists is complete (K % 64 == 0), so per-element
+// bounds checks vanish; always the case for rotations with B >= 64.
+template <typename T, int B, int OUT, bool FULL>
 __global__ void __launch_bounds__(512)
     row_prep_kernel(const __grid_constant__ CUtensorMap map_x,
                     const __grid_constant__ CUtensorMap map_b, const RowPrepArgs a,
@@ -246,9 +249,12 @@ __global__ void __launch_bounds__(512)
   const int64_t K = a.K;
   const int64_t j0 = int64_t(tid) * kChunk;  // first element of this thread's chunk
   const bool have = j0 < K;
-  const int cnt = have ? static_cast<int>(K - j0 < kChunk ? K - j0 : kChunk) : 0;
-  const bool fullchunk = cnt == kChunk;
+  const int cnt = FULL ? (have ? kChunk : 0)
+                       : (have ? static_cast<int>(K - j0 < kChunk ? K - j0 : kChunk) : 0);
+  const bool fullchunk = FULL ? have : cnt == kChunk;
   const bool vec = a.vec_ok != 0;
+  // element i of this thread's chunk exists (folds to `have` when FULL)
+  auto in = [&](int i) { return FULL ? have : (i < cnt); };
   const bool gated = a.branch != nullptr;
   const int inputs = gated ? 2 : 1;
   const int64_t row_bytes = K * int64_t(sizeof(T));
@@ -309,7 +315,8 @@ __global__ void __launch_bounds__(512)
     auto load8_at = [&](const uint8_t* sbase, const T* gbase, int i, float* out) {
       if (sbase != nullptr) {
         if constexpr (sizeof(T) == 2) {
-          cvt8<T>(*swz_slot(sbase, tid, i / 8), out);
+          const uint4 raw = *swz_slot(sbase, tid, i / 8);  // one 16-byte shared load
+          cvt8<T>(raw, out);
         } else {
           const int br = 2 * tid + (i >= 32 ? 1 : 0);
           const int sl = (i % 32) / 4;
@@ -331,7 +338,7 @@ __global__ void __launch_bounds__(512)
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) out[e] = (i + e < cnt) ? to_f32(gbase[j0 + i + e]) : 0.0f;
+        for (int e = 0; e < 8; ++e) out[e] = in(i + e) ? to_f32(gbase[j0 + i + e]) : 0.0f;
       }
     };
     if (have) {
@@ -347,13 +354,13 @@ __global__ void __launch_bounds__(512)
       const bool pvec = fullchunk && a.params_vec;
 #pragma unroll
       for (int i = 0; i < kChunk; i += 8) {
-        if (i < cnt) {
+        if (in(i)) {
           float br[8], g[8];
           load8_at(bs, bg, i, br);
           param8(a.gate, a.gate_dtype, goff + j0 + i, pvec, g);
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            if (i + e < cnt) v[i + e] = round_through<T>(__fmaf_rn(br[e], g[e], v[i + e]));
+            if (in(i + e)) v[i + e] = round_through<T>(__fmaf_rn(br[e], g[e], v[i + e]));
           if (fullchunk && vec) {
             if constexpr (sizeof(T) == 2) {
               uint4 raw;
@@ -370,7 +377,7 @@ __global__ void __launch_bounds__(512)
           } else {
 #pragma unroll
             for (int e = 0; e < 8; ++e)
-              if (i + e < cnt) rrow[j0 + i + e] = from_f32<T>(v[i + e]);
+              if (in(i + e)) rrow[j0 + i + e] = from_f32<T>(v[i + e]);
           }
         }
       }
@@ -400,14 +407,14 @@ __global__ void __launch_bounds__(512)
       const bool pvec = fullchunk && a.params_vec;
 #pragma unroll
       for (int i = 0; i < kChunk; i += 8) {
-        if (i < cnt) {
+        if (in(i)) {
           float g[8], sc[8], sh[8];
           param8(a.gamma, a.gamma_dtype, j0 + i, pvec, g);
           param8(a.scale, a.scale_dtype, moff + j0 + i, pvec, sc);
           param8(a.shift, a.shift_dtype, moff + j0 + i, pvec, sh);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            if (i + e < cnt) {
+            if (in(i + e)) {
               const float t = __fmul_rn(__fmul_rn(__fsub_rn(v[i + e], mean), inv), g[e]);
               float y = __fmaf_rn(t, __fadd_rn(1.0f, sc[e]), sh[e]);
               if (a.round_output) y = round_through<T>(y);
@@ -431,7 +438,7 @@ __global__ void __launch_bounds__(512)
       } else {
 #pragma unroll
         for (int i = 0; i < kChunk; ++i)
-          if (i < cnt && a.signs[j0 + i] < 0) v[i] = -v[i];
+          if (in(i) && a.signs[j0 + i] < 0) v[i] = -v[i];
       }
     }
 
@@ -471,7 +478,7 @@ __global__ void __launch_bounds__(512)
       } else {
 #pragma unroll
         for (int i = 0; i < kChunk; ++i)
-          if (i < cnt) yrow[j0 + i] = v[i];
+          if (in(i)) yrow[j0 + i] = v[i];
       }
     } else {
       // ---- row peak, per-row scale, codes ----------------------------------
@@ -502,16 +509,16 @@ __global__ void __launch_bounds__(512)
 #pragma unroll
           for (int w0 = 0; w0 < kChunk / 4; w0 += 4) {
             uint32_t words[4];
-            const bool redo = quant_i8_fast<16>(v + 4 * w0, rinv, words) || !fast;
-            if (redo) {
-              // rare: a product within 2^-14 of a half-integer; divide exactly
+            if (fast) {
+              quant_i8_fast<16>(v + 4 * w0, scale, rinv, words);
+            } else {  // scale below 2^-100: divide exactly
 #pragma unroll
               for (int w = 0; w < 4; ++w) {
                 const float* p = v + 4 * (w0 + w);
-                words[w] = (quant_i8(p[0], scale, rinv, fast) & 0xFF) |
-                           ((quant_i8(p[1], scale, rinv, fast) & 0xFF) << 8) |
-                           ((quant_i8(p[2], scale, rinv, fast) & 0xFF) << 16) |
-                           ((quant_i8(p[3], scale, rinv, fast) & 0xFF) << 24);
+                words[w] = (quant_i8(p[0], scale, rinv, false) & 0xFF) |
+                           ((quant_i8(p[1], scale, rinv, false) & 0xFF) << 8) |
+                           ((quant_i8(p[2], scale, rinv, false) & 0xFF) << 16) |
+                           ((quant_i8(p[3], scale, rinv, false) & 0xFF) << 24);
               }
             }
             *reinterpret_cast<uint4*>(qrow + j0 + 4 * w0) =
@@ -521,7 +528,7 @@ __global__ void __launch_bounds__(512)
       } else {
 #pragma unroll
         for (int i = 0; i < kChunk; ++i) {
-          if (i < cnt) {
+          if (in(i)) {
             if constexpr (OUT == OUT_E4M3)
               qrow[j0 + i] = static_cast<uint8_t>(quant_e4m3(v[i], scale, rinv, fast));
             else
@@ -544,9 +551,9 @@ __global__ void __launch_bounds__(512)
   }
 }
 
-template <typename T, int B, int OUT>
-static cudaError_t launch_t(const RowPrepArgs& a, const RowMaps& maps, cudaStream_t stream) {
-  auto kern = row_prep_kernel<T, B, OUT>;
+template <typename T, int B, int OUT, bool FULL>
+static cudaError_t launch_f(const RowPrepArgs& a, const RowMaps& maps, cudaStream_t stream) {
+  auto kern = row_prep_kernel<T, B, OUT, FULL>;
   const int threads = a.warps * 32;
   const int64_t row_bytes = a.K * int64_t(sizeof(T));
   const int inputs = a.branch ? 2 : 1;
@@ -574,6 +581,16 @@ static cudaError_t launch_t(const RowPrepArgs& a, const RowMaps& maps, cudaStrea
   kern<<<static_cast<unsigned>(grid), threads, smem, stream>>>(maps.x, maps.b, a, stages,
                                                                maps.box_rows);
   return cudaGetLastError();
+}
+
+template <typename T, int B, int OUT>
+static cudaError_t launch_t(const RowPrepArgs& a, const RowMaps& maps, cudaStream_t stream) {
+  if constexpr (B >= 64) {
+    return launch_f<T, B, OUT, true>(a, maps, stream);  // K % B == 0 implies whole chunks
+  } else {
+    if (a.K % kChunk == 0) return launch_f<T, B, OUT, true>(a, maps, stream);
+    return launch_f<T, B, OUT, false>(a, maps, stream);
+  }
 }
 
 template <typename T, int OUT>

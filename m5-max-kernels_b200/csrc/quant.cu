@@ -63,15 +63,18 @@ __device__ __forceinline__ void unpack(const uint4& raw, float* out) {
 // INT8 codes of one 16-byte vector (8 bf16/fp16 or 4 fp32 values) packed
 // into words, on sm_100 packed-FP32 arithmetic (each lane an IEEE binary32
 // op).  Per pair: t = x * inv, m = t + 1.5*2^23 (RNE to integer, code in the
-// low byte of m), r = m - 1.5*2^23, d = t - r (both exact).  Returns max |d|;
-// max |d| > 0.5 - 2^-14 flags a product near a half-integer.
+// low byte of m), r = m - 1.5*2^23, d = t - r (both exact).  A value with
+// |d| > 0.5 - 2^-14 sits next to a half-integer; its code is decided exactly
+// by int8_code_near_tie (per element, so a warp rarely pays for it).
+// Requires fast (scale >= 2^-100).
 template <typename T>
-__device__ __forceinline__ float pack_i8_vec(const uint4& raw, float inv, uint32_t* words) {
+__device__ __forceinline__ void pack_i8_vec(const uint4& raw, float scale, float inv,
+                                            uint32_t* words) {
   const float2 inv2 = make_float2(inv, inv);
   const float2 mag2 = make_float2(kMagic, kMagic);
   const float2 nmag2 = make_float2(-kMagic, -kMagic);
   const float2 neg1 = make_float2(-1.0f, -1.0f);
-  float dmax = 0.0f;
+  constexpr float kNear = 0.5f - 0x1p-14f;
   constexpr int PAIRS = sizeof(T) == 2 ? 4 : 2;
   uint32_t u[2 * PAIRS];
 #pragma unroll
@@ -90,10 +93,11 @@ __device__ __forceinline__ float pack_i8_vec(const uint4& raw, float inv, uint32
                       reinterpret_cast<const float*>(&raw)[2 * p + 1]);
     }
     const float2 t = __fmul2_rn(v, inv2);
-    const float2 m = __fadd2_rn(t, mag2);
+    float2 m = __fadd2_rn(t, mag2);
     const float2 r = __fadd2_rn(m, nmag2);
     const float2 d = __ffma2_rn(r, neg1, t);
-    dmax = fmaxf(dmax, fmaxf(fabsf(d.x), fabsf(d.y)));
+    if (fabsf(d.x) > kNear) m.x = __fadd_rn(int8_code_near_tie(v.x, scale, t.x, r.x), kMagic);
+    if (fabsf(d.y) > kNear) m.y = __fadd_rn(int8_code_near_tie(v.y, scale, t.y, r.y), kMagic);
     u[2 * p] = __float_as_uint(m.x);
     u[2 * p + 1] = __float_as_uint(m.y);
   }
@@ -101,7 +105,6 @@ __device__ __forceinline__ float pack_i8_vec(const uint4& raw, float inv, uint32
   for (int w = 0; w < PAIRS / 2; ++w)
     words[w] = __byte_perm(__byte_perm(u[4 * w], u[4 * w + 1], 0x0040),
                            __byte_perm(u[4 * w + 2], u[4 * w + 3], 0x0040), 0x5410);
-  return dmax;
 }
 
 __device__ __forceinline__ uint32_t code_i8_exact(float v, float scale) {
@@ -137,8 +140,9 @@ __device__ __forceinline__ void vec_codes(const uint4& raw, float scale, float i
                  (code_e4m3(v[4 * w + 2], scale, inv, fast) << 16) |
                  (code_e4m3(v[4 * w + 3], scale, inv, fast) << 24);
   } else {
-    const float dmax = pack_i8_vec<T>(raw, inv, words);
-    if (!fast || dmax > 0.5f - 0x1p-14f) {
+    if (fast) {
+      pack_i8_vec<T>(raw, scale, inv, words);
+    } else {  // scale below 2^-100: the reciprocal product is not trustworthy
       unpack<T>(raw, v);
 #pragma unroll
       for (int w = 0; w < V / 4; ++w)
