@@ -354,7 +354,9 @@ int m5b_fused_gated_residual_norm_hadamard_quantize(
 
 // A CTA pair (cta_group::2, 256 x 256 tiles) when the problem has at least
 // one full pair tile of rows and more than 128 output columns.
-static bool use_pair(int epi, int64_t m, int64_t n) { return epi != EPI_QK && m >= 256 && n > 128; }
+static bool use_pair(int epi, int64_t m, int64_t n) {
+  return m >= 256 && (epi == EPI_QK ? n >= 256 : n > 128);
+}
 
 static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMap& tbh,
                        const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
@@ -523,8 +525,10 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
   if (!aligned(out, 16)) return fail(M5B_EINVAL, "output base address must be 16-byte aligned");
   GemmArgs g{};
   g.epi = EPI_QK;
+  const bool pair = use_pair(EPI_QK, m, n);
+  const int bn = pair ? 256 : 128;  // one or two 128-wide heads per tile
   CUtensorMap ta, tb, tbh;
-  int rc = gemm_common(g, ta, tb, tbh, a, b, m, n, k, mode, 128, false);
+  int rc = gemm_common(g, ta, tb, tbh, a, b, m, n, k, mode, bn, pair);
   if (rc) return rc;
   g.quantized = quant ? 1 : 0;
   g.a_scales = a_scales;
@@ -536,7 +540,7 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
   g.sin = sin;
   g.rope_half = rope_half;
   g.eps = epsilon;
-  return gemm_launch(ta, tb, tbh, g, 128, false, stream);
+  return gemm_launch(ta, tb, tbh, g, bn, pair, stream);
 }
 
 int64_t m5b_linear_workspace_bytes(int64_t m, int64_t k) {

@@ -406,7 +406,6 @@ __global__ void __launch_bounds__(192, 1)
       int m_blk, n_col;
       bool whole;
       unit_tile(t, m_blk, n_col, whole);
-      const int n_blk = n_col / BN;  // Q/K tiles are always whole (one head)
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, g.status,
@@ -431,67 +430,83 @@ __global__ void __launch_bounds__(192, 1)
         __syncwarp();
         if (lane == 0) release_acc(acc);
       } else {
-        // Pass 1: BF16 projection z, its square sum (sequential over the 128
-        // head channels) and a private staged copy of this row.
+        // One or two 128-wide heads per unit.  Per head, pass 1: BF16
+        // projection z, its square sum (sequential over the head's 128
+        // channels) and a private staged copy of this row; pass 2: RMS,
+        // gamma, split-half RoPE and the head-major store.
         __nv_bfloat16* zrow = qk_stage + (quarter * 32 + lane) * kQKStride;
-        float sumsq = 0.0f;
-        const int head = n_blk;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float z0 = acc_value<KIND>(r[i]), z1 = acc_value<KIND>(r[i + 1]);
-            if (g.quantized) {
-              const int col = head * 128 + c * 32 + i;
-              z0 = __fmul_rn(__fmul_rn(z0, sa), __ldg(g.b_scales + col));
-              z1 = __fmul_rn(__fmul_rn(z1, sa), __ldg(g.b_scales + col + 1));
-            }
-            const __nv_bfloat162 zz = __floats2bfloat162_rn(z0, z1);
-            const float f0 = __low2float(zz), f1 = __high2float(zz);
-            sumsq = __fmaf_rn(f0, f0, sumsq);
-            sumsq = __fmaf_rn(f1, f1, sumsq);
-            *reinterpret_cast<__nv_bfloat162*>(zrow + c * 32 + i) = zz;
-          }
+        const int heads_tile = whole ? BN / 128 : (BN / 2) / 128;
+        const int heads_left = (g.N - n_col) / 128;  // N tail: a second head may not exist
+        const int heads_here = heads_left < heads_tile ? (heads_left > 0 ? heads_left : 0)
+                                                       : heads_tile;
+        if (heads_here == 0) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) release_acc(acc);
         }
-        // The accumulator is no longer needed: hand it back to the MMA warp.
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) release_acc(acc);
-        if (row < g.M) {
-          const float inv =
-              __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, 128.0f), g.eps)));
-          const int R = g.rope_half;
-          const __nv_bfloat16* cs = reinterpret_cast<const __nv_bfloat16*>(g.cos) + row * R;
-          const __nv_bfloat16* sn = reinterpret_cast<const __nv_bfloat16*>(g.sin) + row * R;
-          const __nv_bfloat16* gm = reinterpret_cast<const __nv_bfloat16*>(g.gamma);
-          __nv_bfloat16* yrow =
-              reinterpret_cast<__nv_bfloat16*>(g.out) + (int64_t(head) * g.M + row) * 128;
 #pragma unroll 1
-          for (int j0 = 0; j0 < 128; j0 += 8) {
-            uint4 pk;
-            __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&pk);
+        for (int hh = 0; hh < heads_here; ++hh) {
+          const int head = n_col / 128 + hh;
+          float sumsq = 0.0f;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(taddr + hh * 128 + c * 32, r);
+            tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int j = j0 + e;
-              const float uj = __fmul_rn(__fmul_rn(__bfloat162float(zrow[j]), inv),
-                                         __bfloat162float(gm[j]));
-              float out = uj;
-              if (j < 2 * R) {
-                const int p = j < R ? j + R : j - R;
-                const int ang = j < R ? j : j - R;
-                const float up = __fmul_rn(__fmul_rn(__bfloat162float(zrow[p]), inv),
-                                           __bfloat162float(gm[p]));
-                const float c = __bfloat162float(cs[ang]);
-                const float s = __bfloat162float(sn[ang]);
-                out = j < R ? __fsub_rn(__fmul_rn(uj, c), __fmul_rn(up, s))
-                            : __fadd_rn(__fmul_rn(uj, c), __fmul_rn(up, s));
+            for (int i = 0; i < 32; i += 2) {
+              float z0 = acc_value<KIND>(r[i]), z1 = acc_value<KIND>(r[i + 1]);
+              if (g.quantized) {
+                const int col = head * 128 + c * 32 + i;
+                z0 = __fmul_rn(__fmul_rn(z0, sa), __ldg(g.b_scales + col));
+                z1 = __fmul_rn(__fmul_rn(z1, sa), __ldg(g.b_scales + col + 1));
               }
-              h[e] = __float2bfloat16_rn(out);
+              const __nv_bfloat162 zz = __floats2bfloat162_rn(z0, z1);
+              const float f0 = __low2float(zz), f1 = __high2float(zz);
+              sumsq = __fmaf_rn(f0, f0, sumsq);
+              sumsq = __fmaf_rn(f1, f1, sumsq);
+              *reinterpret_cast<__nv_bfloat162*>(zrow + c * 32 + i) = zz;
             }
-            *reinterpret_cast<uint4*>(yrow + j0) = pk;
+          }
+          if (hh == heads_here - 1) {
+            // The accumulator is no longer needed: hand it back to the MMA warp.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) release_acc(acc);
+          }
+          if (row < g.M) {
+            const float inv =
+                __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, 128.0f), g.eps)));
+            const int R = g.rope_half;
+            const __nv_bfloat16* cs = reinterpret_cast<const __nv_bfloat16*>(g.cos) + row * R;
+            const __nv_bfloat16* sn = reinterpret_cast<const __nv_bfloat16*>(g.sin) + row * R;
+            const __nv_bfloat16* gm = reinterpret_cast<const __nv_bfloat16*>(g.gamma);
+            __nv_bfloat16* yrow =
+                reinterpret_cast<__nv_bfloat16*>(g.out) + (int64_t(head) * g.M + row) * 128;
+#pragma unroll 1
+            for (int j0 = 0; j0 < 128; j0 += 8) {
+              uint4 pk;
+              __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&pk);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int j = j0 + e;
+                const float uj = __fmul_rn(__fmul_rn(__bfloat162float(zrow[j]), inv),
+                                           __bfloat162float(gm[j]));
+                float out = uj;
+                if (j < 2 * R) {
+                  const int p = j < R ? j + R : j - R;
+                  const int ang = j < R ? j : j - R;
+                  const float up = __fmul_rn(__fmul_rn(__bfloat162float(zrow[p]), inv),
+                                             __bfloat162float(gm[p]));
+                  const float c = __bfloat162float(cs[ang]);
+                  const float s = __bfloat162float(sn[ang]);
+                  out = j < R ? __fsub_rn(__fmul_rn(uj, c), __fmul_rn(up, s))
+                              : __fadd_rn(__fmul_rn(uj, c), __fmul_rn(up, s));
+                }
+                h[e] = __float2bfloat16_rn(out);
+              }
+              *reinterpret_cast<uint4*>(yrow + j0) = pk;
+            }
           }
         }
       }
@@ -517,8 +532,10 @@ static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const 
                             const GemmArgs& g, int grid, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, QK, PAIR>;
   auto kern = gemm_tc_kernel<KIND, BN, QK, PAIR>;
-  cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+  static std::atomic<long long> shape[kMaxLaunchDevices];
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaError_t e = launch_shape(reinterpret_cast<const void*>(kern), 192, Cfg::SMEM_BYTES, shape,
+                               &dev, &sms, &per_sm);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
@@ -539,17 +556,15 @@ static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const 
   return cudaGetLastError();
 }
 
-int gemm_block_n(const GemmArgs& g) {
-  if (g.epi == EPI_QK) return 128;
-  return g.N <= 128 ? 128 : 256;
-}
+int gemm_block_n(const GemmArgs& g) { return g.N <= 128 ? 128 : 256; }
 
 cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
                         const GemmArgs& g, int bn, int grid, bool pair, cudaStream_t stream) {
   const bool qk = g.epi == EPI_QK;
 #define M5B_KIND_CASE(KIND_)                                                               \
   case KIND_:                                                                              \
-    if (qk) return launch_k<KIND_, 128, true, false>(ta, tb, tbh, g, grid, stream);        \
+    if (qk) return pair ? launch_k<KIND_, 256, true, true>(ta, tb, tbh, g, grid, stream)   \
+                        : launch_k<KIND_, 128, true, false>(ta, tb, tbh, g, grid, stream); \
     if (pair) return launch_k<KIND_, 256, false, true>(ta, tb, tbh, g, grid, stream);      \
     if (bn == 128) return launch_k<KIND_, 128, false, false>(ta, tb, tbh, g, grid, stream); \
     return launch_k<KIND_, 256, false, false>(ta, tb, tbh, g, grid, stream);

@@ -6,7 +6,49 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace m5b {
+
+// Launch shape of one kernel instance on one device, computed once: the
+// dynamic shared-memory attribute is set and the occupancy query made on the
+// first launch with a given shared-memory size, and reused afterwards (the
+// host path of a launch then makes no attribute or occupancy calls).  `slot`
+// is the instance's per-device cache entry; racing first launches both
+// compute the same value.
+constexpr int kMaxLaunchDevices = 64;
+inline cudaError_t launch_shape(const void* kern, int threads, int smem,
+                                std::atomic<long long>* slots, int* dev_out, int* sms_out,
+                                int* per_sm_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxLaunchDevices) return cudaErrorInvalidDevice;
+  *dev_out = dev;
+  static std::atomic<int> sms_cache[kMaxLaunchDevices];
+  int sms = sms_cache[dev].load(std::memory_order_relaxed);
+  if (sms == 0) {
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    sms_cache[dev].store(sms, std::memory_order_relaxed);
+  }
+  *sms_out = sms;
+  const long long key = static_cast<long long>(smem + 1) << 32;
+  const long long v = slots[dev].load(std::memory_order_acquire);
+  if (v != 0 && (v & ~0xFFFFFFFFll) == key) {
+    *per_sm_out = static_cast<int>(v & 0xFFFFFFFFll);
+    return cudaSuccess;
+  }
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) per_sm = 1;
+  slots[dev].store(key | per_sm, std::memory_order_release);
+  *per_sm_out = per_sm;
+  return cudaSuccess;
+}
 
 enum NormKind : int { NORM_NONE = 0, NORM_RMS = 1, NORM_LAYER = 2 };
 enum RowOut : int { OUT_INT8 = 0, OUT_E4M3 = 1, OUT_F32 = 2 };

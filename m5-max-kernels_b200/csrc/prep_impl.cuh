@@ -74,28 +74,69 @@ __device__ __forceinline__ uint32_t quant_e4m3(float v, float scale, float inv, 
 // low byte of the sum's bit pattern is the two's-complement int8 of rint(t).
 constexpr float kRoundMagic = 12582912.0f;
 
-// Quantize N (multiple of 4) values to int8 codes packed four per word.
-// Values whose product lies within 2^-14 of a half-integer are decided exactly
-// by int8_code_near_tie (per element).  Requires scale >= 2^-100.
-template <int N>
-__device__ __forceinline__ void quant_i8_fast(const float* v, float scale, float inv,
-                                              uint32_t* words) {
+// Sixteen values by value (registers), for the out-of-line near-tie path.
+struct Vals16 {
+  float4 a, b, c, d;
+};
+
+// Exact codes of 16 values of which at least one has its product within
+// 2^-14 of a half-integer: the reciprocal-product code per element, and the
+// division-free decision of int8_code_near_tie where it is needed.  Out of
+// line: it runs for a small fraction of 16-value groups.
+static __device__ __noinline__ uint4 quant_i8_near_tie16(Vals16 in, float scale, float inv) {
   constexpr float kNear = 0.5f - 0x1p-14f;
+  const float v[16] = {in.a.x, in.a.y, in.a.z, in.a.w, in.b.x, in.b.y, in.b.z, in.b.w,
+                       in.c.x, in.c.y, in.c.z, in.c.w, in.d.x, in.d.y, in.d.z, in.d.w};
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-  for (int w = 0; w < N / 4; ++w) {
+  for (int e = 0; e < 16; ++e) {
+    const float t = __fmul_rn(v[e], inv);
+    float m = __fadd_rn(t, kRoundMagic);
+    const float r = __fsub_rn(m, kRoundMagic);
+    if (fabsf(__fsub_rn(t, r)) > kNear)
+      m = __fadd_rn(int8_code_near_tie(v[e], scale, t, r), kRoundMagic);
+    w[e >> 2] |= (__float_as_uint(m) & 0xFFu) << (8 * (e & 3));
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Quantize 16 values to int8 codes packed four per word, on sm_100 packed
+// FP32 arithmetic (each lane an IEEE binary32 op): t = x * inv, m = t +
+// 1.5*2^23 (RNE to integer, code in the low byte of m), r = m - 1.5*2^23,
+// d = t - r (exact).  A group with some |d| > 0.5 - 2^-14 is redone by
+// quant_i8_near_tie16.  Requires scale >= 2^-100.
+__device__ __forceinline__ void quant_i8_fast16(const float* v, float scale, float inv,
+                                                uint32_t* words) {
+  const float2 inv2 = make_float2(inv, inv);
+  const float2 mag2 = make_float2(kRoundMagic, kRoundMagic);
+  const float2 nmag2 = make_float2(-kRoundMagic, -kRoundMagic);
+  const float2 neg1 = make_float2(-1.0f, -1.0f);
+  float dmax = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
     uint32_t u[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float x = v[4 * w + e];
-      const float t = __fmul_rn(x, inv);
-      float m = __fadd_rn(t, kRoundMagic);
-      const float r = __fsub_rn(m, kRoundMagic);
-      if (fabsf(__fsub_rn(t, r)) > kNear)
-        m = __fadd_rn(int8_code_near_tie(x, scale, t, r), kRoundMagic);
-      u[e] = __float_as_uint(m);
+    for (int p = 0; p < 2; ++p) {
+      const float2 t = __fmul2_rn(make_float2(v[4 * w + 2 * p], v[4 * w + 2 * p + 1]), inv2);
+      const float2 m = __fadd2_rn(t, mag2);
+      const float2 r = __fadd2_rn(m, nmag2);
+      const float2 d = __ffma2_rn(r, neg1, t);
+      dmax = fmaxf(dmax, fmaxf(fabsf(d.x), fabsf(d.y)));
+      u[2 * p] = __float_as_uint(m.x);
+      u[2 * p + 1] = __float_as_uint(m.y);
     }
     words[w] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040),
                            0x5410);
+  }
+  if (dmax > 0.5f - 0x1p-14f) {
+    const Vals16 in{make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]),
+                    make_float4(v[8], v[9], v[10], v[11]),
+                    make_float4(v[12], v[13], v[14], v[15])};
+    const uint4 q = quant_i8_near_tie16(in, scale, inv);
+    words[0] = q.x;
+    words[1] = q.y;
+    words[2] = q.z;
+    words[3] = q.w;
   }
 }
 
@@ -510,7 +551,7 @@ __global__ void __launch_bounds__(512)
           for (int w0 = 0; w0 < kChunk / 4; w0 += 4) {
             uint32_t words[4];
             if (fast) {
-              quant_i8_fast<16>(v + 4 * w0, scale, rinv, words);
+              quant_i8_fast16(v + 4 * w0, scale, rinv, words);
             } else {  // scale below 2^-100: divide exactly
 #pragma unroll
               for (int w = 0; w < 4; ++w) {
@@ -564,17 +605,10 @@ static cudaError_t launch_f(const RowPrepArgs& a, const RowMaps& maps, cudaStrea
     stages = per_stage <= 24 * 1024 ? 4 : (per_stage <= 48 * 1024 ? 3 : (per_stage <= 96 * 1024 ? 2 : 0));
   }
   const int smem = stages > 0 ? static_cast<int>(stages * buf_stride * inputs) + 1024 : 0;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
-  if (e != cudaSuccess) return e;
-  if (per_sm < 1) per_sm = 1;
-  int sms = 0;
-  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  static std::atomic<long long> shape[kMaxLaunchDevices];
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaError_t e = launch_shape(reinterpret_cast<const void*>(kern), threads, smem, shape, &dev,
+                               &sms, &per_sm);
   if (e != cudaSuccess) return e;
   int64_t grid = int64_t(sms) * per_sm;
   if (grid > a.rows) grid = a.rows;

@@ -63,18 +63,16 @@ __device__ __forceinline__ void unpack(const uint4& raw, float* out) {
 // INT8 codes of one 16-byte vector (8 bf16/fp16 or 4 fp32 values) packed
 // into words, on sm_100 packed-FP32 arithmetic (each lane an IEEE binary32
 // op).  Per pair: t = x * inv, m = t + 1.5*2^23 (RNE to integer, code in the
-// low byte of m), r = m - 1.5*2^23, d = t - r (both exact).  A value with
-// |d| > 0.5 - 2^-14 sits next to a half-integer; its code is decided exactly
-// by int8_code_near_tie (per element, so a warp rarely pays for it).
-// Requires fast (scale >= 2^-100).
+// low byte of m), r = m - 1.5*2^23, d = t - r (both exact).  Returns max |d|;
+// max |d| > 0.5 - 2^-14 flags a product next to a half-integer, whose vector
+// is then redone by i8_words_near_tie.
 template <typename T>
-__device__ __forceinline__ void pack_i8_vec(const uint4& raw, float scale, float inv,
-                                            uint32_t* words) {
+__device__ __forceinline__ float pack_i8_vec(const uint4& raw, float inv, uint32_t* words) {
   const float2 inv2 = make_float2(inv, inv);
   const float2 mag2 = make_float2(kMagic, kMagic);
   const float2 nmag2 = make_float2(-kMagic, -kMagic);
   const float2 neg1 = make_float2(-1.0f, -1.0f);
-  constexpr float kNear = 0.5f - 0x1p-14f;
+  float dmax = 0.0f;
   constexpr int PAIRS = sizeof(T) == 2 ? 4 : 2;
   uint32_t u[2 * PAIRS];
 #pragma unroll
@@ -93,11 +91,10 @@ __device__ __forceinline__ void pack_i8_vec(const uint4& raw, float scale, float
                       reinterpret_cast<const float*>(&raw)[2 * p + 1]);
     }
     const float2 t = __fmul2_rn(v, inv2);
-    float2 m = __fadd2_rn(t, mag2);
+    const float2 m = __fadd2_rn(t, mag2);
     const float2 r = __fadd2_rn(m, nmag2);
     const float2 d = __ffma2_rn(r, neg1, t);
-    if (fabsf(d.x) > kNear) m.x = __fadd_rn(int8_code_near_tie(v.x, scale, t.x, r.x), kMagic);
-    if (fabsf(d.y) > kNear) m.y = __fadd_rn(int8_code_near_tie(v.y, scale, t.y, r.y), kMagic);
+    dmax = fmaxf(dmax, fmaxf(fabsf(d.x), fabsf(d.y)));
     u[2 * p] = __float_as_uint(m.x);
     u[2 * p + 1] = __float_as_uint(m.y);
   }
@@ -105,6 +102,31 @@ __device__ __forceinline__ void pack_i8_vec(const uint4& raw, float scale, float
   for (int w = 0; w < PAIRS / 2; ++w)
     words[w] = __byte_perm(__byte_perm(u[4 * w], u[4 * w + 1], 0x0040),
                            __byte_perm(u[4 * w + 2], u[4 * w + 3], 0x0040), 0x5410);
+  return dmax;
+}
+
+// The exact codes of a vector that holds a product next to a half-integer:
+// per element the reciprocal-product code, and for an element within 2^-14
+// of a half-integer the division-free decision of int8_code_near_tie.  Kept
+// out of line: it runs for a small fraction of vectors.  Requires
+// scale >= 2^-100.
+template <typename T>
+__device__ __noinline__ uint2 i8_words_near_tie(uint4 raw, float scale, float inv) {
+  constexpr int V = kVec<T>;
+  constexpr float kNear = 0.5f - 0x1p-14f;
+  float v[V];
+  unpack<T>(raw, v);
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int e = 0; e < V; ++e) {
+    const float t = __fmul_rn(v[e], inv);
+    float m = __fadd_rn(t, kMagic);
+    const float r = __fadd_rn(m, -kMagic);
+    if (fabsf(__fsub_rn(t, r)) > kNear)
+      m = __fadd_rn(int8_code_near_tie(v[e], scale, t, r), kMagic);
+    w[e >> 2] |= (__float_as_uint(m) & 0xFFu) << (8 * (e & 3));
+  }
+  return make_uint2(w[0], w[1]);
 }
 
 __device__ __forceinline__ uint32_t code_i8_exact(float v, float scale) {
@@ -141,7 +163,11 @@ __device__ __forceinline__ void vec_codes(const uint4& raw, float scale, float i
                  (code_e4m3(v[4 * w + 3], scale, inv, fast) << 24);
   } else {
     if (fast) {
-      pack_i8_vec<T>(raw, scale, inv, words);
+      if (pack_i8_vec<T>(raw, inv, words) > 0.5f - 0x1p-14f) {
+        const uint2 w = i8_words_near_tie<T>(raw, scale, inv);
+        words[0] = w.x;
+        if constexpr (V == 8) words[1] = w.y;
+      }
     } else {  // scale below 2^-100: the reciprocal product is not trustworthy
       unpack<T>(raw, v);
 #pragma unroll
@@ -240,14 +266,12 @@ __global__ void __launch_bounds__(kThreads)
 template <typename T, int OUT, int VPT>
 cudaError_t launch_quant_v(const RowPrepArgs& a, cudaStream_t stream) {
   auto kern = quant_rows_kernel<T, OUT, VPT>;
+  static std::atomic<long long> shape[kMaxLaunchDevices];
   int dev = 0, sms = 0, per_sm = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  cudaError_t e =
+      launch_shape(reinterpret_cast<const void*>(kern), kThreads, 0, shape, &dev, &sms, &per_sm);
   if (e != cudaSuccess) return e;
-  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) return e;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0);
-  if (e != cudaSuccess) return e;
-  int64_t grid = int64_t(sms) * (per_sm > 0 ? per_sm : 1);
+  int64_t grid = int64_t(sms) * per_sm;
   if (grid > a.rows) grid = a.rows;
   kern<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
       reinterpret_cast<const T*>(a.x), a.rows, a.K, reinterpret_cast<uint8_t*>(a.q), a.s);

@@ -37,7 +37,11 @@ def _inputs(m, n, k, half, seed=29):
 
 @pytest.mark.parametrize("shape,half", [((1, 128, 64), 64), ((17, 384, 96), 48),
                                         ((65, 256, 256), 64), ((129, 128, 64), 1),
-                                        ((300, 512, 1024), 64), ((200, 256, 512), 33)])
+                                        ((300, 512, 1024), 64), ((200, 256, 512), 33),
+                                        # CTA-pair tiles of two heads: an odd head count
+                                        # (last tile holds one head), and a last wave split
+                                        # into half tiles, one of them past the last head
+                                        ((512, 384, 256), 64), ((4096, 1408, 256), 64)])
 def test_qk_rope_bit_exact_and_reference(ops, shape, half):
     m, n, k = shape
     x, w, gamma, cos, sin = _inputs(m, n, k, half)

@@ -29,7 +29,11 @@ def tie_rows(rows, k, dtype, seed):
     jitter = torch.randint(-2, 3, (rows, k), generator=g).float()
     x = x.to(dtype)
     if dtype != torch.float32:  # nudge some values by one unit in the last place
-        bits = x.view(torch.int16).to(torch.int32) + jitter.to(torch.int32) * (torch.rand(rows, k, generator=g) < 0.2)
+        raw = x.view(torch.int16).to(torch.int32)
+        # values that flushed to zero (tiny peaks in f16) keep their bits: one
+        # unit below +0 is a NaN pattern
+        nudge = (torch.rand(rows, k, generator=g) < 0.2) & ((raw & 0x7FFF) >= 4)
+        bits = raw + jitter.to(torch.int32) * nudge
         x = bits.to(torch.int16).view(dtype)
     x[:, 0] = peaks.to(dtype)
     x[:, 1] = -(peaks / 2).to(dtype)
