@@ -417,7 +417,8 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMa
 }
 
 static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
-                       GemmArgs& g, int bn, bool pair, void* stream) {
+                       GemmArgs& g, int bn, bool pair, void* stream,
+                       const CUtensorMap* to = nullptr) {
   unsigned int* status = nullptr;
   int sms = 0;
   int rc = device_state(&status, &sms);
@@ -433,7 +434,8 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     g.num_units = g.num_full + 2 * rem;
   }
   const int grid = (g.num_units < slots ? g.num_units : slots) * (pair ? 2 : 1);
-  cudaError_t e = launch_gemm(ta, tb, tbh, g, bn, grid, pair, static_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_gemm(ta, tb, tbh, to ? *to : tbh, g, bn, grid, pair,
+                              static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
   return ok();
 }
@@ -540,7 +542,23 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
   g.sin = sin;
   g.rope_half = rope_half;
   g.eps = epsilon;
-  return gemm_launch(ta, tb, tbh, g, bn, pair, stream);
+  // Vector path with TMA head-block stores: channel pairs (a, a + R) in whole
+  // 16-byte chunks and 16-byte aligned tables.
+  g.qk_fast = rope_half % 8 == 0 && aligned(gamma, 16) && aligned(cos, 16) && aligned(sin, 16);
+  CUtensorMap to{};
+  if (g.qk_fast) {
+    // Head-major output [N/128, M, 128] bf16 as a 3D map; boxes of 64 channels x
+    // 32 rows (one epilogue warp's rows), 128-byte swizzle; rows past M clipped.
+    cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(m), static_cast<cuuint64_t>(n / 128)};
+    cuuint64_t strides[2] = {256, static_cast<cuuint64_t>(m) * 256};
+    cuuint32_t box[3] = {64, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(M5B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  }
+  return gemm_launch(ta, tb, tbh, g, bn, pair, stream, &to);
 }
 
 int64_t m5b_linear_workspace_bytes(int64_t m, int64_t k) {

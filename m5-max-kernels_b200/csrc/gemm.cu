@@ -43,7 +43,6 @@
 namespace m5b {
 
 constexpr int kBM = 128;
-constexpr int kQKStride = 130;  // bf16 elements per staged Q/K row (conflict-free)
 
 template <int BN, bool QK, bool PAIR>
 struct GemmCfg {
@@ -55,8 +54,8 @@ struct GemmCfg {
   static constexpr int STAGES = QK ? 5 : (STAGE_BYTES <= 32 * 1024 ? 6 : 4);
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
-  static constexpr int QK_BYTES = QK ? kBM * kQKStride * 2 : 0;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + 16 + QK_BYTES;
+  static constexpr int QK_BYTES = QK ? kBM * 256 : 0;  // 128 rows x 128 bf16 channels
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + QK_BYTES + BAR_BYTES + 16;
 };
 
 __device__ __forceinline__ void tile_coords(int t, const GemmArgs& g, int& m_blk, int& n_blk) {
@@ -187,7 +186,8 @@ template <int KIND, int BN, bool QK, bool PAIR>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b,
-                   const __grid_constant__ CUtensorMap tmap_b_half, const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tmap_b_half,
+                   const __grid_constant__ CUtensorMap tmap_out, const GemmArgs g) {
   using Cfg = GemmCfg<BN, QK, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int K_ELEMS = (KIND == KIND_BF16 || KIND == KIND_F16) ? 64 : 128;
@@ -199,15 +199,14 @@ __global__ void __launch_bounds__(192, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint8_t* qk_stage = sB + STAGES * Cfg::B_BYTES;  // 1024-aligned (QK only)
+  uint64_t* full = reinterpret_cast<uint64_t*>(qk_stage + Cfg::QK_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  __nv_bfloat16* qk_stage =
-      reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(full) + Cfg::BAR_BYTES + 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -233,6 +232,7 @@ __global__ void __launch_bounds__(192, 1)
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
     if (g.num_units > g.num_full) tma_prefetch_desc(&tmap_b_half);
+    if (QK && g.qk_fast) tma_prefetch_desc(&tmap_out);
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -432,9 +432,19 @@ __global__ void __launch_bounds__(192, 1)
       } else {
         // One or two 128-wide heads per unit.  Per head, pass 1: BF16
         // projection z, its square sum (sequential over the head's 128
-        // channels) and a private staged copy of this row; pass 2: RMS,
+        // channels) and a staged copy of this thread's row; pass 2: RMS,
         // gamma, split-half RoPE and the head-major store.
-        __nv_bfloat16* zrow = qk_stage + (quarter * 32 + lane) * kQKStride;
+        //
+        // Staging: each warp owns 32 rows x 128 channels (8 KB) as two
+        // 64-channel halves of 32 rows x 128 bytes whose 16-byte chunks are
+        // XOR-swizzled by (row & 7) -- the TMA 128-byte swizzle, so one
+        // thread's row is read and written without bank conflicts and the
+        // finished 32 x 128 head block leaves with two tiled TMA stores
+        // (rows past M clipped by the tensor map).
+        uint8_t* wstage = qk_stage + quarter * 8192;
+        auto chunk = [&](int ch) -> uint8_t* {  // channels 8*ch .. 8*ch+7 of this row
+          return wstage + (ch >> 3) * 4096 + lane * 128 + (((ch & 7) ^ (lane & 7)) << 4);
+        };
         const int heads_tile = whole ? BN / 128 : (BN / 2) / 128;
         const int heads_left = (g.N - n_col) / 128;  // N tail: a second head may not exist
         const int heads_here = heads_left < heads_tile ? (heads_left > 0 ? heads_left : 0)
@@ -444,9 +454,12 @@ __global__ void __launch_bounds__(192, 1)
           __syncwarp();
           if (lane == 0) release_acc(acc);
         }
+        const int64_t row0 = row - lane;  // this warp's first row
 #pragma unroll 1
         for (int hh = 0; hh < heads_here; ++hh) {
           const int head = n_col / 128 + hh;
+          if (lane == 0) bulk_wait_group_read0();  // the previous store has read the staging
+          __syncwarp();
           float sumsq = 0.0f;
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
@@ -454,18 +467,24 @@ __global__ void __launch_bounds__(192, 1)
             tmem_ld32(taddr + hh * 128 + c * 32, r);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              float z0 = acc_value<KIND>(r[i]), z1 = acc_value<KIND>(r[i + 1]);
-              if (g.quantized) {
-                const int col = head * 128 + c * 32 + i;
-                z0 = __fmul_rn(__fmul_rn(z0, sa), __ldg(g.b_scales + col));
-                z1 = __fmul_rn(__fmul_rn(z1, sa), __ldg(g.b_scales + col + 1));
+            for (int q = 0; q < 4; ++q) {
+              uint32_t pk[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int e = q * 8 + 2 * i;
+                float z0 = acc_value<KIND>(r[e]), z1 = acc_value<KIND>(r[e + 1]);
+                if (g.quantized) {
+                  const int col = head * 128 + c * 32 + e;
+                  z0 = __fmul_rn(__fmul_rn(z0, sa), __ldg(g.b_scales + col));
+                  z1 = __fmul_rn(__fmul_rn(z1, sa), __ldg(g.b_scales + col + 1));
+                }
+                const __nv_bfloat162 zz = __floats2bfloat162_rn(z0, z1);
+                const float f0 = __low2float(zz), f1 = __high2float(zz);
+                sumsq = __fmaf_rn(f0, f0, sumsq);
+                sumsq = __fmaf_rn(f1, f1, sumsq);
+                pk[i] = *reinterpret_cast<const uint32_t*>(&zz);
               }
-              const __nv_bfloat162 zz = __floats2bfloat162_rn(z0, z1);
-              const float f0 = __low2float(zz), f1 = __high2float(zz);
-              sumsq = __fmaf_rn(f0, f0, sumsq);
-              sumsq = __fmaf_rn(f1, f1, sumsq);
-              *reinterpret_cast<__nv_bfloat162*>(zrow + c * 32 + i) = zz;
+              *reinterpret_cast<uint4*>(chunk(c * 4 + q)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
           }
           if (hh == heads_here - 1) {
@@ -474,13 +493,72 @@ __global__ void __launch_bounds__(192, 1)
             __syncwarp();
             if (lane == 0) release_acc(acc);
           }
-          if (row < g.M) {
-            const float inv =
-                __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, 128.0f), g.eps)));
-            const int R = g.rope_half;
+          const float inv =
+              __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, 128.0f), g.eps)));
+          const int R = g.rope_half;
+          const __nv_bfloat16* gm = reinterpret_cast<const __nv_bfloat16*>(g.gamma);
+          if (g.qk_fast) {
+            // R % 8 == 0: channel a pairs with a + R, both whole 16-byte chunks.
+            if (row < g.M) {
+              const int RC = R >> 3;
+              const uint4* cs4 =
+                  reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(g.cos) + row * R);
+              const uint4* sn4 =
+                  reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(g.sin) + row * R);
+              const uint4* gm4 = reinterpret_cast<const uint4*>(gm);
+#pragma unroll 1
+              for (int q = 0; q < RC; ++q) {
+                uint4 zl = *reinterpret_cast<const uint4*>(chunk(q));
+                uint4 zh = *reinterpret_cast<const uint4*>(chunk(q + RC));
+                const uint4 gl = __ldg(gm4 + q), gh = __ldg(gm4 + q + RC);
+                const uint4 c8 = __ldg(cs4 + q), s8 = __ldg(sn4 + q);
+                __nv_bfloat16* zlh = reinterpret_cast<__nv_bfloat16*>(&zl);
+                __nv_bfloat16* zhh = reinterpret_cast<__nv_bfloat16*>(&zh);
+                const __nv_bfloat16* glh = reinterpret_cast<const __nv_bfloat16*>(&gl);
+                const __nv_bfloat16* ghh = reinterpret_cast<const __nv_bfloat16*>(&gh);
+                const __nv_bfloat16* ch = reinterpret_cast<const __nv_bfloat16*>(&c8);
+                const __nv_bfloat16* sh = reinterpret_cast<const __nv_bfloat16*>(&s8);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  const float ul = __fmul_rn(__fmul_rn(__bfloat162float(zlh[e]), inv),
+                                             __bfloat162float(glh[e]));
+                  const float uh = __fmul_rn(__fmul_rn(__bfloat162float(zhh[e]), inv),
+                                             __bfloat162float(ghh[e]));
+                  const float cv = __bfloat162float(ch[e]), sv = __bfloat162float(sh[e]);
+                  zlh[e] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(ul, cv), __fmul_rn(uh, sv)));
+                  zhh[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(uh, cv), __fmul_rn(ul, sv)));
+                }
+                *reinterpret_cast<uint4*>(chunk(q)) = zl;
+                *reinterpret_cast<uint4*>(chunk(q + RC)) = zh;
+              }
+#pragma unroll 1
+              for (int q = 2 * RC; q < 16; ++q) {
+                uint4 z = *reinterpret_cast<const uint4*>(chunk(q));
+                const uint4 g8 = __ldg(gm4 + q);
+                __nv_bfloat16* zh = reinterpret_cast<__nv_bfloat16*>(&z);
+                const __nv_bfloat16* gh = reinterpret_cast<const __nv_bfloat16*>(&g8);
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  zh[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(__bfloat162float(zh[e]), inv),
+                                                        __bfloat162float(gh[e])));
+                *reinterpret_cast<uint4*>(chunk(q)) = z;
+              }
+            }
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0 && row0 < g.M) {
+              tma_store_3d(&tmap_out, wstage, 0, static_cast<int32_t>(row0), head);
+              tma_store_3d(&tmap_out, wstage + 4096, 64, static_cast<int32_t>(row0), head);
+              bulk_commit_group();
+            }
+          } else if (row < g.M) {
+            // Any R in [1, 64]: element-wise from the staged row, direct stores.
+            auto zat = [&](int j) -> float {
+              return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(chunk(j >> 3) +
+                                                                              (j & 7) * 2));
+            };
             const __nv_bfloat16* cs = reinterpret_cast<const __nv_bfloat16*>(g.cos) + row * R;
             const __nv_bfloat16* sn = reinterpret_cast<const __nv_bfloat16*>(g.sin) + row * R;
-            const __nv_bfloat16* gm = reinterpret_cast<const __nv_bfloat16*>(g.gamma);
             __nv_bfloat16* yrow =
                 reinterpret_cast<__nv_bfloat16*>(g.out) + (int64_t(head) * g.M + row) * 128;
 #pragma unroll 1
@@ -490,14 +568,12 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const int j = j0 + e;
-                const float uj = __fmul_rn(__fmul_rn(__bfloat162float(zrow[j]), inv),
-                                           __bfloat162float(gm[j]));
+                const float uj = __fmul_rn(__fmul_rn(zat(j), inv), __bfloat162float(gm[j]));
                 float out = uj;
                 if (j < 2 * R) {
                   const int p = j < R ? j + R : j - R;
                   const int ang = j < R ? j : j - R;
-                  const float up = __fmul_rn(__fmul_rn(__bfloat162float(zrow[p]), inv),
-                                             __bfloat162float(gm[p]));
+                  const float up = __fmul_rn(__fmul_rn(zat(p), inv), __bfloat162float(gm[p]));
                   const float c = __bfloat162float(cs[ang]);
                   const float s = __bfloat162float(sn[ang]);
                   out = j < R ? __fsub_rn(__fmul_rn(uj, c), __fmul_rn(up, s))
@@ -510,6 +586,10 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
+    }
+    if constexpr (QK) {
+      if (lane == 0) bulk_wait_group0();  // this warp's head stores are complete
+      __syncwarp();
     }
   }
 
@@ -529,7 +609,8 @@ __global__ void __launch_bounds__(192, 1)
 
 template <int KIND, int BN, bool QK, bool PAIR>
 static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
-                            const GemmArgs& g, int grid, cudaStream_t stream) {
+                            const CUtensorMap& to, const GemmArgs& g, int grid,
+                            cudaStream_t stream) {
   using Cfg = GemmCfg<BN, QK, PAIR>;
   auto kern = gemm_tc_kernel<KIND, BN, QK, PAIR>;
   static std::atomic<long long> shape[kMaxLaunchDevices];
@@ -551,7 +632,7 @@ static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tbh, g);
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tbh, to, g);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -559,15 +640,16 @@ static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const 
 int gemm_block_n(const GemmArgs& g) { return g.N <= 128 ? 128 : 256; }
 
 cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
-                        const GemmArgs& g, int bn, int grid, bool pair, cudaStream_t stream) {
+                        const CUtensorMap& to, const GemmArgs& g, int bn, int grid, bool pair,
+                        cudaStream_t stream) {
   const bool qk = g.epi == EPI_QK;
 #define M5B_KIND_CASE(KIND_)                                                               \
   case KIND_:                                                                              \
-    if (qk) return pair ? launch_k<KIND_, 256, true, true>(ta, tb, tbh, g, grid, stream)   \
-                        : launch_k<KIND_, 128, true, false>(ta, tb, tbh, g, grid, stream); \
-    if (pair) return launch_k<KIND_, 256, false, true>(ta, tb, tbh, g, grid, stream);      \
-    if (bn == 128) return launch_k<KIND_, 128, false, false>(ta, tb, tbh, g, grid, stream); \
-    return launch_k<KIND_, 256, false, false>(ta, tb, tbh, g, grid, stream);
+    if (qk) return pair ? launch_k<KIND_, 256, true, true>(ta, tb, tbh, to, g, grid, stream)   \
+                        : launch_k<KIND_, 128, true, false>(ta, tb, tbh, to, g, grid, stream); \
+    if (pair) return launch_k<KIND_, 256, false, true>(ta, tb, tbh, to, g, grid, stream);      \
+    if (bn == 128) return launch_k<KIND_, 128, false, false>(ta, tb, tbh, to, g, grid, stream); \
+    return launch_k<KIND_, 256, false, false>(ta, tb, tbh, to, g, grid, stream);
   switch (g.kind) {
     M5B_KIND_CASE(KIND_I8)
     M5B_KIND_CASE(KIND_F8)

@@ -125,6 +125,7 @@ struct GemmArgs {
   const void* cos;            // [M, R] bf16 (QK)
   const void* sin;            // [M, R] bf16 (QK)
   int rope_half;
+  int qk_fast;                // QK: rope_half % 8 == 0 and 16-byte aligned tables (vector path)
   float eps;
   int num_m_blocks, num_n_blocks, num_k_blocks;
   int group_m;
@@ -136,8 +137,11 @@ struct GemmArgs {
   unsigned int* status;       // device status word (bounded-wait errors)
 };
 
+// `to`: the Q/K output map (3D {128, M, N/128} bf16, boxes {64, 32, 1}, 128-byte
+// swizzle); ignored by the other epilogues.
 cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb_half,
-                        const GemmArgs& g, int bn, int grid, bool pair, cudaStream_t stream);
+                        const CUtensorMap& to, const GemmArgs& g, int bn, int grid, bool pair,
+                        cudaStream_t stream);
 int gemm_block_n(const GemmArgs& g);
 
 }  // namespace m5b
