@@ -83,6 +83,58 @@ __device__ __forceinline__ float int8_code_near_tie(float x, float s, float t, f
   return fminf(fmaxf(q, -127.0f), 127.0f);
 }
 
+// Bracketed INT8 rounding of packed pairs (sm_100 FFMA2).  With
+// inv = RN(1/s), inv_hi = RN(inv (1 + 2^-21)) and inv_lo = RN(inv (1 - 2^-21)),
+// x*inv_hi and x*inv_lo (exact products inside the FMA) bracket RN(x/s) for
+// every x: the three rounding errors are at most 2^-24 each (2^-22.4 together),
+// inside the 2^-21 margin.  Adding 1.5*2^23 in the same FMA rounds each bracket end to
+// the nearest integer, ties to even (the constant is even), so the low byte
+// of the result is the two's-complement int8 of rint(end).  rint is monotone,
+// so when both ends give the same integer it is rint(RN(x/s)), the
+// reference's code; `acc` collects the bits where the ends differ, and a
+// nonzero acc sends the group to an exact path.  |x| <= 127.0001 s keeps the
+// ends inside +-127.5, so no clipping is needed.  Requires s >= 2^-100.
+struct I8Bracket {
+  float2 lo, hi;
+};
+// A power-of-two scale has an exact reciprocal: x*inv is then x/s itself and
+// one end suffices (both ends equal, acc stays zero).  Such scales are the
+// ones under which 16-bit inputs land exactly on half-integers (a row peak
+// of 127 * 2^e), so without this shortcut those rows would take the exact
+// path element by element.
+__device__ __forceinline__ I8Bracket i8_bracket(float inv, float scale) {
+  if ((__float_as_uint(scale) & 0x007FFFFFu) == 0u)
+    return I8Bracket{make_float2(inv, inv), make_float2(inv, inv)};
+  const float lo = __fmul_rn(inv, 1.0f - 0x1p-21f), hi = __fmul_rn(inv, 1.0f + 0x1p-21f);
+  return I8Bracket{make_float2(lo, lo), make_float2(hi, hi)};
+}
+// Codes of one pair in the low bytes of the returned words' bit patterns.
+__device__ __forceinline__ float2 i8_pair(float2 v, const I8Bracket& b, uint32_t& acc) {
+  const float2 mag = make_float2(12582912.0f, 12582912.0f);
+  const float2 h = __ffma2_rn(v, b.hi, mag);
+  const float2 l = __ffma2_rn(v, b.lo, mag);
+  acc |= (__float_as_uint(h.x) ^ __float_as_uint(l.x)) | (__float_as_uint(h.y) ^ __float_as_uint(l.y));
+  return h;
+}
+// Four int8 codes (low bytes of a, b, c, d) packed into one word.
+__device__ __forceinline__ uint32_t pack4_low_bytes(float a, float b, float c, float d) {
+  return __byte_perm(__byte_perm(__float_as_uint(a), __float_as_uint(b), 0x0040),
+                     __byte_perm(__float_as_uint(c), __float_as_uint(d), 0x0040), 0x5410);
+}
+
+// max(|a|, |b|) lane-wise on packed 16-bit floats, one instruction; the sign
+// bit of the result is garbage (the xor of the inputs' signs).
+__device__ __forceinline__ uint32_t max_xorsign_abs_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t max_xorsign_abs_f16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // OCP E4M3 code with round-to-nearest-even and saturation to +-448.
 __device__ __forceinline__ uint8_t e4m3_code(float v, float scale) {
   float z = __fdiv_rn(v, scale);
@@ -173,6 +225,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Tiled TMA load of a 3D box into shared memory, completion on an mbarrier.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
 }
 
 // Tiled TMA store of a 3D box from shared memory (bulk-group completion).

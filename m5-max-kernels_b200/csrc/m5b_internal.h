@@ -93,7 +93,8 @@ int set_last_error(int code, const char* msg);
 
 int row_prep_warps(int64_t K, int block);
 bool quant_rows_applicable(const RowPrepArgs& a, int x_dtype, int block, int out);
-cudaError_t launch_quant_rows(const RowPrepArgs& a, int x_dtype, int out, cudaStream_t stream);
+cudaError_t launch_quant_rows(const RowPrepArgs& a, const RowMaps& m, int x_dtype, int out,
+                              cudaStream_t stream);
 cudaError_t launch_row_prep(const RowPrepArgs& a, const RowMaps& maps, int x_dtype, int block,
                             int out, cudaStream_t stream);
 

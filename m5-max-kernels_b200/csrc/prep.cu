@@ -25,7 +25,7 @@ cudaError_t launch_row_prep(const RowPrepArgs& a, const RowMaps& m, int x_dtype,
                             int out, cudaStream_t stream) {
   // Plain per-token quantization needs no register-resident row: two
   // streaming passes (quant.cu) keep many more rows in flight per SM.
-  if (quant_rows_applicable(a, x_dtype, block, out)) return launch_quant_rows(a, x_dtype, out, stream);
+  if (quant_rows_applicable(a, x_dtype, block, out)) return launch_quant_rows(a, m, x_dtype, out, stream);
   switch (x_dtype) {
     case DT_BF16: return launch_row_prep_bf16(a, m, block, out, stream);
     case DT_F16: return launch_row_prep_f16(a, m, block, out, stream);

@@ -61,6 +61,8 @@ __device__ __forceinline__ int quant_i8(float v, float scale, float inv, bool fa
 __device__ __forceinline__ uint32_t quant_e4m3(float v, float scale, float inv, bool fast) {
   if (fast) {
     const float t = __fmul_rn(v, inv);
+    if ((__float_as_uint(scale) & 0x007FFFFFu) == 0u)  // exact reciprocal: t == v / scale
+      return static_cast<uint32_t>(__nv_cvt_float_to_fp8(t, __NV_SATFINITE, __NV_E4M3));
     const __nv_fp8x2_storage_t two = __nv_cvt_float2_to_fp8x2(
         make_float2(__fmul_rn(t, 1.0f - 0x1p-18f), __fmul_rn(t, 1.0f + 0x1p-18f)), __NV_SATFINITE,
         __NV_E4M3);
@@ -100,35 +102,21 @@ static __device__ __noinline__ uint4 quant_i8_near_tie16(Vals16 in, float scale,
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// Quantize 16 values to int8 codes packed four per word, on sm_100 packed
-// FP32 arithmetic (each lane an IEEE binary32 op): t = x * inv, m = t +
-// 1.5*2^23 (RNE to integer, code in the low byte of m), r = m - 1.5*2^23,
-// d = t - r (exact).  A group with some |d| > 0.5 - 2^-14 is redone by
-// quant_i8_near_tie16.  Requires scale >= 2^-100.
+// Quantize 16 values to int8 codes packed four per word by bracketed
+// rounding of packed pairs (i8_pair, common.cuh); a group whose brackets
+// disagree somewhere is redone by quant_i8_near_tie16.  Requires
+// scale >= 2^-100.
 __device__ __forceinline__ void quant_i8_fast16(const float* v, float scale, float inv,
                                                 uint32_t* words) {
-  const float2 inv2 = make_float2(inv, inv);
-  const float2 mag2 = make_float2(kRoundMagic, kRoundMagic);
-  const float2 nmag2 = make_float2(-kRoundMagic, -kRoundMagic);
-  const float2 neg1 = make_float2(-1.0f, -1.0f);
-  float dmax = 0.0f;
+  const I8Bracket br = i8_bracket(inv, scale);
+  uint32_t acc = 0u;
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
-    uint32_t u[4];
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const float2 t = __fmul2_rn(make_float2(v[4 * w + 2 * p], v[4 * w + 2 * p + 1]), inv2);
-      const float2 m = __fadd2_rn(t, mag2);
-      const float2 r = __fadd2_rn(m, nmag2);
-      const float2 d = __ffma2_rn(r, neg1, t);
-      dmax = fmaxf(dmax, fmaxf(fabsf(d.x), fabsf(d.y)));
-      u[2 * p] = __float_as_uint(m.x);
-      u[2 * p + 1] = __float_as_uint(m.y);
-    }
-    words[w] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040),
-                           0x5410);
+    const float2 m0 = i8_pair(make_float2(v[4 * w], v[4 * w + 1]), br, acc);
+    const float2 m1 = i8_pair(make_float2(v[4 * w + 2], v[4 * w + 3]), br, acc);
+    words[w] = pack4_low_bytes(m0.x, m0.y, m1.x, m1.y);
   }
-  if (dmax > 0.5f - 0x1p-14f) {
+  if (acc != 0u) {
     const Vals16 in{make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]),
                     make_float4(v[8], v[9], v[10], v[11]),
                     make_float4(v[12], v[13], v[14], v[15])};
@@ -253,14 +241,6 @@ __device__ __forceinline__ float cta_max(float v, float* red, int W) {
 // with the 128-byte swizzle, so 16-byte slot i of box row r sits at physical
 // slot i ^ (r & 7): threads that read their own chunk slot by slot hit eight
 // different bank groups.
-__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
-                                            int32_t x, int32_t y, int32_t z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
 
 // 16-byte slot `slot` (0..7 within the chunk's 128-byte box row `br`) of a
 // swizzled row buffer.

@@ -24,24 +24,45 @@ namespace m5b {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kTieQueue = 64;  // queued near-tie vectors per warp and row
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: RNE to integer for |t| < 2^22
 
+// Running row peak max|x|.  16-bit inputs stay packed: one
+// max.xorsign.abs per pair of words (the magnitudes are exact, the sign bits
+// are cleared at the end); fp32 inputs use FMNMX with |.|.
 template <typename T>
-__device__ __forceinline__ float vec_absmax(const uint4& raw) {
-  if constexpr (sizeof(T) == 2) {
-    // |x| of a 16-bit float is its bit pattern with the sign cleared, and for
-    // finite values that pattern orders like the value: integer max suffices.
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(&raw);
-    uint32_t m = __vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu);
-    m = __vmaxu2(m, __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
-    const uint32_t hi = m >> 16, lo = m & 0xFFFFu;
-    const uint16_t best = static_cast<uint16_t>(hi > lo ? hi : lo);
-    return to_f32(*reinterpret_cast<const T*>(&best));
-  } else {
-    const float* f = reinterpret_cast<const float*>(&raw);
-    return fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
+struct Peak {
+  uint32_t h = 0u;
+  float f = 0.0f;
+  __device__ __forceinline__ void add(const uint4& raw) {
+    if constexpr (sizeof(T) == 2) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        h = max_xorsign_abs_bf16x2(
+            h, max_xorsign_abs_bf16x2(max_xorsign_abs_bf16x2(raw.x, raw.y),
+                                      max_xorsign_abs_bf16x2(raw.z, raw.w)));
+      } else {
+        h = max_xorsign_abs_f16x2(
+            h, max_xorsign_abs_f16x2(max_xorsign_abs_f16x2(raw.x, raw.y),
+                                     max_xorsign_abs_f16x2(raw.z, raw.w)));
+      }
+    } else {
+      f = fmaxf(f, fmaxf(fmaxf(fabsf(__uint_as_float(raw.x)), fabsf(__uint_as_float(raw.y))),
+                         fmaxf(fabsf(__uint_as_float(raw.z)), fabsf(__uint_as_float(raw.w)))));
+    }
   }
-}
+  __device__ __forceinline__ float value() const {
+    if constexpr (sizeof(T) == 2) {
+      // |x| of a 16-bit float is its bit pattern with the sign cleared, and for
+      // finite values that pattern orders like the value.
+      const uint32_t m = h & 0x7FFF7FFFu;
+      const uint32_t hi = m >> 16, lo = m & 0xFFFFu;
+      const uint16_t best = static_cast<uint16_t>(hi > lo ? hi : lo);
+      return to_f32(*reinterpret_cast<const T*>(&best));
+    } else {
+      return f;
+    }
+  }
+};
 
 // Elements per 16-byte vector.
 template <typename T>
@@ -61,20 +82,16 @@ __device__ __forceinline__ void unpack(const uint4& raw, float* out) {
 }
 
 // INT8 codes of one 16-byte vector (8 bf16/fp16 or 4 fp32 values) packed
-// into words, on sm_100 packed-FP32 arithmetic (each lane an IEEE binary32
-// op).  Per pair: t = x * inv, m = t + 1.5*2^23 (RNE to integer, code in the
-// low byte of m), r = m - 1.5*2^23, d = t - r (both exact).  Returns max |d|;
-// max |d| > 0.5 - 2^-14 flags a product next to a half-integer, whose vector
-// is then redone by i8_words_near_tie.
+// into words by bracketed rounding of packed pairs (i8_pair).  Returns the
+// bracket disagreement bits: nonzero means some element may round
+// differently from the reference, and the vector is redone by
+// i8_words_near_tie.
 template <typename T>
-__device__ __forceinline__ float pack_i8_vec(const uint4& raw, float inv, uint32_t* words) {
-  const float2 inv2 = make_float2(inv, inv);
-  const float2 mag2 = make_float2(kMagic, kMagic);
-  const float2 nmag2 = make_float2(-kMagic, -kMagic);
-  const float2 neg1 = make_float2(-1.0f, -1.0f);
-  float dmax = 0.0f;
+__device__ __forceinline__ uint32_t pack_i8_vec(const uint4& raw, const I8Bracket& br,
+                                                uint32_t* words) {
   constexpr int PAIRS = sizeof(T) == 2 ? 4 : 2;
-  uint32_t u[2 * PAIRS];
+  float2 m[PAIRS];
+  uint32_t acc = 0u;
 #pragma unroll
   for (int p = 0; p < PAIRS; ++p) {
     float2 v;
@@ -90,19 +107,12 @@ __device__ __forceinline__ float pack_i8_vec(const uint4& raw, float inv, uint32
       v = make_float2(reinterpret_cast<const float*>(&raw)[2 * p],
                       reinterpret_cast<const float*>(&raw)[2 * p + 1]);
     }
-    const float2 t = __fmul2_rn(v, inv2);
-    const float2 m = __fadd2_rn(t, mag2);
-    const float2 r = __fadd2_rn(m, nmag2);
-    const float2 d = __ffma2_rn(r, neg1, t);
-    dmax = fmaxf(dmax, fmaxf(fabsf(d.x), fabsf(d.y)));
-    u[2 * p] = __float_as_uint(m.x);
-    u[2 * p + 1] = __float_as_uint(m.y);
+    m[p] = i8_pair(v, br, acc);
   }
 #pragma unroll
   for (int w = 0; w < PAIRS / 2; ++w)
-    words[w] = __byte_perm(__byte_perm(u[4 * w], u[4 * w + 1], 0x0040),
-                           __byte_perm(u[4 * w + 2], u[4 * w + 3], 0x0040), 0x5410);
-  return dmax;
+    words[w] = pack4_low_bytes(m[2 * w].x, m[2 * w].y, m[2 * w + 1].x, m[2 * w + 1].y);
+  return acc;
 }
 
 // The exact codes of a vector that holds a product next to a half-integer:
@@ -138,6 +148,8 @@ __device__ __forceinline__ uint32_t code_i8_exact(float v, float scale) {
 __device__ __forceinline__ uint32_t code_e4m3(float v, float scale, float inv, bool fast) {
   if (fast) {
     const float t = __fmul_rn(v, inv);
+    if ((__float_as_uint(scale) & 0x007FFFFFu) == 0u)  // exact reciprocal: t == v / scale
+      return static_cast<uint32_t>(__nv_cvt_float_to_fp8(t, __NV_SATFINITE, __NV_E4M3));
     const __nv_fp8x2_storage_t two = __nv_cvt_float2_to_fp8x2(
         make_float2(__fmul_rn(t, 1.0f - 0x1p-18f), __fmul_rn(t, 1.0f + 0x1p-18f)), __NV_SATFINITE,
         __NV_E4M3);
@@ -163,7 +175,7 @@ __device__ __forceinline__ void vec_codes(const uint4& raw, float scale, float i
                  (code_e4m3(v[4 * w + 3], scale, inv, fast) << 24);
   } else {
     if (fast) {
-      if (pack_i8_vec<T>(raw, inv, words) > 0.5f - 0x1p-14f) {
+      if (pack_i8_vec<T>(raw, i8_bracket(inv, scale), words) != 0u) {
         const uint2 w = i8_words_near_tie<T>(raw, scale, inv);
         words[0] = w.x;
         if constexpr (V == 8) words[1] = w.y;
@@ -207,6 +219,9 @@ __global__ void __launch_bounds__(kThreads)
                       float* __restrict__ s) {
   constexpr int V = kVec<T>;
   __shared__ float red[kThreads / 32];
+  __shared__ uint4 tie_raw[kThreads / 32][kTieQueue];
+  __shared__ int tie_idx[kThreads / 32][kTieQueue];
+  __shared__ int tie_n[kThreads / 32];
   const int tid = threadIdx.x;
   const int nvec = static_cast<int>(K / V);  // K % V == 0 on this path
   const float qmax = OUT == OUT_E4M3 ? 448.0f : 127.0f;
@@ -220,36 +235,74 @@ __global__ void __launch_bounds__(kThreads)
         const int j = tid + i * kThreads;
         raw[i] = j < nvec ? __ldg(xr + j) : make_uint4(0, 0, 0, 0);
       }
-      float peak = 0.0f;
+      Peak<T> pk;
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) peak = fmaxf(peak, vec_absmax<T>(raw[i]));
-      peak = cta_peak(peak, red);
+      for (int i = 0; i < VPT; ++i) pk.add(raw[i]);
+      const float peak = cta_peak(pk.value(), red);
       const float scale = peak == 0.0f ? 1.0f : __fdiv_rn(peak, qmax);
       const float inv = __frcp_rn(scale);
       const bool fast = scale >= 0x1p-100f;
       if (tid == 0) s[row] = scale;
+      if (OUT == OUT_INT8 && fast) {
+        // Bracketed codes for every vector; a vector whose brackets disagree
+        // (a quotient next to a half-integer) is queued and redone exactly
+        // after the pass by the whole warp, one queued vector per lane, so
+        // the exact path does not serialise the warp vector by vector.
+        const I8Bracket br = i8_bracket(inv, scale);
+        const int warp = tid >> 5, lane = tid & 31;
+        if (lane == 0) tie_n[warp] = 0;
+        __syncwarp();
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) {
-        const int j = tid + i * kThreads;
-        if (j < nvec) {
-          uint32_t words[V / 4];
-          vec_codes<T, OUT>(raw[i], scale, inv, fast, words);
-          store_codes<T>(qr, j, words);
+        for (int i = 0; i < VPT; ++i) {
+          const int j = tid + i * kThreads;
+          if (j < nvec) {
+            uint32_t words[V / 4];
+            const uint32_t acc = pack_i8_vec<T>(raw[i], br, words);
+            store_codes<T>(qr, j, words);
+            if (acc != 0u) {
+              const int slot = atomicAdd(&tie_n[warp], 1);
+              if (slot < kTieQueue) {
+                tie_raw[warp][slot] = raw[i];
+                tie_idx[warp][slot] = j;
+              } else {  // queue full: redo in place
+                const uint2 w = i8_words_near_tie<T>(raw[i], scale, inv);
+                store_codes<T>(qr, j, reinterpret_cast<const uint32_t*>(&w));
+              }
+            }
+          }
+        }
+        __syncwarp();
+        const int n = min(tie_n[warp], kTieQueue);
+        for (int k = lane; k < n; k += 32) {
+          const uint2 w = i8_words_near_tie<T>(tie_raw[warp][k], scale, inv);
+          store_codes<T>(qr, tie_idx[warp][k], reinterpret_cast<const uint32_t*>(&w));
+        }
+        __syncwarp();
+      } else {
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+          const int j = tid + i * kThreads;
+          if (j < nvec) {
+            uint32_t words[V / 4];
+            vec_codes<T, OUT>(raw[i], scale, inv, fast, words);
+            store_codes<T>(qr, j, words);
+          }
         }
       }
     } else {
-      float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f, p3 = 0.0f;
+      Peak<T> p0, p1, p2, p3;
       int j = tid;
       for (; j + 3 * kThreads < nvec; j += 4 * kThreads) {
         const uint4 a = __ldg(xr + j), b = __ldg(xr + j + kThreads);
         const uint4 c = __ldg(xr + j + 2 * kThreads), d = __ldg(xr + j + 3 * kThreads);
-        p0 = fmaxf(p0, vec_absmax<T>(a));
-        p1 = fmaxf(p1, vec_absmax<T>(b));
-        p2 = fmaxf(p2, vec_absmax<T>(c));
-        p3 = fmaxf(p3, vec_absmax<T>(d));
+        p0.add(a);
+        p1.add(b);
+        p2.add(c);
+        p3.add(d);
       }
-      for (; j < nvec; j += kThreads) p0 = fmaxf(p0, vec_absmax<T>(__ldg(xr + j)));
-      const float peak = cta_peak(fmaxf(fmaxf(p0, p1), fmaxf(p2, p3)), red);
+      for (; j < nvec; j += kThreads) p0.add(__ldg(xr + j));
+      const float peak =
+          cta_peak(fmaxf(fmaxf(p0.value(), p1.value()), fmaxf(p2.value(), p3.value())), red);
       const float scale = peak == 0.0f ? 1.0f : __fdiv_rn(peak, qmax);
       const float inv = __frcp_rn(scale);
       const bool fast = scale >= 0x1p-100f;
@@ -301,7 +354,8 @@ bool quant_rows_applicable(const RowPrepArgs& a, int x_dtype, int block, int out
   return (a.K % vec) == 0 && (xa % 16) == 0 && (qa % vec) == 0;
 }
 
-cudaError_t launch_quant_rows(const RowPrepArgs& a, int x_dtype, int out, cudaStream_t stream) {
+cudaError_t launch_quant_rows(const RowPrepArgs& a, const RowMaps& /*m*/, int x_dtype, int out,
+                              cudaStream_t stream) {
   const bool e4 = out == OUT_E4M3;
   switch (x_dtype) {
     case DT_BF16:
