@@ -248,12 +248,12 @@ def run_secondary(args, world, rank, local):
     SETS = 2
     sets = [make_set() for _ in range(SETS)]
     if args.workload == "prep_c3":
-        nbytes, unit, kernel = 4096 * (3 * 16384 + 4), "GB/s", "rotq_kernel<bf16,128,int8>"
+        nbytes, unit, kernel = 4096 * (3 * 16384 + 4), "GB/s", "lean_kernel<bf16,128,int8,plain>"
     elif args.workload == "prep_c4":
-        nbytes, unit, kernel = 4096 * (7 * 4096 + 4), "GB/s", "row_prep_kernel<bf16,128,int8> (gated)"
+        nbytes, unit, kernel = 4096 * (7 * 4096 + 4), "GB/s", "lean_kernel<bf16,128,int8,norm_gated>"
     else:
         nbytes, unit = 2.0 * 9914 * 4096 * 4096, "TOPS"
-        kernel = "rotq_kernel<bf16,256,int8> + gemm_tc_kernel<i8,256,qk,pair>"
+        kernel = "lean_kernel<bf16,256,int8,plain> + gemm_tc_kernel<i8,256,qk,pair>"
 
     def graph_ms(fns):
         for _ in range(args.warmup):

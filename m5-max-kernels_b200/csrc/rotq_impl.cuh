@@ -1,29 +1,31 @@
-// Rotation + per-token quantization of plain rows: the online activation
-// prep of the rotated W8A8 / FP8 projection (no normalization, no gated
-// residual), and the FP32 rotation alone.
+// Lean row-preparation kernels for the common shapes: rotation (+ per-token
+// quantization) of plain rows, and the fused RMS / LayerNorm + AdaLN
+// modulation (+ gated residual) + rotation + quantization.
 //
 // Reference contracts: src/m5kernels/hadamard.py:33-77 (rotate: X D H with
 // the signs applied before the Sylvester-order Walsh-Hadamard transform of
 // each block of B channels, scaled by 1/sqrt(B)), hadamard_gemm.py:65-66
-// (quantize(rotate(x))), numerics.py:29-46 (per-token symmetric INT8 / E4M3).
+// (quantize(rotate(x))), numerics.py:29-46 (per-token symmetric INT8 / E4M3),
+// norm_hadamard.py:122-176 and 198-265 (fused norm / gated residual forms).
 //
-// This is the lean form of row_prep_kernel (prep_impl.cuh) for the common
-// case; the results are identical bit for bit (same butterfly order, same
+// These are lean forms of row_prep_kernel (prep_impl.cuh); the results are
+// identical bit for bit (same reduction tree, same butterfly order, same
 // rounding of every operation), only the schedule differs:
-//   * 256-thread CTAs, two per SM, split into independent pipeline units of
-//     max(K/64, 32) threads (one thread per 64-element chunk, as in
-//     row_prep_kernel): a unit of K = 4096 is two warps on one row, a unit of
-//     K = 1024 is one warp on two rows.  Each unit has its own ring of row
-//     slots in shared memory filled by TMA (its first thread issues, one
-//     mbarrier per slot) and synchronises with a named barrier (or
-//     __syncwarp), so the units of a CTA never wait for one another.
+//   * CTAs split into independent pipeline units of max(K/64, 32) threads
+//     (one thread per 64-element chunk, as in row_prep_kernel): a unit of
+//     K = 4096 is two warps on one row, a unit of K = 1024 is one warp on two
+//     rows.  Each unit has its own ring of row slots in shared memory filled
+//     by TMA (its first thread issues, one mbarrier per slot) and
+//     synchronises with a named barrier (or __syncwarp), so the units of a
+//     CTA never wait for one another.
 //   * Chunk values are held as 32 float2 pairs (elements 2k, 2k+1) so that
-//     every Hadamard stage of stride >= 2, the 1/sqrt(B) scale and the INT8
-//     rounding run on sm_100 packed FP32 instructions (two IEEE binary32
-//     operations per instruction); cross-lane stages exchange values with
-//     shuffles and combine with one packed FMA by +-1.
-//   * Only this path's code is in the kernel (no norm, modulation or gate
-//     branches), which keeps its instruction footprint small.
+//     the chunk sums, the modulation, the gated update, every Hadamard stage
+//     of stride >= 2, the 1/sqrt(B) scale and the INT8 rounding run on sm_100
+//     packed FP32 instructions (two IEEE binary32 operations per
+//     instruction); cross-lane stages exchange values with shuffles and
+//     combine with one packed FMA by +-1.
+//   * Each mode (plain, norm, gated norm) is its own instantiation, which
+//     keeps the instruction footprint small.
 #pragma once
 #include <type_traits>
 
@@ -35,6 +37,7 @@ namespace rotq {
 constexpr int kThreads = 256;
 constexpr int kMaxStages = 4;
 constexpr int kMaxUnits = kThreads / 32;
+enum Mode : int { kPlain = 0, kNorm = 1, kNormGated = 2 };
 
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 
@@ -103,19 +106,106 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Eight elements [8 i, 8 i + 8) of chunk t of a swizzled staged row.
+template <typename T>
+__device__ __forceinline__ void load8(const uint8_t* base, int t, int i, float2* out) {
+  if constexpr (sizeof(T) == 2) {
+    const uint4 raw = *swz_slot(base, t, i);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value)
+        out[p] = make_float2(__uint_as_float(w[p] << 16), __uint_as_float(w[p] & 0xFFFF0000u));
+      else
+        out[p] = __half22float2(*reinterpret_cast<const __half2*>(&w[p]));
+    }
+  } else {
+    const int br = 2 * t + (i >= 4 ? 1 : 0);
+    const int sl = (i % 4) * 2;
+    const uint4 p = *swz_slot(base, br, sl);
+    const uint4 q = *swz_slot(base, br, sl + 1);
+    out[0] = make_float2(__uint_as_float(p.x), __uint_as_float(p.y));
+    out[1] = make_float2(__uint_as_float(p.z), __uint_as_float(p.w));
+    out[2] = make_float2(__uint_as_float(q.x), __uint_as_float(q.y));
+    out[3] = make_float2(__uint_as_float(q.z), __uint_as_float(q.w));
+  }
+}
+
+// Round a pair through T (RNE) and back.
+template <typename T>
+__device__ __forceinline__ float2 round2(float2 y) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    return __bfloat1622float2(__float22bfloat162_rn(y));
+  else if constexpr (std::is_same<T, __half>::value)
+    return __half22float2(__float22half2_rn(y));
+  else
+    return y;
+}
+
+// Store 8 values (already representable in T) at dst.
+template <typename T>
+__device__ __forceinline__ void store8(T* dst, const float2* v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 h[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) h[p] = __float22bfloat162_rn(v[p]);
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(h);
+  } else if constexpr (std::is_same<T, __half>::value) {
+    __half2 h[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) h[p] = __float22half2_rn(v[p]);
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(h);
+  } else {
+    reinterpret_cast<float4*>(dst)[0] = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
+    reinterpret_cast<float4*>(dst)[1] = make_float4(v[2].x, v[2].y, v[3].x, v[3].y);
+  }
+}
+
+// Canonical chunk sum on pairs: accumulators a[e] (element e mod 8) held as
+// four packed pairs, elements added in index order, combined
+// ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)).  KIND 0: v, 1: v*v, 2: (v-mean)^2.
+template <int KIND>
+__device__ __forceinline__ float chunk_sum2(const float2* v, float mean) {
+  float2 A[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) A[p] = f2(0.0f);
+  const float2 nm = f2(-mean);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float2 x = v[4 * q + p];
+      if constexpr (KIND == 0) {
+        A[p] = __fadd2_rn(A[p], x);
+      } else if constexpr (KIND == 1) {
+        A[p] = __ffma2_rn(x, x, A[p]);
+      } else {
+        const float2 d = __fadd2_rn(x, nm);
+        A[p] = __ffma2_rn(d, d, A[p]);
+      }
+    }
+  }
+  return __fadd_rn(__fadd_rn(__fadd_rn(A[0].x, A[0].y), __fadd_rn(A[1].x, A[1].y)),
+                   __fadd_rn(__fadd_rn(A[2].x, A[2].y), __fadd_rn(A[3].x, A[3].y)));
+}
+
 // Pipeline units: a unit is max(K/64, 32) threads working on RPU = unit / (K/64)
 // rows at a time, with its own ring of `stages` slots and mbarriers, so the
 // units of a CTA never wait for one another (a named barrier, or __syncwarp
 // for one-warp units, synchronises a unit).
-template <typename T, int B, int OUT>
+template <typename T, int B, int OUT, int MODE>
 __global__ void __launch_bounds__(kThreads, 2)
-    rotq_kernel(const __grid_constant__ CUtensorMap map_x, const RowPrepArgs a, const int tpr,
-                const int stages, const int box_rows, const int64_t buf_stride) {
+    lean_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_b,
+                const RowPrepArgs a, const int tpr, const int stages, const int box_rows,
+                const int64_t buf_stride) {
   constexpr int LANE_SPAN = B / kChunk;  // lanes per Hadamard block (B >= 64)
+  constexpr int INPUTS = MODE == kNormGated ? 2 : 1;
   extern __shared__ uint8_t dsmem_raw[];
   uint8_t* dsmem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   __shared__ float red[kThreads / 32];
+  __shared__ float red_sum[kThreads / 32];
+  __shared__ float red_var[kThreads / 32];
   __shared__ __align__(8) uint64_t full_bar[kMaxUnits * kMaxStages];
   __shared__ int abort_flag[kMaxUnits];
 
@@ -134,7 +224,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int64_t row_bytes = K * int64_t(sizeof(T));
   const int row_box_rows = static_cast<int>(row_bytes / 128);
   const int64_t steps_total = (a.rows + RPU - 1) / RPU;  // row groups of RPU rows
-  const int64_t slot_bytes = int64_t(RPU) * buf_stride;
+  const int64_t row_slot = int64_t(INPUTS) * buf_stride;  // one row's inputs
+  const int64_t slot_bytes = int64_t(RPU) * row_slot;
   uint8_t* ring = dsmem + int64_t(u) * stages * slot_bytes;
   uint64_t* bars = full_bar + u * kMaxStages;
   const int64_t first_step = int64_t(blockIdx.x) * U + u;
@@ -144,6 +235,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncwarp();
     else
       named_sync(1 + u, PW);
+  };
+  // Canonical row sum: lanes as a pairwise tree over chunk index, then the
+  // unit's warps pairwise in index order.  Also a unit barrier.
+  auto unit_sum = [&](float v, float* buf) -> float {
+    const int span = tpr < 32 ? tpr : 32;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1)
+      if (off < span) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (tpr > 32 && lane == 0) buf[tid >> 5] = v;
+    unit_sync();
+    if (tpr > 32) {
+      const int w0 = (u * PW) >> 5, W = PW >> 5;
+      float part[kThreads / 32];
+#pragma unroll
+      for (int w = 0; w < kThreads / 32; ++w) part[w] = w < W ? buf[w0 + w] : 0.0f;
+#pragma unroll
+      for (int step = 1; step < kThreads / 32; step <<= 1)
+#pragma unroll
+        for (int w = 0; w + step < kThreads / 32; w += 2 * step)
+          part[w] = __fadd_rn(part[w], part[w + step]);
+      v = part[0];
+    }
+    return v;
   };
 
   if (tid == 0) {
@@ -158,11 +272,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int64_t first = st * RPU;
     const int n = static_cast<int>(a.rows - first < RPU ? a.rows - first : RPU);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_arrive_expect_tx(&bars[s], static_cast<uint32_t>(n * row_bytes));
+    mbar_arrive_expect_tx(&bars[s], static_cast<uint32_t>(n * INPUTS * row_bytes));
     for (int r = 0; r < n; ++r)
-      for (int c = 0; c < row_box_rows; c += box_rows)
-        tma_load_3d(dst + r * buf_stride + c * 128, &map_x, &bars[s], 0, c,
+      for (int c = 0; c < row_box_rows; c += box_rows) {
+        tma_load_3d(dst + r * row_slot + c * 128, &map_x, &bars[s], 0, c,
                     static_cast<int32_t>(first + r));
+        if constexpr (MODE == kNormGated)
+          tma_load_3d(dst + r * row_slot + buf_stride + c * 128, &map_b, &bars[s], 0, c,
+                      static_cast<int32_t>(first + r));
+      }
   };
   if (leader) {
     for (int s = 0; s < stages; ++s) {
@@ -182,14 +300,96 @@ __global__ void __launch_bounds__(kThreads, 2)
     (void)mbar_try_wait(&bars[s], parity);  // acquire of the TMA writes for every thread
     const int64_t row = st * RPU + rr;
     const bool live = row < a.rows;
+    const uint8_t* xslot = ring + s * slot_bytes + rr * row_slot;
+    auto refill = [&]() {
+      if (leader && st + int64_t(stages) * step_stride < steps_total)
+        issue(st + int64_t(stages) * step_stride, s);
+    };
 
     float2 v[32];
-    if (live) {
-      load_chunk<T>(ring + s * slot_bytes + rr * buf_stride, t,
-                    a.signs != nullptr ? a.signs + j0 : nullptr, v);
-    } else {
+    if constexpr (MODE == kPlain) {
+      if (live) {
+        load_chunk<T>(xslot, t, a.signs != nullptr ? a.signs + j0 : nullptr, v);
+      } else {
 #pragma unroll
-      for (int k = 0; k < 32; ++k) v[k] = f2(0.0f);
+        for (int k = 0; k < 32; ++k) v[k] = f2(0.0f);
+      }
+    } else {
+      if (live) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) load8<T>(xslot, t, i, v + 4 * i);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] = f2(0.0f);
+      }
+      if constexpr (MODE == kNormGated) {
+        // R' = cast_T(R + branch * gate), written once.
+        if (live) {
+          const int64_t goff = a.gate_row_map ? int64_t(a.gate_row_map[row]) * K : 0;
+          T* rrow = reinterpret_cast<T*>(a.r_out) + row * K + j0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float2 br[4];
+            float g[8];
+            load8<T>(xslot + buf_stride, t, i, br);
+            param8(a.gate, a.gate_dtype, goff + j0 + 8 * i, true, g);
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+              v[4 * i + p] = round2<T>(__ffma2_rn(br[p], make_float2(g[2 * p], g[2 * p + 1]),
+                                                  v[4 * i + p]));
+            store8<T>(rrow + 8 * i, v + 4 * i);
+          }
+        }
+      }
+      // ---- normalization statistics (canonical tree) -----------------------
+      const float kf = static_cast<float>(K);
+      const float first = __fdiv_rn(
+          unit_sum(a.norm == NORM_LAYER ? chunk_sum2<0>(v, 0.0f) : chunk_sum2<1>(v, 0.0f), red_sum),
+          kf);
+      refill();  // every thread of the unit has read slot s
+      float mean = 0.0f, moment = first;
+      if (a.norm == NORM_LAYER) {
+        mean = first;
+        moment = __fdiv_rn(unit_sum(chunk_sum2<2>(v, mean), red_var), kf);
+      }
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(moment, a.eps)));
+      // ---- modulation, optional rounding, signs ------------------------------
+      if (live) {
+        const int64_t moff = a.row_map ? int64_t(a.row_map[row]) * K : 0;
+        const float2 nm = f2(-mean), inv2 = f2(inv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float g[8], sc[8], sh[8];
+          param8(a.gamma, a.gamma_dtype, j0 + 8 * i, true, g);
+          param8(a.scale, a.scale_dtype, moff + j0 + 8 * i, true, sc);
+          param8(a.shift, a.shift_dtype, moff + j0 + 8 * i, true, sh);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const float2 tq = __fmul2_rn(__fmul2_rn(__fadd2_rn(v[4 * i + p], nm), inv2),
+                                         make_float2(g[2 * p], g[2 * p + 1]));
+            const float2 one_sc = __fadd2_rn(f2(1.0f), make_float2(sc[2 * p], sc[2 * p + 1]));
+            float2 y = __ffma2_rn(tq, one_sc, make_float2(sh[2 * p], sh[2 * p + 1]));
+            if (a.round_output) y = round2<T>(y);
+            v[4 * i + p] = y;
+          }
+        }
+        if (a.signs != nullptr) {
+#pragma unroll
+          for (int i = 0; i < kChunk; i += 16) {
+            const uint4 sv = __ldg(reinterpret_cast<const uint4*>(a.signs + j0 + i));
+            const uint32_t w[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float2& p0 = v[(i + 4 * q) / 2];
+              float2& p1 = v[(i + 4 * q) / 2 + 1];
+              p0.x = __uint_as_float(__float_as_uint(p0.x) ^ ((w[q] << 24) & 0x80000000u));
+              p0.y = __uint_as_float(__float_as_uint(p0.y) ^ ((w[q] << 16) & 0x80000000u));
+              p1.x = __uint_as_float(__float_as_uint(p1.x) ^ ((w[q] << 8) & 0x80000000u));
+              p1.y = __uint_as_float(__float_as_uint(p1.y) ^ (w[q] & 0x80000000u));
+            }
+          }
+        }
+      }
     }
     // ---- Walsh-Hadamard transform of each B block (natural Sylvester order)
 #pragma unroll
@@ -223,8 +423,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     if constexpr (OUT == OUT_F32) {
       unit_sync();  // slot s consumed
-      if (leader && st + int64_t(stages) * step_stride < steps_total)
-        issue(st + int64_t(stages) * step_stride, s);
+      if constexpr (MODE == kPlain) refill();
       if (live) {
         float4* y = reinterpret_cast<float4*>(a.y + row * K + j0);
 #pragma unroll
@@ -240,9 +439,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int off = 16; off > 0; off >>= 1)
         if (off < span) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
       if (tpr > 32 && lane == 0) red[tid >> 5] = m;
-      unit_sync();  // slot s consumed; warp peaks visible
-      if (leader && st + int64_t(stages) * step_stride < steps_total)
-        issue(st + int64_t(stages) * step_stride, s);
+      unit_sync();  // warp peaks visible (plain mode: slot s consumed)
+      if constexpr (MODE == kPlain) refill();
       if (tpr > 32) {
         const int w0 = (u * PW) >> 5;
         m = red[w0];
@@ -312,36 +510,56 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-// The lean kernel takes rows without normalization or gate, rotated with
-// B >= 64, staged by TMA (16-byte aligned, K % 64 == 0), with 16-byte aligned
-// signs and outputs, and rows whose chunks tile the 256-thread CTA (K / 64 a
-// power of two below 32, or a multiple of 32 up to 256), and whose row-group
-// slot (rows padded to 1024 bytes for the swizzle) is at most 64 KB.
-inline bool applicable(const RowPrepArgs& a, const RowMaps& m, int block, int elem_bytes) {
-  if (a.norm != NORM_NONE || a.branch != nullptr || block < 64 || !m.valid || !a.vec_ok)
-    return false;
+// The lean kernels take rows staged by TMA (16-byte aligned, K % 64 == 0)
+// with 16-byte aligned outputs, signs and parameter tables, whose chunks
+// tile a unit (K / 64 a power of two below 32, or a multiple of 32 up to
+// 256), rotated with B >= 64 (B <= 256 with normalization).  Plain rows also
+// need a row-group slot (rows padded to 1024 bytes for the swizzle) of at
+// most 64 KB; normalized rows a two-stage ring of at most 200 KB.
+inline int mode_of(const RowPrepArgs& a) {
+  if (a.norm == NORM_NONE) return a.branch ? -1 : kPlain;
+  return a.branch ? kNormGated : kNorm;
+}
+
+inline bool applicable(const RowPrepArgs& a, const RowMaps& m, int block, int out,
+                       int elem_bytes) {
+  const int mode = mode_of(a);
+  if (mode < 0 || block < 64 || !m.valid || !a.vec_ok) return false;
+  if (mode != kPlain && (block > 256 || out == OUT_F32 || !a.params_vec)) return false;
   if (a.signs != nullptr && !a.params_vec) return false;
   if (a.K % kChunk) return false;
   const int64_t tpr = a.K / kChunk;
   if (tpr < 32 ? (32 % tpr) != 0 : (tpr % 32 != 0 || tpr > kThreads)) return false;
   const int64_t buf_stride = (a.K * elem_bytes + 1023) & ~int64_t(1023);
-  return (kThreads / tpr) * buf_stride <= 64 * 1024;
+  const int64_t pw = tpr >= 32 ? tpr : 32;
+  const int64_t unit_slot = (mode == kNormGated ? 2 : 1) * (pw / tpr) * buf_stride;
+  if (mode == kPlain) return (kThreads / pw) * unit_slot <= 64 * 1024;
+  return 2 * unit_slot <= 200 * 1024;
 }
 
-template <typename T, int B, int OUT>
-cudaError_t launch_b(const RowPrepArgs& a, const RowMaps& m, cudaStream_t stream) {
-  auto kern = rotq_kernel<T, B, OUT>;
+template <typename T, int B, int OUT, int MODE>
+cudaError_t launch_m(const RowPrepArgs& a, const RowMaps& m, cudaStream_t stream) {
+  auto kern = lean_kernel<T, B, OUT, MODE>;
   const int tpr = static_cast<int>(a.K / kChunk);
   const int pw = tpr >= 32 ? tpr : 32;  // threads per pipeline unit
-  const int units = kThreads / pw;
-  const int threads = units * pw;
   const int rpu = pw / tpr;
   const int64_t row_bytes = a.K * int64_t(sizeof(T));
   const int64_t buf_stride = (row_bytes + 1023) & ~int64_t(1023);
-  const int64_t slot = int64_t(units) * rpu * buf_stride;  // one slot of every unit
-  int stages = static_cast<int>((110 * 1024) / slot);
-  stages = stages < 2 ? 2 : (stages > 3 ? 3 : stages);
-  const int smem = static_cast<int>(stages * slot) + 1024;
+  const int64_t unit_slot = int64_t(MODE == kNormGated ? 2 : 1) * rpu * buf_stride;
+  int units, stages;
+  if (MODE == kPlain) {
+    units = kThreads / pw;
+    stages = static_cast<int>((110 * 1024) / (units * unit_slot));
+    stages = stages < 2 ? 2 : (stages > 3 ? 3 : stages);
+  } else {
+    // Two stages per unit; as many units per CTA as keep the CTA near
+    // 72 KB, so that three CTAs share an SM where the rows allow it.
+    stages = 2;
+    units = static_cast<int>((72 * 1024) / (stages * unit_slot));
+    units = units < 1 ? 1 : (units > kThreads / pw ? kThreads / pw : units);
+  }
+  const int threads = units * pw;
+  const int smem = static_cast<int>(int64_t(stages) * units * unit_slot) + 1024;
   static std::atomic<long long> shape[kMaxLaunchDevices];
   int dev = 0, sms = 0, per_sm = 0;
   cudaError_t e = launch_shape(reinterpret_cast<const void*>(kern), threads, smem, shape, &dev,
@@ -351,19 +569,38 @@ cudaError_t launch_b(const RowPrepArgs& a, const RowMaps& m, cudaStream_t stream
   const int64_t ctas_needed = (unit_steps + units - 1) / units;
   int64_t grid = int64_t(sms) * per_sm;
   if (grid > ctas_needed) grid = ctas_needed;
-  kern<<<static_cast<unsigned>(grid), threads, smem, stream>>>(m.x, a, tpr, stages, m.box_rows,
-                                                               buf_stride);
+  kern<<<static_cast<unsigned>(grid), threads, smem, stream>>>(
+      m.x, MODE == kNormGated ? m.b : m.x, a, tpr, stages, m.box_rows, buf_stride);
   return cudaGetLastError();
 }
 
-template <typename T, int OUT>
-cudaError_t launch_o(const RowPrepArgs& a, const RowMaps& m, int block, cudaStream_t stream) {
+template <typename T, int MODE, int OUT>
+cudaError_t launch_bo(const RowPrepArgs& a, const RowMaps& m, int block, cudaStream_t stream) {
   switch (block) {
-    case 64: return launch_b<T, 64, OUT>(a, m, stream);
-    case 128: return launch_b<T, 128, OUT>(a, m, stream);
-    case 256: return launch_b<T, 256, OUT>(a, m, stream);
-    case 512: return launch_b<T, 512, OUT>(a, m, stream);
-    case 1024: return launch_b<T, 1024, OUT>(a, m, stream);
+    case 64: return launch_m<T, 64, OUT, MODE>(a, m, stream);
+    case 128: return launch_m<T, 128, OUT, MODE>(a, m, stream);
+    case 256: return launch_m<T, 256, OUT, MODE>(a, m, stream);
+    default: break;
+  }
+  if constexpr (MODE == kPlain) {
+    switch (block) {
+      case 512: return launch_m<T, 512, OUT, MODE>(a, m, stream);
+      case 1024: return launch_m<T, 1024, OUT, MODE>(a, m, stream);
+      default: break;
+    }
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <typename T, int MODE>
+cudaError_t launch_mode(const RowPrepArgs& a, const RowMaps& m, int block, int out,
+                        cudaStream_t stream) {
+  switch (out) {
+    case OUT_INT8: return launch_bo<T, MODE, OUT_INT8>(a, m, block, stream);
+    case OUT_E4M3: return launch_bo<T, MODE, OUT_E4M3>(a, m, block, stream);
+    case OUT_F32:
+      if constexpr (MODE == kPlain) return launch_bo<T, MODE, OUT_F32>(a, m, block, stream);
+      return cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }
@@ -371,10 +608,10 @@ cudaError_t launch_o(const RowPrepArgs& a, const RowMaps& m, int block, cudaStre
 template <typename T>
 cudaError_t launch(const RowPrepArgs& a, const RowMaps& m, int block, int out,
                    cudaStream_t stream) {
-  switch (out) {
-    case OUT_INT8: return launch_o<T, OUT_INT8>(a, m, block, stream);
-    case OUT_E4M3: return launch_o<T, OUT_E4M3>(a, m, block, stream);
-    case OUT_F32: return launch_o<T, OUT_F32>(a, m, block, stream);
+  switch (mode_of(a)) {
+    case kPlain: return launch_mode<T, kPlain>(a, m, block, out, stream);
+    case kNorm: return launch_mode<T, kNorm>(a, m, block, out, stream);
+    case kNormGated: return launch_mode<T, kNormGated>(a, m, block, out, stream);
     default: return cudaErrorInvalidValue;
   }
 }
