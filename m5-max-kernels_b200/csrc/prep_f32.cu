@@ -5,7 +5,7 @@
 namespace m5b {
 cudaError_t launch_row_prep_f32(const RowPrepArgs& a, const RowMaps& m, int block, int out,
                                  cudaStream_t stream) {
-  if (rotq::applicable(a, m, block, out, sizeof(float))) return rotq::launch<float>(a, m, block, out, stream);
+  if (rotq::applicable(a, m, block, out, sizeof(float), DT_F32)) return rotq::launch<float>(a, m, block, out, stream);
   return launch_o<float>(a, m, block, out, stream);
 }
 }  // namespace m5b

@@ -131,6 +131,38 @@ __device__ __forceinline__ void load8(const uint8_t* base, int t, int i, float2*
   }
 }
 
+// Eight values of a parameter table of the input dtype T as raw bits,
+// loaded ahead of their use (the tables are read from L2 / L1 on every row,
+// so the next group's loads are issued before the current group is
+// computed).
+template <typename T>
+struct Raw8 {
+  uint4 w[sizeof(T) == 4 ? 2 : 1];
+};
+template <typename T>
+__device__ __forceinline__ Raw8<T> raw8_load(const void* base, int64_t j) {
+  Raw8<T> r;
+  const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(base) + j);
+  r.w[0] = __ldg(p);
+  if constexpr (sizeof(T) == 4) r.w[1] = __ldg(p + 1);
+  return r;
+}
+// Value pair q (elements 2q, 2q+1) of a Raw8.
+template <typename T>
+__device__ __forceinline__ float2 raw8_pair(const Raw8<T>& r, int q) {
+  if constexpr (sizeof(T) == 4) {
+    const uint4& v = r.w[q >> 1];
+    return (q & 1) ? make_float2(__uint_as_float(v.z), __uint_as_float(v.w))
+                   : make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
+  } else {
+    const uint32_t x = q == 0 ? r.w[0].x : q == 1 ? r.w[0].y : q == 2 ? r.w[0].z : r.w[0].w;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value)
+      return make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xFFFF0000u));
+    else
+      return __half22float2(*reinterpret_cast<const __half2*>(&x));
+  }
+}
+
 // Round a pair through T (RNE) and back.
 template <typename T>
 __device__ __forceinline__ float2 round2(float2 y) {
@@ -327,16 +359,20 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (live) {
           const int64_t goff = a.gate_row_map ? int64_t(a.gate_row_map[row]) * K : 0;
           T* rrow = reinterpret_cast<T*>(a.r_out) + row * K + j0;
+          // 16-bit tables: the next group's gate loads go out before this
+          // group is computed (fp32 tables would not fit the registers).
+          constexpr bool kAhead = sizeof(T) == 2;
+          Raw8<T> gn = raw8_load<T>(a.gate, goff + j0);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
+            const Raw8<T> gc = kAhead || i == 0 ? gn : raw8_load<T>(a.gate, goff + j0 + 8 * i);
+            if (kAhead && i < 7) gn = raw8_load<T>(a.gate, goff + j0 + 8 * (i + 1));
             float2 br[4];
-            float g[8];
             load8<T>(xslot + buf_stride, t, i, br);
-            param8(a.gate, a.gate_dtype, goff + j0 + 8 * i, true, g);
 #pragma unroll
             for (int p = 0; p < 4; ++p)
-              v[4 * i + p] = round2<T>(__ffma2_rn(br[p], make_float2(g[2 * p], g[2 * p + 1]),
-                                                  v[4 * i + p]));
+              v[4 * i + p] = round2<T>(
+                  __ffma2_rn(br[p], raw8_pair<T>(gc, p), v[4 * i + p]));
             store8<T>(rrow + 8 * i, v + 4 * i);
           }
         }
@@ -357,18 +393,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (live) {
         const int64_t moff = a.row_map ? int64_t(a.row_map[row]) * K : 0;
         const float2 nm = f2(-mean), inv2 = f2(inv);
+        constexpr bool kAhead = sizeof(T) == 2;  // see the gated update
+        Raw8<T> gn = raw8_load<T>(a.gamma, j0);
+        Raw8<T> cn = raw8_load<T>(a.scale, moff + j0);
+        Raw8<T> hn = raw8_load<T>(a.shift, moff + j0);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          float g[8], sc[8], sh[8];
-          param8(a.gamma, a.gamma_dtype, j0 + 8 * i, true, g);
-          param8(a.scale, a.scale_dtype, moff + j0 + 8 * i, true, sc);
-          param8(a.shift, a.shift_dtype, moff + j0 + 8 * i, true, sh);
+          if (!kAhead && i > 0) {
+            gn = raw8_load<T>(a.gamma, j0 + 8 * i);
+            cn = raw8_load<T>(a.scale, moff + j0 + 8 * i);
+            hn = raw8_load<T>(a.shift, moff + j0 + 8 * i);
+          }
+          const Raw8<T> gc = gn, cc = cn, hc = hn;
+          if (kAhead && i < 7) {
+            gn = raw8_load<T>(a.gamma, j0 + 8 * (i + 1));
+            cn = raw8_load<T>(a.scale, moff + j0 + 8 * (i + 1));
+            hn = raw8_load<T>(a.shift, moff + j0 + 8 * (i + 1));
+          }
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
             const float2 tq = __fmul2_rn(__fmul2_rn(__fadd2_rn(v[4 * i + p], nm), inv2),
-                                         make_float2(g[2 * p], g[2 * p + 1]));
-            const float2 one_sc = __fadd2_rn(f2(1.0f), make_float2(sc[2 * p], sc[2 * p + 1]));
-            float2 y = __ffma2_rn(tq, one_sc, make_float2(sh[2 * p], sh[2 * p + 1]));
+                                         raw8_pair<T>(gc, p));
+            const float2 one_sc = __fadd2_rn(f2(1.0f), raw8_pair<T>(cc, p));
+            float2 y = __ffma2_rn(tq, one_sc, raw8_pair<T>(hc, p));
             if (a.round_output) y = round2<T>(y);
             v[4 * i + p] = y;
           }
@@ -522,10 +569,15 @@ inline int mode_of(const RowPrepArgs& a) {
 }
 
 inline bool applicable(const RowPrepArgs& a, const RowMaps& m, int block, int out,
-                       int elem_bytes) {
+                       int elem_bytes, int x_dtype) {
   const int mode = mode_of(a);
   if (mode < 0 || block < 64 || !m.valid || !a.vec_ok) return false;
   if (mode != kPlain && (block > 256 || out == OUT_F32 || !a.params_vec)) return false;
+  // normalized rows: 16-bit inputs with modulation (and gate) tables of the
+  // input dtype (fp32 rows do not fit the registers of this schedule)
+  if (mode != kPlain && (elem_bytes != 2 || a.gamma_dtype != x_dtype || a.scale_dtype != x_dtype ||
+                         a.shift_dtype != x_dtype || (a.gate && a.gate_dtype != x_dtype)))
+    return false;
   if (a.signs != nullptr && !a.params_vec) return false;
   if (a.K % kChunk) return false;
   const int64_t tpr = a.K / kChunk;
@@ -610,10 +662,16 @@ cudaError_t launch(const RowPrepArgs& a, const RowMaps& m, int block, int out,
                    cudaStream_t stream) {
   switch (mode_of(a)) {
     case kPlain: return launch_mode<T, kPlain>(a, m, block, out, stream);
-    case kNorm: return launch_mode<T, kNorm>(a, m, block, out, stream);
-    case kNormGated: return launch_mode<T, kNormGated>(a, m, block, out, stream);
-    default: return cudaErrorInvalidValue;
+    default: break;
   }
+  if constexpr (sizeof(T) == 2) {
+    switch (mode_of(a)) {
+      case kNorm: return launch_mode<T, kNorm>(a, m, block, out, stream);
+      case kNormGated: return launch_mode<T, kNormGated>(a, m, block, out, stream);
+      default: break;
+    }
+  }
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace rotq
