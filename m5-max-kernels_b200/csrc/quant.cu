@@ -18,186 +18,16 @@
 
 #include "common.cuh"
 #include "m5b_internal.h"
+#include "quant_vec.cuh"
 
 namespace m5b {
 
 namespace {
 
+using namespace qv;
+
 constexpr int kThreads = 256;
 constexpr int kTieQueue = 64;  // queued near-tie vectors per warp and row
-constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: RNE to integer for |t| < 2^22
-
-// Running row peak max|x|.  16-bit inputs stay packed: one
-// max.xorsign.abs per pair of words (the magnitudes are exact, the sign bits
-// are cleared at the end); fp32 inputs use FMNMX with |.|.
-template <typename T>
-struct Peak {
-  uint32_t h = 0u;
-  float f = 0.0f;
-  __device__ __forceinline__ void add(const uint4& raw) {
-    if constexpr (sizeof(T) == 2) {
-      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        h = max_xorsign_abs_bf16x2(
-            h, max_xorsign_abs_bf16x2(max_xorsign_abs_bf16x2(raw.x, raw.y),
-                                      max_xorsign_abs_bf16x2(raw.z, raw.w)));
-      } else {
-        h = max_xorsign_abs_f16x2(
-            h, max_xorsign_abs_f16x2(max_xorsign_abs_f16x2(raw.x, raw.y),
-                                     max_xorsign_abs_f16x2(raw.z, raw.w)));
-      }
-    } else {
-      f = fmaxf(f, fmaxf(fmaxf(fabsf(__uint_as_float(raw.x)), fabsf(__uint_as_float(raw.y))),
-                         fmaxf(fabsf(__uint_as_float(raw.z)), fabsf(__uint_as_float(raw.w)))));
-    }
-  }
-  __device__ __forceinline__ float value() const {
-    if constexpr (sizeof(T) == 2) {
-      // |x| of a 16-bit float is its bit pattern with the sign cleared, and for
-      // finite values that pattern orders like the value.
-      const uint32_t m = h & 0x7FFF7FFFu;
-      const uint32_t hi = m >> 16, lo = m & 0xFFFFu;
-      const uint16_t best = static_cast<uint16_t>(hi > lo ? hi : lo);
-      return to_f32(*reinterpret_cast<const T*>(&best));
-    } else {
-      return f;
-    }
-  }
-};
-
-// Elements per 16-byte vector.
-template <typename T>
-constexpr int kVec = 16 / sizeof(T);
-
-template <typename T>
-__device__ __forceinline__ void unpack(const uint4& raw, float* out) {
-  if constexpr (sizeof(T) == 2) {
-    const T* h = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) out[e] = to_f32(h[e]);
-  } else {
-    const float* f = reinterpret_cast<const float*>(&raw);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) out[e] = f[e];
-  }
-}
-
-// INT8 codes of one 16-byte vector (8 bf16/fp16 or 4 fp32 values) packed
-// into words by bracketed rounding of packed pairs (i8_pair).  Returns the
-// bracket disagreement bits: nonzero means some element may round
-// differently from the reference, and the vector is redone by
-// i8_words_near_tie.
-template <typename T>
-__device__ __forceinline__ uint32_t pack_i8_vec(const uint4& raw, const I8Bracket& br,
-                                                uint32_t* words) {
-  constexpr int PAIRS = sizeof(T) == 2 ? 4 : 2;
-  float2 m[PAIRS];
-  uint32_t acc = 0u;
-#pragma unroll
-  for (int p = 0; p < PAIRS; ++p) {
-    float2 v;
-    if constexpr (sizeof(T) == 2) {
-      const uint32_t w = reinterpret_cast<const uint32_t*>(&raw)[p];
-      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        v = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
-      } else {
-        const __half2 h = *reinterpret_cast<const __half2*>(&w);
-        v = __half22float2(h);
-      }
-    } else {
-      v = make_float2(reinterpret_cast<const float*>(&raw)[2 * p],
-                      reinterpret_cast<const float*>(&raw)[2 * p + 1]);
-    }
-    m[p] = i8_pair(v, br, acc);
-  }
-#pragma unroll
-  for (int w = 0; w < PAIRS / 2; ++w)
-    words[w] = pack4_low_bytes(m[2 * w].x, m[2 * w].y, m[2 * w + 1].x, m[2 * w + 1].y);
-  return acc;
-}
-
-// The exact codes of a vector that holds a product next to a half-integer:
-// per element the reciprocal-product code, and for an element within 2^-14
-// of a half-integer the division-free decision of int8_code_near_tie.  Kept
-// out of line: it runs for a small fraction of vectors.  Requires
-// scale >= 2^-100.
-template <typename T>
-__device__ __noinline__ uint2 i8_words_near_tie(uint4 raw, float scale, float inv) {
-  constexpr int V = kVec<T>;
-  constexpr float kNear = 0.5f - 0x1p-14f;
-  float v[V];
-  unpack<T>(raw, v);
-  uint32_t w[2] = {0u, 0u};
-#pragma unroll
-  for (int e = 0; e < V; ++e) {
-    const float t = __fmul_rn(v[e], inv);
-    float m = __fadd_rn(t, kMagic);
-    const float r = __fadd_rn(m, -kMagic);
-    if (fabsf(__fsub_rn(t, r)) > kNear)
-      m = __fadd_rn(int8_code_near_tie(v[e], scale, t, r), kMagic);
-    w[e >> 2] |= (__float_as_uint(m) & 0xFFu) << (8 * (e & 3));
-  }
-  return make_uint2(w[0], w[1]);
-}
-
-__device__ __forceinline__ uint32_t code_i8_exact(float v, float scale) {
-  float r = rintf(__fdiv_rn(v, scale));
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu;
-}
-
-__device__ __forceinline__ uint32_t code_e4m3(float v, float scale, float inv, bool fast) {
-  if (fast) {
-    const float t = __fmul_rn(v, inv);
-    if ((__float_as_uint(scale) & 0x007FFFFFu) == 0u)  // exact reciprocal: t == v / scale
-      return static_cast<uint32_t>(__nv_cvt_float_to_fp8(t, __NV_SATFINITE, __NV_E4M3));
-    const __nv_fp8x2_storage_t two = __nv_cvt_float2_to_fp8x2(
-        make_float2(__fmul_rn(t, 1.0f - 0x1p-18f), __fmul_rn(t, 1.0f + 0x1p-18f)), __NV_SATFINITE,
-        __NV_E4M3);
-    if ((two & 0xFFu) == (two >> 8)) return two & 0xFFu;
-  }
-  return static_cast<uint32_t>(
-      __nv_cvt_float_to_fp8(__fdiv_rn(v, scale), __NV_SATFINITE, __NV_E4M3));
-}
-
-// Codes of one 16-byte vector into `words` (V/4 words).
-template <typename T, int OUT>
-__device__ __forceinline__ void vec_codes(const uint4& raw, float scale, float inv, bool fast,
-                                          uint32_t* words) {
-  constexpr int V = kVec<T>;
-  float v[V];
-  if constexpr (OUT == OUT_E4M3) {
-    unpack<T>(raw, v);
-#pragma unroll
-    for (int w = 0; w < V / 4; ++w)
-      words[w] = code_e4m3(v[4 * w], scale, inv, fast) |
-                 (code_e4m3(v[4 * w + 1], scale, inv, fast) << 8) |
-                 (code_e4m3(v[4 * w + 2], scale, inv, fast) << 16) |
-                 (code_e4m3(v[4 * w + 3], scale, inv, fast) << 24);
-  } else {
-    if (fast) {
-      if (pack_i8_vec<T>(raw, i8_bracket(inv, scale), words) != 0u) {
-        const uint2 w = i8_words_near_tie<T>(raw, scale, inv);
-        words[0] = w.x;
-        if constexpr (V == 8) words[1] = w.y;
-      }
-    } else {  // scale below 2^-100: the reciprocal product is not trustworthy
-      unpack<T>(raw, v);
-#pragma unroll
-      for (int w = 0; w < V / 4; ++w)
-        words[w] = code_i8_exact(v[4 * w], scale) | (code_i8_exact(v[4 * w + 1], scale) << 8) |
-                   (code_i8_exact(v[4 * w + 2], scale) << 16) |
-                   (code_i8_exact(v[4 * w + 3], scale) << 24);
-    }
-  }
-}
-
-template <typename T>
-__device__ __forceinline__ void store_codes(uint8_t* qr, int64_t j, const uint32_t* words) {
-  if constexpr (kVec<T> == 8)
-    *reinterpret_cast<uint2*>(qr + j * 8) = make_uint2(words[0], words[1]);
-  else
-    *reinterpret_cast<uint32_t*>(qr + j * 4) = words[0];
-}
 
 __device__ __forceinline__ float cta_peak(float peak, float* red) {
 #pragma unroll
