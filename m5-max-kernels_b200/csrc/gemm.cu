@@ -51,10 +51,17 @@ struct GemmCfg {
   static constexpr int B_BYTES = B_ROWS * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TILE_M = PAIR ? 2 * kBM : kBM;
-  static constexpr int STAGES = QK ? 5 : (STAGE_BYTES <= 32 * 1024 ? 6 : 4);
+  // (Q/K pair tiles keep 4 stages: their 64 KB of staging would otherwise
+  // leave the L1 almost no room for the epilogue's table loads.)
+  static constexpr int STAGES = QK ? (PAIR ? 4 : 5) : (STAGE_BYTES <= 32 * 1024 ? 6 : 4);
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
-  static constexpr int QK_BYTES = QK ? kBM * 256 : 0;  // 128 rows x 128 bf16 channels
+  // Epilogue warps: 4, or 8 for Q/K pair tiles (each warp drains one of the
+  // tile's two heads for its 32 rows).
+  static constexpr int EPI_WARPS = (QK && PAIR) ? 8 : 4;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  // 128 rows x 128 bf16 channels per head staged at once
+  static constexpr int QK_BYTES = QK ? (EPI_WARPS / 4) * kBM * 256 : 0;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + QK_BYTES + BAR_BYTES + 16;
 };
 
@@ -183,7 +190,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
 }
 
 template <int KIND, int BN, bool QK, bool PAIR>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_b_half,
@@ -222,7 +229,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], PAIR ? 8 : 4);
+      mbar_init(&acc_empty[a], (PAIR ? 2 : 1) * Cfg::EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -391,6 +398,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
+    const int ehalf = (warp - 2) >> 2;  // 8-warp Q/K epilogue: which head of the tile
     const int row_in_tile = static_cast<int>(rank) * kBM + quarter * 32 + lane;
     // acc_empty lives in the even CTA of a pair: the odd CTA arrives remotely.
     const uint32_t acc_empty_remote0 = PAIR ? map_to_rank(&acc_empty[0], 0) : 0u;
@@ -441,7 +449,8 @@ __global__ void __launch_bounds__(192, 1)
         // thread's row is read and written without bank conflicts and the
         // finished 32 x 128 head block leaves with two tiled TMA stores
         // (rows past M clipped by the tensor map).
-        uint8_t* wstage = qk_stage + quarter * 8192;
+        constexpr bool kHeadPerWarp = Cfg::EPI_WARPS == 8;
+        uint8_t* wstage = qk_stage + (kHeadPerWarp ? ehalf * (kBM * 256) : 0) + quarter * 8192;
         auto chunk = [&](int ch) -> uint8_t* {  // channels 8*ch .. 8*ch+7 of this row
           return wstage + (ch >> 3) * 4096 + lane * 128 + (((ch & 7) ^ (lane & 7)) << 4);
         };
@@ -449,14 +458,19 @@ __global__ void __launch_bounds__(192, 1)
         const int heads_left = (g.N - n_col) / 128;  // N tail: a second head may not exist
         const int heads_here = heads_left < heads_tile ? (heads_left > 0 ? heads_left : 0)
                                                        : heads_tile;
-        if (heads_here == 0) {
+        // this warp's heads: all of them, or with 8 warps the one matching ehalf
+        const int h_first = kHeadPerWarp ? ehalf : 0;
+        const int h_step = kHeadPerWarp ? BN / 128 : 1;
+        int h_last = -1;
+        for (int hh = h_first; hh < heads_here; hh += h_step) h_last = hh;
+        if (h_last < 0) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) release_acc(acc);
         }
         const int64_t row0 = row - lane;  // this warp's first row
 #pragma unroll 1
-        for (int hh = 0; hh < heads_here; ++hh) {
+        for (int hh = h_first; hh < heads_here; hh += h_step) {
           const int head = n_col / 128 + hh;
           if (lane == 0) bulk_wait_group_read0();  // the previous store has read the staging
           __syncwarp();
@@ -487,7 +501,7 @@ __global__ void __launch_bounds__(192, 1)
               *reinterpret_cast<uint4*>(chunk(c * 4 + q)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
           }
-          if (hh == heads_here - 1) {
+          if (hh == h_last) {
             // The accumulator is no longer needed: hand it back to the MMA warp.
             tc_fence_before();
             __syncwarp();
@@ -615,12 +629,12 @@ static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const 
   auto kern = gemm_tc_kernel<KIND, BN, QK, PAIR>;
   static std::atomic<long long> shape[kMaxLaunchDevices];
   int dev = 0, sms = 0, per_sm = 0;
-  cudaError_t e = launch_shape(reinterpret_cast<const void*>(kern), 192, Cfg::SMEM_BYTES, shape,
+  cudaError_t e = launch_shape(reinterpret_cast<const void*>(kern), Cfg::THREADS, Cfg::SMEM_BYTES, shape,
                                &dev, &sms, &per_sm);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
