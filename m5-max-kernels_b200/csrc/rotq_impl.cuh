@@ -163,6 +163,29 @@ __device__ __forceinline__ float2 raw8_pair(const Raw8<T>& r, int q) {
   }
 }
 
+// Table slices through shared memory: the 32 chunks of a warp cover 4 KB of
+// a 16-bit table row.  The warp loads the 4 KB coalesced (lane l takes 16-byte
+// vectors l, l + 32, ...) and stores each vector where its owning lane reads
+// it, in the same swizzled layout as a staged activation row (chunk at 128-byte
+// row `lane`, 16-byte slot s at s ^ (lane & 7)); owners then read their
+// 128 bytes conflict-free.  Per-lane 16-byte loads from global memory would
+// touch 32 lines per instruction instead of 4.
+__device__ __forceinline__ void stage_table16(uint8_t* wbuf, const void* seg, int lane) {
+  const uint4* g4 = reinterpret_cast<const uint4*>(seg);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __ldg(g4 + lane + 32 * (4 * h + i));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = lane + 32 * (4 * h + i);
+      const int owner = idx >> 3, slot = idx & 7;
+      *reinterpret_cast<uint4*>(wbuf + owner * 128 + ((slot ^ (owner & 7)) << 4)) = v[i];
+    }
+  }
+}
+
 // Round a pair through T (RNE) and back.
 template <typename T>
 __device__ __forceinline__ float2 round2(float2 y) {
@@ -225,11 +248,14 @@ __device__ __forceinline__ float chunk_sum2(const float2* v, float mean) {
 // rows at a time, with its own ring of `stages` slots and mbarriers, so the
 // units of a CTA never wait for one another (a named barrier, or __syncwarp
 // for one-warp units, synchronises a unit).
+// Plain rows: two 256-thread CTAs per SM (128 registers).  Normalized rows
+// run 1-2 units per CTA (shared memory bounds them to ~8 warps per SM), so
+// they may use more registers.
 template <typename T, int B, int OUT, int MODE>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, MODE == kPlain ? 2 : 1)
     lean_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_b,
                 const RowPrepArgs a, const int tpr, const int stages, const int box_rows,
-                const int64_t buf_stride) {
+                const int64_t buf_stride, const int tbl_off) {
   constexpr int LANE_SPAN = B / kChunk;  // lanes per Hadamard block (B >= 64)
   constexpr int INPUTS = MODE == kNormGated ? 2 : 1;
   extern __shared__ uint8_t dsmem_raw[];
@@ -259,6 +285,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int64_t row_slot = int64_t(INPUTS) * buf_stride;  // one row's inputs
   const int64_t slot_bytes = int64_t(RPU) * row_slot;
   uint8_t* ring = dsmem + int64_t(u) * stages * slot_bytes;
+  // Normalized rows with K >= 2048: 8 KB per warp for table slices (tbl_off > 0)
+  uint8_t* tbl_a = dsmem + tbl_off + (tid >> 5) * 8192;
+  uint8_t* tbl_b = tbl_a + 4096;
+  (void)tbl_off;
   uint64_t* bars = full_bar + u * kMaxStages;
   const int64_t first_step = int64_t(blockIdx.x) * U + u;
   const int64_t step_stride = int64_t(gridDim.x) * U;
@@ -359,14 +389,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (live) {
           const int64_t goff = a.gate_row_map ? int64_t(a.gate_row_map[row]) * K : 0;
           T* rrow = reinterpret_cast<T*>(a.r_out) + row * K + j0;
-          // 16-bit tables: the next group's gate loads go out before this
-          // group is computed (fp32 tables would not fit the registers).
-          constexpr bool kAhead = sizeof(T) == 2;
-          Raw8<T> gn = raw8_load<T>(a.gate, goff + j0);
+          stage_table16(tbl_a, reinterpret_cast<const T*>(a.gate) + goff + (j0 - 64 * lane), lane);
+          __syncwarp();
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const Raw8<T> gc = kAhead || i == 0 ? gn : raw8_load<T>(a.gate, goff + j0 + 8 * i);
-            if (kAhead && i < 7) gn = raw8_load<T>(a.gate, goff + j0 + 8 * (i + 1));
+            Raw8<T> gc;
+            gc.w[0] = *swz_slot(tbl_a, lane, i);
             float2 br[4];
             load8<T>(xslot + buf_stride, t, i, br);
 #pragma unroll
@@ -393,33 +421,39 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (live) {
         const int64_t moff = a.row_map ? int64_t(a.row_map[row]) * K : 0;
         const float2 nm = f2(-mean), inv2 = f2(inv);
-        constexpr bool kAhead = sizeof(T) == 2;  // see the gated update
-        Raw8<T> gn = raw8_load<T>(a.gamma, j0);
-        Raw8<T> cn = raw8_load<T>(a.scale, moff + j0);
-        Raw8<T> hn = raw8_load<T>(a.shift, moff + j0);
+        // gamma and scale slices, then t = ((v - mean) * inv) * gamma in place;
+        // then the shift slice and y = fma(t, 1 + scale, shift).
+        const int64_t wcol = j0 - 64 * lane;  // the warp's first column
+        __syncwarp();  // every lane is done with the gate slice
+        stage_table16(tbl_a, reinterpret_cast<const T*>(a.gamma) + wcol, lane);
+        stage_table16(tbl_b, reinterpret_cast<const T*>(a.scale) + moff + wcol, lane);
+        __syncwarp();
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          if (!kAhead && i > 0) {
-            gn = raw8_load<T>(a.gamma, j0 + 8 * i);
-            cn = raw8_load<T>(a.scale, moff + j0 + 8 * i);
-            hn = raw8_load<T>(a.shift, moff + j0 + 8 * i);
-          }
-          const Raw8<T> gc = gn, cc = cn, hc = hn;
-          if (kAhead && i < 7) {
-            gn = raw8_load<T>(a.gamma, j0 + 8 * (i + 1));
-            cn = raw8_load<T>(a.scale, moff + j0 + 8 * (i + 1));
-            hn = raw8_load<T>(a.shift, moff + j0 + 8 * (i + 1));
-          }
+          Raw8<T> gc;
+          gc.w[0] = *swz_slot(tbl_a, lane, i);
+#pragma unroll
+          for (int p = 0; p < 4; ++p)
+            v[4 * i + p] = __fmul2_rn(__fmul2_rn(__fadd2_rn(v[4 * i + p], nm), inv2),
+                                      raw8_pair<T>(gc, p));
+        }
+        __syncwarp();
+        stage_table16(tbl_a, reinterpret_cast<const T*>(a.shift) + moff + wcol, lane);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          Raw8<T> cc, hc;
+          cc.w[0] = *swz_slot(tbl_b, lane, i);
+          hc.w[0] = *swz_slot(tbl_a, lane, i);
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
-            const float2 tq = __fmul2_rn(__fmul2_rn(__fadd2_rn(v[4 * i + p], nm), inv2),
-                                         raw8_pair<T>(gc, p));
             const float2 one_sc = __fadd2_rn(f2(1.0f), raw8_pair<T>(cc, p));
-            float2 y = __ffma2_rn(tq, one_sc, raw8_pair<T>(hc, p));
+            float2 y = __ffma2_rn(v[4 * i + p], one_sc, raw8_pair<T>(hc, p));
             if (a.round_output) y = round2<T>(y);
             v[4 * i + p] = y;
           }
         }
+        __syncwarp();  // slices read before the next row's gate slice
         if (a.signs != nullptr) {
 #pragma unroll
           for (int i = 0; i < kChunk; i += 16) {
@@ -572,7 +606,7 @@ inline bool applicable(const RowPrepArgs& a, const RowMaps& m, int block, int ou
                        int elem_bytes, int x_dtype) {
   const int mode = mode_of(a);
   if (mode < 0 || block < 64 || !m.valid || !a.vec_ok) return false;
-  if (mode != kPlain && (block > 256 || out == OUT_F32 || !a.params_vec)) return false;
+  if (mode != kPlain && (block > 256 || out == OUT_F32 || !a.params_vec || a.K < 2048)) return false;
   // normalized rows: 16-bit inputs with modulation (and gate) tables of the
   // input dtype (fp32 rows do not fit the registers of this schedule)
   if (mode != kPlain && (elem_bytes != 2 || a.gamma_dtype != x_dtype || a.scale_dtype != x_dtype ||
@@ -599,6 +633,8 @@ cudaError_t launch_m(const RowPrepArgs& a, const RowMaps& m, cudaStream_t stream
   const int64_t buf_stride = (row_bytes + 1023) & ~int64_t(1023);
   const int64_t unit_slot = int64_t(MODE == kNormGated ? 2 : 1) * rpu * buf_stride;
   int units, stages;
+  // normalized rows (>= 2048 elements) stage their table slices per warp
+  const int64_t tbl_per_unit = MODE != kPlain ? int64_t(pw / 32) * 8192 : 0;
   if (MODE == kPlain) {
     units = kThreads / pw;
     stages = static_cast<int>((110 * 1024) / (units * unit_slot));
@@ -607,11 +643,13 @@ cudaError_t launch_m(const RowPrepArgs& a, const RowMaps& m, cudaStream_t stream
     // Two stages per unit; as many units per CTA as keep the CTA near
     // 72 KB, so that three CTAs share an SM where the rows allow it.
     stages = 2;
-    units = static_cast<int>((72 * 1024) / (stages * unit_slot));
+    units = static_cast<int>((72 * 1024) / (stages * unit_slot + tbl_per_unit));
     units = units < 1 ? 1 : (units > kThreads / pw ? kThreads / pw : units);
   }
   const int threads = units * pw;
-  const int smem = static_cast<int>(int64_t(stages) * units * unit_slot) + 1024;
+  const int tbl_off = tbl_per_unit ? static_cast<int>(int64_t(stages) * units * unit_slot) : 0;
+  const int smem =
+      static_cast<int>(int64_t(stages) * units * unit_slot + units * tbl_per_unit) + 1024;
   static std::atomic<long long> shape[kMaxLaunchDevices];
   int dev = 0, sms = 0, per_sm = 0;
   cudaError_t e = launch_shape(reinterpret_cast<const void*>(kern), threads, smem, shape, &dev,
@@ -622,7 +660,7 @@ cudaError_t launch_m(const RowPrepArgs& a, const RowMaps& m, cudaStream_t stream
   int64_t grid = int64_t(sms) * per_sm;
   if (grid > ctas_needed) grid = ctas_needed;
   kern<<<static_cast<unsigned>(grid), threads, smem, stream>>>(
-      m.x, MODE == kNormGated ? m.b : m.x, a, tpr, stages, m.box_rows, buf_stride);
+      m.x, MODE == kNormGated ? m.b : m.x, a, tpr, stages, m.box_rows, buf_stride, tbl_off);
   return cudaGetLastError();
 }
 
