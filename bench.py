@@ -187,6 +187,8 @@ def run_secondary(args, world, rank, local):
              of 2048 tokens) + H128 + INT8 (M=4096, K=4096), bytes 7K+4 per row.
     qk_c5:   H256 + INT8 online prep and the Q/K projection with RMSNorm + RoPE
              (M=9914, K=4096, 32 heads x 128, theta 10000, R=64).
+    rms_q:   RMS scale-folding prep (random gamma, H256, INT8) + W8A8 GEMM on the
+             reference's rms-quant Q shape (M=4096, K=5376, N=7168).
 
     Each step runs on one of SETS independent input sets (their footprint is
     above L2), and the SETS steps are captured once as a CUDA graph that is
@@ -226,6 +228,25 @@ def run_secondary(args, world, rank, local):
             return (lambda: m5.fused_gated_residual_norm_hadamard_quantize(  # noqa: E731
                 res, br, gate, gamma, scale, shift, signs, 128, norm="layer", epsilon=1e-6,
                 gate_row_map=rmap, row_map=rmap)), {}
+        if args.workload == "rms_q":
+            m, k, n = 4096, 5376, 7168
+            x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+            w = torch.randn(n, k, device=dev, generator=g).to(torch.bfloat16)
+            gamma = (1 + 0.2 * torch.randn(k, device=dev, generator=g)).float()
+            signs = (2 * torch.randint(0, 2, (k,), device=dev, generator=g) - 1).to(torch.int8)
+            wq, ws = m5.hadamard_quantize(w, 256, signs, "int8")
+            q0, s0 = m5.rms_quantize(x, gamma, signs, 256, fold_scale=True)
+
+            def rms_step():
+                q, s = m5.rms_quantize(x, gamma, signs, 256, fold_scale=True)
+                return m5.gemm(q, wq, "int8", a_scales=s, b_scales=ws,
+                               output_dtype=torch.bfloat16)
+
+            return rms_step, {
+                "prep": lambda: m5.rms_quantize(x, gamma, signs, 256, fold_scale=True),  # noqa: E731
+                "gemm": lambda: m5.gemm(q0, wq, "int8", a_scales=s0, b_scales=ws,  # noqa: E731
+                                        output_dtype=torch.bfloat16),
+            }
         m, k, n = 9914, 4096, 4096  # qk_c5
         x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
         w = (0.02 * torch.randn(n, k, device=dev, generator=g)).to(torch.bfloat16)
@@ -251,6 +272,9 @@ def run_secondary(args, world, rank, local):
         nbytes, unit, kernel = 4096 * (3 * 16384 + 4), "GB/s", "lean_kernel<bf16,128,int8,plain>"
     elif args.workload == "prep_c4":
         nbytes, unit, kernel = 4096 * (7 * 4096 + 4), "GB/s", "lean_kernel<bf16,128,int8,norm_gated>"
+    elif args.workload == "rms_q":
+        nbytes, unit = 2.0 * 4096 * 7168 * 5376, "TOPS"
+        kernel = "row_prep_kernel<bf16,256,int8> (rms fold) + gemm_tc_kernel<i8,256,plain,pair>"
     else:
         nbytes, unit = 2.0 * 9914 * 4096 * 4096, "TOPS"
         kernel = "lean_kernel<bf16,256,int8,plain> + gemm_tc_kernel<i8,256,qk,pair>"
@@ -289,7 +313,13 @@ def run_secondary(args, world, rank, local):
             "timing": f"CUDA graph replay, {SETS} input sets rotating"}
     if part_ms:
         line["parts_ms"] = part_ms
-        line["qk_gemm_tops"] = nbytes / (part_ms["qk_gemm"] * 1e-3) / 1e12
+        if "qk_gemm" in part_ms:
+            line["qk_gemm_tops"] = nbytes / (part_ms["qk_gemm"] * 1e-3) / 1e12
+        if args.workload == "rms_q":
+            prep_bytes = 4096 * (3 * 5376 + 4)
+            line["prep_gbs"] = prep_bytes / (part_ms["prep"] * 1e-3) / 1e9
+            line["prep_frac_of_measured_hbm"] = line["prep_gbs"] / peaks["hbm_gbs"]
+            line["gemm_tops"] = nbytes / (part_ms["gemm"] * 1e-3) / 1e12
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
@@ -500,7 +530,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="ffn_down",
-                    choices=["ffn_down", "prep_c3", "prep_c4", "qk_c5"],
+                    choices=["ffn_down", "prep_c3", "prep_c4", "qk_c5", "rms_q"],
                     help="ffn_down is the headline; the others time one other BASELINE config")
     ap.add_argument("--profile", action="store_true",
                     help="profiling run: timed steps and per-kernel timing only (no e2e, no CPU leg)")

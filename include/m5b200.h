@@ -123,6 +123,21 @@ M5B_API int m5b_fused_gated_residual_norm_hadamard_quantize(
     int block_size, int norm, float epsilon, int round_output, int mode, void* q, float* scales,
     void* residual_out, void* stream);
 
+/* RMS preparation with the inverse RMS folded into the INT8 row scale:
+ *   r = 1/sqrt(sum(x^2)/k + eps)            (x the ORIGINAL row, FP32)
+ *   fold_scale 1: u = (x * gamma) D H,  scale = (peak(u) * r) / 127
+ *   fold_scale 0: u = ((x * r) * gamma) D H, scale = peak(u) / 127
+ *   q = clip(rint((u / peak(u)) * 127), +-127); a zero row of u gets q = 0,
+ *   scale 1.  No additive shift, no rounding to the input dtype in between.
+ * gamma: fp32[k]; signs: int8[k] of +-1 (required); block_size 1 (no
+ * rotation, any k) or a power of two from 32 through 1024 dividing k.
+ * Replaces src/m5kernels/rms_quant.py:41-117 (rms_quantize) with the
+ * semantics of rms_quant_reference.py:24-89. */
+M5B_API int m5b_rms_quantize(const void* x, int x_dtype, int64_t rows, int64_t k,
+                             const float* gamma, const int8_t* signs, int block_size,
+                             int fold_scale, float epsilon, int8_t* q, float* scales,
+                             void* stream);
+
 /* C[m, n] = epilogue(A[m, k] . B[n, k]^T) on tcgen05 tensor cores.
  *   mode INT8: int8 operands, INT32 accumulation; FP8: E4M3 operands, FP32
  *   accumulation (k % 128 == 0); BF16 / FP16: FP32 accumulation.

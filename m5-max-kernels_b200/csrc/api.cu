@@ -352,6 +352,32 @@ int m5b_fused_gated_residual_norm_hadamard_quantize(
   return run_row_prep(a, x_dtype, block_size, out, stream);
 }
 
+int m5b_rms_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, const float* gamma,
+                     const int8_t* signs, int block_size, int fold_scale, float epsilon,
+                     int8_t* q, float* scales, void* stream) {
+  RowPrepArgs a;
+  int rc = prep_common(a, x, x_dtype, rows, k);
+  if (rc) return rc;
+  if (!gamma) return fail(M5B_EINVAL, "gamma must be a float32 vector of length K");
+  if (!signs) return fail(M5B_EINVAL, "signs must be an int8 vector of length K containing only +/-1");
+  if (block_size != 1) {
+    rc = check_block(block_size, k);
+    if (rc) return rc;
+  }
+  if (fold_scale != 0 && fold_scale != 1) return fail(M5B_EINVAL, "fold_scale must be a boolean");
+  if (!(epsilon > 0.0f) || !std::isfinite(epsilon))
+    return fail(M5B_EINVAL, "epsilon must remain finite and positive in float32");
+  if (!q || !scales) return fail(M5B_EINVAL, "output pointers are NULL");
+  a.gamma = gamma;
+  a.gamma_dtype = DT_F32;
+  a.signs = signs;
+  a.eps = epsilon;
+  a.rms_quant = fold_scale ? RMSQ_FOLD : RMSQ_DIRECT;
+  a.q = q;
+  a.s = scales;
+  return run_row_prep(a, x_dtype, block_size == 1 ? 0 : block_size, OUT_INT8, stream);
+}
+
 // A CTA pair (cta_group::2, 256 x 256 tiles) when the problem has at least
 // one full pair tile of rows and more than 128 output columns.
 static bool use_pair(int epi, int64_t m, int64_t n) {

@@ -52,6 +52,9 @@ inline cudaError_t launch_shape(const void* kern, int threads, int smem,
 
 enum NormKind : int { NORM_NONE = 0, NORM_RMS = 1, NORM_LAYER = 2 };
 enum RowOut : int { OUT_INT8 = 0, OUT_E4M3 = 1, OUT_F32 = 2 };
+// RMS scale folding (codes from (X gamma) D H, inverse RMS in the row scale)
+// and its direct counterpart (normalize first); both INT8 only.
+enum RmsQuant : int { RMSQ_NONE = 0, RMSQ_FOLD = 1, RMSQ_DIRECT = 2 };
 
 struct RowPrepArgs {
   const void* x;               // [rows, K] input (the residual R when gated)
@@ -69,6 +72,7 @@ struct RowPrepArgs {
   int norm;                    // NormKind
   float eps;
   int round_output;            // round the modulated value through the input dtype
+  int rms_quant;               // RmsQuant; gamma is then an fp32 [K] vector, no scale / shift
   float inv_sqrt_block;        // fp32(1/sqrt(block)) for the rotation
   int warps;                   // warps per CTA (row_prep_warps)
   int vec_ok;                  // 16-byte vector loads / stores of rows are aligned

@@ -11,6 +11,9 @@
 //       (src/m5kernels/norm_hadamard.py:122-176, norm_hadamard_reference.py:67-94)
 //   * the gated-residual extension R' = cast_R(R + branch * gate), written once
 //       (src/m5kernels/norm_hadamard.py:198-265, gated_residual_reference.py:21-60)
+//   * RMS scale folding: codes of (X gamma) D H, inverse RMS folded into the
+//       row scale, or the direct form that normalizes first
+//       (src/m5kernels/rms_quant.py:41-117, rms_quant_reference.py:24-89)
 //
 // Data layout in HBM: row-major [rows, K] activations; codes [rows, K] int8 /
 // uint8 (E4M3 bits); scales fp32 [rows].  Each row is read once and its codes
@@ -128,6 +131,55 @@ __device__ __forceinline__ void quant_i8_fast16(const float* v, float scale, flo
   }
 }
 
+// Codes of the RMS preparation, rint(RN(RN(v / peak) * 127)) clipped to
+// +-127 (the reference's order: divide by the row peak, then scale by 127),
+// for 16 values.  Both roundings together move the result by less than
+// 2^-23 relative, so products with RN(127 / peak)(1 -+ 2^-21), which bracket
+// it, decide the integer whenever they agree; a group where they disagree
+// somewhere is redone exactly by rel_i8_exact16.  Requires peak >= 2^-100.
+static __device__ __noinline__ uint4 rel_i8_exact16(Vals16 in, float peak) {
+  const float v[16] = {in.a.x, in.a.y, in.a.z, in.a.w, in.b.x, in.b.y, in.b.z, in.b.w,
+                       in.c.x, in.c.y, in.c.z, in.c.w, in.d.x, in.d.y, in.d.z, in.d.w};
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const float c = rintf(__fmul_rn(__fdiv_rn(v[e], peak), 127.0f));
+    const int code = static_cast<int>(fminf(fmaxf(c, -127.0f), 127.0f));
+    w[e >> 2] |= (static_cast<uint32_t>(code) & 0xFFu) << (8 * (e & 3));
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ void rel_i8_fast16(const float* v, float peak, uint32_t* words) {
+  const float r = __fdiv_rn(127.0f, peak);
+  const float lo = __fmul_rn(r, 1.0f - 0x1p-21f), hi = __fmul_rn(r, 1.0f + 0x1p-21f);
+  const I8Bracket br{make_float2(lo, lo), make_float2(hi, hi)};
+  uint32_t acc = 0u;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float2 m0 = i8_pair(make_float2(v[4 * w], v[4 * w + 1]), br, acc);
+    const float2 m1 = i8_pair(make_float2(v[4 * w + 2], v[4 * w + 3]), br, acc);
+    words[w] = pack4_low_bytes(m0.x, m0.y, m1.x, m1.y);
+  }
+  if (acc != 0u) {
+    const Vals16 in{make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]),
+                    make_float4(v[8], v[9], v[10], v[11]),
+                    make_float4(v[12], v[13], v[14], v[15])};
+    const uint4 q = rel_i8_exact16(in, peak);
+    words[0] = q.x;
+    words[1] = q.y;
+    words[2] = q.z;
+    words[3] = q.w;
+  }
+}
+
+// One RMS-preparation code, exactly (ragged tails, tiny peaks).
+__device__ __forceinline__ int rel_i8_code(float v, float peak) {
+  if (peak == 0.0f) return 0;
+  const float c = rintf(__fmul_rn(__fdiv_rn(v, peak), 127.0f));
+  return static_cast<int>(fminf(fmaxf(c, -127.0f), 127.0f));
+}
+
 // ---------------------------------------------------------------- loads
 template <typename T>
 __device__ __forceinline__ void cvt8(const uint4& raw, float* out) {
@@ -235,6 +287,32 @@ __device__ __forceinline__ float cta_max(float v, float* red, int W) {
   return t;
 }
 
+// Sum (canonical order, as cta_sum) and max over the CTA with one pair of
+// barriers: the RMS scale-folding kernel reduces the squared norm of the
+// input and the peak of the rotated row together.
+__device__ __forceinline__ float2 cta_sum_max(float v, float m, float* red, float* red_max,
+                                              int W) {
+  v = warp_sum_tree(v);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if ((threadIdx.x & 31) == 0) {
+    red[threadIdx.x >> 5] = v;
+    red_max[threadIdx.x >> 5] = m;
+  }
+  __syncthreads();
+  float part[16];
+#pragma unroll
+  for (int w = 0; w < 16; ++w) part[w] = (w < W) ? red[w] : 0.0f;
+#pragma unroll
+  for (int step = 1; step < 16; step <<= 1)
+#pragma unroll
+    for (int w = 0; w + step < 16; w += 2 * step) part[w] = __fadd_rn(part[w], part[w + step]);
+  float t = red_max[0];
+  for (int w = 1; w < W; ++w) t = fmaxf(t, red_max[w]);
+  __syncthreads();
+  return make_float2(part[0], t);
+}
+
 // ---------------------------------------------------------------- TMA row tiles
 // A row of K elements is viewed as [K / E] box rows of E = 128 / sizeof(T)
 // elements (128 bytes); the 3D tensor map {E, K/E, rows} loads whole rows
@@ -261,6 +339,7 @@ __global__ void __launch_bounds__(512)
   uint8_t* dsmem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   __shared__ float red[16];
+  __shared__ float red_max[16];
   __shared__ __align__(8) uint64_t full_bar[4];
   __shared__ int abort_flag;
 
@@ -411,7 +490,37 @@ __global__ void __launch_bounds__(512)
 
     // ---- normalization statistics ----------------------------------------
     float mean = 0.0f, inv = 1.0f;
-    if (a.norm != NORM_NONE) {
+    float sq_part = 0.0f;  // RMS folding: this thread's share of sum(x^2)
+    if (a.rms_quant != RMSQ_NONE) {
+      // RMS statistics of the ORIGINAL row; the direct form normalizes now,
+      // the folded form keeps the inverse RMS for the row scale.
+      sq_part = chunk_sum<1>(v, cnt, 0.0f);
+      if (a.rms_quant == RMSQ_DIRECT) {
+        const float moment = __fdiv_rn(cta_sum(sq_part, red, W), static_cast<float>(K));
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(moment, a.eps)));
+      }
+      const bool pvec = fullchunk && a.params_vec;
+#pragma unroll
+      for (int i = 0; i < kChunk; i += 8) {
+        if (in(i)) {
+          float g[8];
+          if (pvec) {
+            param8(a.gamma, DT_F32, j0 + i, true, g);
+          } else {  // ragged rows (any K without rotation): never read past gamma[K - 1]
+            const float* gp = reinterpret_cast<const float*>(a.gamma) + j0 + i;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) g[e] = in(i + e) ? __ldg(gp + e) : 0.0f;
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (in(i + e)) {
+              const float t = (a.rms_quant == RMSQ_DIRECT) ? __fmul_rn(v[i + e], inv) : v[i + e];
+              v[i + e] = __fmul_rn(t, g[e]);
+            }
+          }
+        }
+      }
+    } else if (a.norm != NORM_NONE) {
       const float acc = (a.norm == NORM_LAYER) ? chunk_sum<0>(v, cnt, 0.0f)
                                                : chunk_sum<1>(v, cnt, 0.0f);
       const float kf = static_cast<float>(K);
@@ -500,6 +609,34 @@ __global__ void __launch_bounds__(512)
 #pragma unroll
         for (int i = 0; i < kChunk; ++i)
           if (in(i)) yrow[j0 + i] = v[i];
+      }
+    } else if (a.rms_quant != RMSQ_NONE) {
+      // ---- RMS preparation: peak of the rotated row, folded scale, codes ---
+      float peak;
+      if (a.rms_quant == RMSQ_FOLD) {
+        const float2 sm = cta_sum_max(sq_part, chunk_absmax(v, cnt), red, red_max, W);
+        const float moment = __fdiv_rn(sm.x, static_cast<float>(K));
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(moment, a.eps)));
+        peak = sm.y;
+      } else {
+        peak = cta_max(chunk_absmax(v, cnt), red, W);
+        inv = 1.0f;
+      }
+      const float scale = (peak == 0.0f) ? 1.0f : __fdiv_rn(__fmul_rn(peak, inv), 127.0f);
+      if (tid == 0) a.s[row] = scale;
+      int8_t* qrow = reinterpret_cast<int8_t*>(a.q) + row * K;
+      if (fullchunk && vec && (K % 16) == 0 && peak >= 0x1p-100f) {
+#pragma unroll
+        for (int w0 = 0; w0 < kChunk / 4; w0 += 4) {
+          uint32_t words[4];
+          rel_i8_fast16(v + 4 * w0, peak, words);
+          *reinterpret_cast<uint4*>(qrow + j0 + 4 * w0) =
+              make_uint4(words[0], words[1], words[2], words[3]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i)
+          if (in(i)) qrow[j0 + i] = static_cast<int8_t>(rel_i8_code(v[i], peak));
       }
     } else {
       // ---- row peak, per-row scale, codes ----------------------------------

@@ -178,7 +178,9 @@ cudaError_t launch_quant_t(const RowPrepArgs& a, cudaStream_t stream) {
 // width is a whole number of 16-byte vectors and whose codes can be stored
 // 8 (fp32: 4) bytes at a time.
 bool quant_rows_applicable(const RowPrepArgs& a, int x_dtype, int block, int out) {
-  if (block != 0 || a.norm != NORM_NONE || a.branch || a.signs || out == OUT_F32) return false;
+  if (block != 0 || a.norm != NORM_NONE || a.rms_quant != RMSQ_NONE || a.branch || a.signs ||
+      out == OUT_F32)
+    return false;
   const int vec = x_dtype == DT_F32 ? 4 : 8;
   const uintptr_t xa = reinterpret_cast<uintptr_t>(a.x), qa = reinterpret_cast<uintptr_t>(a.q);
   return (a.K % vec) == 0 && (xa % 16) == 0 && (qa % vec) == 0;

@@ -598,6 +598,7 @@ __global__ void __launch_bounds__(kThreads, MODE == kPlain ? 2 : 1)
 // need a row-group slot (rows padded to 1024 bytes for the swizzle) of at
 // most 64 KB; normalized rows a two-stage ring of at most 200 KB.
 inline int mode_of(const RowPrepArgs& a) {
+  if (a.rms_quant != RMSQ_NONE) return -1;  // row_prep_kernel's RMS folding form
   if (a.norm == NORM_NONE) return a.branch ? -1 : kPlain;
   return a.branch ? kNormGated : kNorm;
 }

@@ -6,6 +6,7 @@ The `cuda-b200` backend of the m5kernels operator contracts:
     fused_norm_hadamard_quantize,
     fused_gated_residual_norm_hadamard_quantize   (twin of m5kernels.norm_hadamard)
     projection_qk_rope                 (twin of m5kernels.qk_rope)
+    rms_quantize                       (twin of m5kernels.rms_quant)
     linear                             (the online quantize -> gemm stage in one call)
 All of them run hand-written CUDA kernels from libm5b200.so through its C ABI
 (include/m5b200.h); there is no CPU fallback.
@@ -16,9 +17,10 @@ from .hadamard import SUPPORTED_BLOCK_SIZES, hadamard_quantize, rotate
 from .linear import linear
 from .norm_hadamard import fused_gated_residual_norm_hadamard_quantize, fused_norm_hadamard_quantize
 from .qk_rope import projection_qk_rope, rope_tables
+from .rms_quant import rms_quantize
 
 __all__ = [
     "gemm", "quantize", "rotate", "hadamard_quantize", "SUPPORTED_BLOCK_SIZES",
     "fused_norm_hadamard_quantize", "fused_gated_residual_norm_hadamard_quantize",
-    "projection_qk_rope", "rope_tables", "linear",
+    "projection_qk_rope", "rope_tables", "linear", "rms_quantize",
 ]

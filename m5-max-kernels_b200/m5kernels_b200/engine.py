@@ -13,6 +13,8 @@ Backends (the `backend` string of run_case):
     norm_hadamard_gemm        cuda-b200-norm-fused fused norm/modulation/rotation/INT8 prep + GEMM
     gated_norm_hadamard_gemm  cuda-b200-residual-fused   gated residual + the above, R' written once
     qk_rope                   cuda-b200-qk-fused   H + INT8 prep + projection with RMSNorm + RoPE epilogue
+    rms_quant_gemm            cuda-b200-rms-folded RMS prep with the inverse RMS folded into the scale + GEMM
+                              cuda-b200-rms-direct RMS prep normalizing first + GEMM
 """
 
 from __future__ import annotations
@@ -33,12 +35,14 @@ from .cuda import gemm, quantize
 from .hadamard import hadamard_quantize, rotate
 from .norm_hadamard import fused_gated_residual_norm_hadamard_quantize, fused_norm_hadamard_quantize
 from .qk_rope import projection_qk_rope, rope_tables
+from .rms_quant import rms_quantize
 
 BACKENDS = {
     "gemm": ("cuda-b200", "cuda-b200-hadamard"),
     "norm_hadamard_gemm": ("cuda-b200-norm-fused",),
     "gated_norm_hadamard_gemm": ("cuda-b200-residual-fused",),
     "qk_rope": ("cuda-b200-qk-fused",),
+    "rms_quant_gemm": ("cuda-b200-rms-folded", "cuda-b200-rms-direct"),
 }
 
 
@@ -386,11 +390,154 @@ def prepare_qk_rope(c, backend, precision, seed, distribution, tile):
         "activation_prepare": prep, "online_activation_plus_gemm": online}, meta
 
 
+def validate_rms_config(c, backend, precision, distribution) -> dict:
+    """Semantics of an rms_quant_gemm case (src/m5kernels/rms_quant_gemm.py:14-65)."""
+    if backend not in BACKENDS["rms_quant_gemm"] or precision != "int8":
+        raise NotImplementedError(
+            "rms_quant_gemm supports cuda-b200-rms-direct/cuda-b200-rms-folded with INT8 only")
+    if c.get("op") != "rms_quant_gemm":
+        raise ValueError("operation must be rms_quant_gemm")
+    forbidden = {"shift", "norm", "round_output"}.intersection(c)
+    if forbidden:
+        raise NotImplementedError(f"unsupported RMS semantics options: {sorted(forbidden)}")
+    for key in ("m", "n", "k"):
+        if isinstance(c.get(key), bool) or not isinstance(c.get(key), int) or c[key] <= 0:
+            raise ValueError(f"{key} must be a positive integer")
+    cfg = c.get("rms_quant", {})
+    if not isinstance(cfg, dict):
+        raise ValueError("rms_quant must be a configuration object")
+    unknown = set(cfg) - {"block_size", "gamma", "threads", "epsilon", "sign_seed"}
+    if unknown:
+        raise NotImplementedError(
+            f"unsupported rms_quant options: {sorted(unknown)}; "
+            "this experiment requires RMS, zero shift and no BF16 intermediate")
+    config = dict(block_size=1, gamma="identity", threads=256, epsilon=1e-5, sign_seed=None)
+    config.update(cfg)
+    block = config["block_size"]
+    if isinstance(block, bool) or not isinstance(block, int) or block <= 0:
+        raise ValueError("block_size must be a positive integer")
+    if block not in (1, 256):
+        raise NotImplementedError("rms_quant_gemm supports block_size 1 or 256")
+    if c["k"] % block:
+        raise NotImplementedError("K must be divisible by block_size; padding is not implicit")
+    if config["gamma"] not in ("identity", "random"):
+        raise NotImplementedError("gamma must be identity or random")
+    threads = config["threads"]
+    if isinstance(threads, bool) or not isinstance(threads, int):
+        raise ValueError("threads must be an integer")
+    if threads not in (128, 256, 512):
+        raise NotImplementedError("supported threadgroup sizes are 128, 256 and 512")
+    eps = config["epsilon"]
+    if isinstance(eps, bool) or not isinstance(eps, (int, float)) or not np.isfinite(eps) or eps <= 0:
+        raise ValueError("epsilon must be positive and finite")
+    with np.errstate(over="ignore", under="ignore"):
+        eps32 = np.float32(eps)
+    if not np.isfinite(eps32) or eps32 <= 0:
+        raise ValueError("epsilon must remain positive and finite in float32")
+    sign_seed = config["sign_seed"]
+    if sign_seed is not None and (isinstance(sign_seed, bool) or not isinstance(sign_seed, int)
+                                  or sign_seed < 0):
+        raise ValueError("sign_seed must be a nonnegative integer or null")
+    if distribution not in ("normal", "outliers", "zeros"):
+        raise ValueError("distribution must be normal, outliers or zeros")
+    return config
+
+
+def prepare_rms_quant_gemm(c, backend, precision, seed, distribution, tile):
+    """RMS scale-folding (or direct) INT8 preparation + W8A8 GEMM, BF16 out.
+
+    Twin of src/m5kernels/rms_quant_gemm.py:68-260: identical BF16 inputs and
+    weights and FP32 gamma for both backends of one seed; weights are signed
+    (and rotated for block 256) and quantized per output channel offline.
+    """
+    cfg = validate_rms_config(c, backend, precision, distribution)
+    from .reference_checks import rms_reference_rows
+
+    dev = torch.device("cuda")
+    m, n, k = c["m"], c["n"], c["k"]
+    block, eps, sign_seed = cfg["block_size"], cfg["epsilon"], cfg["sign_seed"]
+    fold = backend == "cuda-b200-rms-folded"
+    x, w = _inputs(c, seed, distribution, dev)
+    g = torch.Generator(device="cpu").manual_seed(seed + 1)
+    gamma = (1 + 0.2 * torch.randn(k, generator=g) if cfg["gamma"] == "random"
+             else torch.ones(k)).float()
+    if sign_seed is not None:
+        from numpy.random import PCG64, Generator
+
+        draws = Generator(PCG64(sign_seed)).integers(0, 2, size=k, dtype=np.int8)
+        signs_np = (2 * draws - 1).astype(np.int8)
+    else:
+        signs_np = np.ones(k, np.int8)
+    gamma_d, signs = gamma.to(dev), torch.from_numpy(signs_np).to(dev)
+    ri, ci = sample_indices(m), sample_indices(n)
+
+    def offline_weight_prepare():
+        if block == 1:
+            return quantize(w.float() * signs.float(), "int8")
+        return hadamard_quantize(w, block, signs, "int8")
+
+    def activation():
+        return rms_quantize(x, gamma_d, signs, block, threads=cfg["threads"], fold_scale=fold,
+                            epsilon=eps)
+
+    bq, sb = offline_weight_prepare()
+    aq, sa = activation()
+    ref_x = _f64(x[torch.as_tensor(ri, device=dev)])
+    ref_w = _f64(w[torch.as_tensor(ci, device=dev)])
+    ref_a = rms_reference_rows(ref_x, gamma.numpy(), signs_np, block, eps)
+    ref_norm = ref_x * ref_a["inverse_rms"][:, None] * gamma.double().numpy()
+    original = ref_norm @ ref_w.T
+    actual_a = _decoded(aq, sa, ri, "int8")
+    expected = actual_a @ _decoded(bq, sb, ci, "int8").T
+    idx = torch.as_tensor(ri, device=dev)
+    activation_error = metrics(actual_a, ref_a["dequantized"])
+    scale_error = metrics(_f64(sa[idx]), ref_a["scales"])
+    max_code_error = float(np.max(np.abs(_f64(aq[idx]) - ref_a["quantized"])))
+    finite = bool(torch.isfinite(sa).all() and (sa > 0).all() and (aq >= -127).all()
+                  and torch.isfinite(sb).all() and (sb > 0).all())
+    transform_pass = bool(finite and activation_error["finite"]
+                          and activation_error["relative_l2"] <= 0.008
+                          and scale_error["finite"] and scale_error["relative_l2"] <= 1e-5
+                          and max_code_error <= 1)
+
+    def compute(q, s):
+        return gemm(q, bq, "int8", tile, a_scales=s, b_scales=sb, output_dtype=torch.bfloat16)
+
+    def fn():
+        return compute(aq, sa)
+
+    def online():
+        return compute(*activation())
+
+    def check(y):
+        return _f64(y[torch.as_tensor(ri, device=dev)][:, torch.as_tensor(ci, device=dev)])
+
+    meta = dict(compute_path=f"rms_{'folded' if fold else 'direct'}_prep + tcgen05_int8_gemm",
+                input_dtype="bf16", output_dtype="bf16", preparation_dtype="fp32",
+                mac_operations=2 * m * n * k, sample_rows=ri.tolist(), sample_cols=ci.tolist(),
+                norm="rms", epsilon=eps, gamma=cfg["gamma"],
+                gamma_sha256=hashlib.sha256(gamma.numpy().tobytes()).hexdigest(),
+                fold_scale=fold, additive_shift=False, normalization_rounding="fp32",
+                quantization="symmetric_per_token_rotated_A_per_output_channel_rotated_W",
+                weight_preparation_in_online=False, weight_preparation_timed=True,
+                all_preparation_values_finite=finite, transform_pass=transform_pass,
+                activation_implementation_error=activation_error,
+                activation_scale_error=scale_error,
+                activation_max_code_difference=max_code_error,
+                transform=dict(kind="signed_identity" if block == 1
+                               else "normalized_block_sylvester_hadamard",
+                               block_size=block, sign_seed=sign_seed, threads=cfg["threads"]))
+    stages = {"activation_prepare": activation, "online_activation_plus_gemm": online,
+              "offline_weight_prepare": offline_weight_prepare}
+    return fn, check, expected, original, stages, meta
+
+
 PREPARE = {
     "gemm": prepare_gemm,
     "norm_hadamard_gemm": prepare_norm_hadamard_gemm,
     "gated_norm_hadamard_gemm": prepare_norm_hadamard_gemm,
     "qk_rope": prepare_qk_rope,
+    "rms_quant_gemm": prepare_rms_quant_gemm,
 }
 
 QUALITY_LIMIT = {"int8": 0.05, "fp8": 0.10}

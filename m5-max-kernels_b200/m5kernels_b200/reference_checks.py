@@ -83,3 +83,24 @@ def qk_reference_rows(dot: np.ndarray, gamma, cos, sin, eps: float, heads: int) 
     out[..., :half] = lo * c[:, None, :] - hi * s[:, None, :]
     out[..., half:2 * half] = hi * c[:, None, :] + lo * s[:, None, :]
     return _bf16_round(out).transpose(1, 0, 2)
+
+
+def rms_reference_rows(x_rows: np.ndarray, gamma: np.ndarray, signs: np.ndarray, block: int,
+                       eps: float) -> dict:
+    """Ideal folded RMS preparation of sampled rows (float64).
+
+    The harness check of src/m5kernels/rms_quant_gemm.py:108-118: inverse RMS of
+    the original rows, U = (X * gamma) D H, codes rint(U / (peak / 127)),
+    scales peak / 127 * r, zero rows scale 1.
+    """
+    x = np.asarray(x_rows, dtype=np.float64)
+    inv = 1.0 / np.sqrt((x * x).mean(axis=1) + float(eps))
+    weighted = x * np.asarray(gamma, dtype=np.float64) * np.asarray(signs, dtype=np.float64)
+    unscaled = weighted / np.sqrt(block) if block == 1 else _fwht(weighted, block)
+    peak = np.abs(unscaled).max(axis=1)
+    unit = np.where(peak == 0, 1.0, peak / 127.0)
+    codes = np.clip(np.rint(unscaled / unit[:, None]), -127, 127)
+    scales = np.where(peak == 0, 1.0, unit * inv)
+    return {"inverse_rms": inv, "quantized": codes, "scales": scales,
+            "dequantized": codes * scales[:, None],
+            "normalized_rotated": unscaled * inv[:, None]}

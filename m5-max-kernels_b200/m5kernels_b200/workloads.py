@@ -17,6 +17,7 @@ FIELDS = {
     "norm_hadamard_gemm": ("m", "n", "k"),
     "gated_norm_hadamard_gemm": ("m", "n", "k"),
     "qk_rope": ("m", "n", "k"),
+    "rms_quant_gemm": ("m", "n", "k"),
 }
 
 
@@ -48,6 +49,18 @@ def _baseline_cases():
     return cases
 
 
+def _rms_cases():
+    # the reference's rms-quant manifest shapes: Q-sized GEMM, zero-shift RMS prep
+    cases = []
+    for m in (4096, 9914):
+        for name, block, gamma in (("plain", 1, "identity"), ("weighted", 1, "random"),
+                                   ("weighted_h256", 256, "random")):
+            cases.append(dict(id=f"rms.{name}.m{m}", op="rms_quant_gemm", m=m, n=7168, k=5376,
+                              rms_quant=dict(block_size=block, gamma=gamma, threads=256,
+                                             epsilon=1e-5)))
+    return cases
+
+
 SUITES = {
     "baseline": {"schema_version": 1, "cases": _baseline_cases()},
     "smoke": {"schema_version": 1, "cases": [
@@ -58,7 +71,10 @@ SUITES = {
         dict(id="smoke.norm", op="norm_hadamard_gemm", m=64, n=256, k=768,
              fusion=dict(norm="rms", block_size=256)),
         dict(id="smoke.qk", op="qk_rope", m=77, n=256, k=512, rope_half=48),
+        dict(id="smoke.rms", op="rms_quant_gemm", m=70, n=256, k=768,
+             rms_quant=dict(block_size=256, gamma="random", sign_seed=5)),
     ]},
+    "rms_quant": {"schema_version": 1, "cases": _rms_cases()},
 }
 
 

@@ -58,6 +58,8 @@ def lib() -> ctypes.CDLL:
         _lib.m5o_gemm_epilogue_i32.restype = None
         _lib.m5o_qk_rope_from_acc.argtypes = [P, I64, I64, P, P, P, P, P, I32, F, P]
         _lib.m5o_qk_rope_from_acc.restype = None
+        _lib.m5o_rms_quantize.argtypes = [P, I32, P, P, I64, I64, I32, I32, F, P, P]
+        _lib.m5o_rms_quantize.restype = None
     return _lib
 
 
@@ -115,6 +117,23 @@ def quantize(x, mode="int8"):
 
 def rotate(x, block, signs=None):
     return row_prep(x, block=block, signs=signs, out="f32")["y"]
+
+
+def rms_quantize(x, gamma, signs, block_size=1, *, fold_scale=True, epsilon=1e-5):
+    """RMS scale-folding (or direct) INT8 preparation; returns (codes, scales).
+
+    block_size 1 means no rotation, as in the reference's rms_quantize.
+    """
+    x = _cpu(x)
+    rows, k = x.shape
+    gamma = _cpu(gamma.to(torch.float32))
+    signs = _cpu(signs.to(torch.int8))
+    q = torch.empty((rows, k), dtype=torch.int8)
+    s = torch.empty((rows,), dtype=torch.float32)
+    lib().m5o_rms_quantize(_ptr(x), _code(x), _ptr(gamma), _ptr(signs), rows, k,
+                           0 if block_size == 1 else int(block_size), int(bool(fold_scale)),
+                           float(epsilon), _ptr(q), _ptr(s))
+    return q, s
 
 
 def e4m3_encode_scalar(v: float) -> int:

@@ -17,6 +17,8 @@
  *   W8A8 GEMM + scale/bias/gate epilogue src/m5kernels/metal.py:167-207
  *   Q/K RMSNorm + split-half RoPE        src/m5kernels/qk_rope_reference.py:45-134,
  *                                          shaders/qk_rope_body.metal:1-20
+ *   RMS scale-folding INT8 preparation   src/m5kernels/rms_quant_reference.py:24-89,
+ *                                          rms_quant.py:41-117, shaders/rms_quant.metal:1-97
  *
  * The reference's own references are float64; its GPU kernels round in FP32
  * with an unspecified reduction order, which is why the reference accepts a
@@ -268,6 +270,51 @@ void m5o_row_prep(const void* x, int x_dtype, const void* branch, const void* ga
     uint8_t* qrow = (uint8_t*)q + r * K;
     for (int64_t j = 0; j < K; ++j)
       qrow[j] = out == OUT_E4M3 ? e4m3_code(v[j], sc) : (uint8_t)int8_code(v[j], sc);
+  }
+  free(v);
+}
+
+/*
+ * RMS preparation with the inverse RMS folded into the row scale (fold != 0)
+ * or applied before gamma (fold == 0), INT8 codes only.  gamma is fp32[K],
+ * signs int8[K] (+-1), block 0 = no rotation.  Per row:
+ *   r = 1 / sqrt(sum(x^2) / K + eps), sum in the canonical order;
+ *   u_j = (x_j * gamma_j) * sign_j          (fold)
+ *   u_j = ((x_j * r) * gamma_j) * sign_j    (direct)
+ *   u = blockwise Hadamard butterflies, then * fp32(1/sqrt(block));
+ *   peak = max |u|; scale = peak == 0 ? 1 : (peak * r) / 127 (fold) or
+ *   peak / 127 (direct); q_j = peak == 0 ? 0 : clip(rint((u_j / peak) * 127)).
+ */
+void m5o_rms_quantize(const void* x, int x_dtype, const float* gamma, const int8_t* signs,
+                      int64_t rows, int64_t K, int block, int fold, float eps, int8_t* q,
+                      float* s) {
+  float* v = (float*)malloc(sizeof(float) * (size_t)K);
+  const int W = m5o_row_prep_warps(K, block);
+  const float inv_sqrt_block = block > 0 ? (float)(1.0 / sqrt((double)block)) : 1.0f;
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t j = 0; j < K; ++j) v[j] = load_elem(x, x_dtype, r * K + j);
+    const float moment = row_reduce(v, K, W, 1, 0.0f) / (float)K;
+    const float inv = 1.0f / sqrtf(moment + eps);
+    for (int64_t j = 0; j < K; ++j) {
+      float t = fold ? v[j] : v[j] * inv;
+      t = t * gamma[j];
+      if (signs && signs[j] < 0) t = -t;
+      v[j] = t;
+    }
+    if (block > 0) {
+      for (int64_t b0 = 0; b0 < K; b0 += block) fwht_block(v + b0, block);
+      for (int64_t j = 0; j < K; ++j) v[j] = v[j] * inv_sqrt_block;
+    }
+    float peak = 0.0f;
+    for (int64_t j = 0; j < K; ++j) peak = fmaxf(peak, fabsf(v[j]));
+    s[r] = peak == 0.0f ? 1.0f : (peak * (fold ? inv : 1.0f)) / 127.0f;
+    for (int64_t j = 0; j < K; ++j) {
+      float c = 0.0f;
+      if (peak != 0.0f) c = rintf((v[j] / peak) * 127.0f);
+      if (c > 127.0f) c = 127.0f;
+      if (c < -127.0f) c = -127.0f;
+      q[r * K + j] = (int8_t)(int)c;
+    }
   }
   free(v);
 }

@@ -280,3 +280,59 @@ def qk_rope_reference(projected, gamma, cos, sin, *, epsilon=1e-5, projection_bf
         "rotated": rotated,
         "output": np.ascontiguousarray(out.transpose(1, 0, 2)),
     }
+
+
+# ------------------------------------------------------- RMS scale folding
+
+
+def rms_quantize_reference(x, gamma, signs=None, block_size=1, eps=1e-5) -> dict:
+    """RMS(X) * gamma, signed block Hadamard, per-row INT8 with folded scales.
+
+    Restates src/m5kernels/rms_quant_reference.py:24-89 in float64:
+    r = 1 / sqrt(mean(X^2) + eps) from the ORIGINAL rows; U = (X * gamma) D H;
+    codes rint(U / (peak(U) / 127)) clipped to +-127 (nearest even), scales
+    peak(U) / 127 * r; a row with peak(U) == 0 gets codes 0 and scale 1.  The
+    positive factor r changes the scales only, never the codes.
+    """
+    if isinstance(eps, bool) or not np.isscalar(eps) or np.iscomplexobj(eps):
+        raise ValueError("eps must be a positive finite real scalar")
+    if not np.isfinite(eps) or eps <= 0:
+        raise ValueError("eps must be a positive finite real scalar")
+    xv, gv = np.asarray(x), np.asarray(gamma)
+    for name, value in (("input", xv), ("gamma", gv)):
+        if np.iscomplexobj(value):
+            raise ValueError(f"{name} must be real")
+    xv = np.asarray(xv, dtype=np.float64)
+    gv = np.asarray(gv, dtype=np.float64)
+    if not np.isfinite(xv).all():
+        raise ValueError("input must be finite")
+    if not np.isfinite(gv).all():
+        raise ValueError("gamma must be finite")
+    if xv.ndim != 2 or 0 in xv.shape:
+        raise ValueError("input must have nonempty shape [M,K]")
+    if gv.shape != (xv.shape[1],):
+        raise ValueError("gamma must have shape [K]")
+    with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+        moment = np.mean(xv * xv, axis=1)
+        inverse_rms = 1.0 / np.sqrt(moment + float(eps))
+        weighted = xv * gv
+    if (not np.isfinite(moment).all() or not np.isfinite(inverse_rms).all()
+            or not np.all(inverse_rms > 0) or not np.isfinite(weighted).all()):
+        raise ValueError("RMS or gamma multiplication exceeds finite float64 range")
+    unscaled = block_hadamard_reference(weighted, block_size, signs)
+    peak = np.max(np.abs(unscaled), axis=1)
+    nonzero = peak != 0
+    unscaled_scales = np.where(nonzero, peak / 127.0, 1.0)
+    with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+        normalized_rotated = unscaled * inverse_rms[:, None]
+        scales = np.where(nonzero, unscaled_scales * inverse_rms, 1.0)
+    codes = np.clip(np.rint(unscaled / unscaled_scales[:, None]), -127, 127).astype(np.int8)
+    return {
+        "normalized_rotated": normalized_rotated,
+        "quantized": codes,
+        "scales": scales,
+        "dequantized": codes.astype(np.float64) * scales[:, None],
+        "unscaled_rotated": unscaled,
+        "inverse_rms": inverse_rms,
+        "unscaled_scales": unscaled_scales,
+    }

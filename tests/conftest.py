@@ -25,3 +25,10 @@ def golden():
     import numpy as np
 
     return dict(np.load(ROOT / "tests" / "golden" / "reference_vectors.npz"))
+
+
+@pytest.fixture(scope="session")
+def rms_golden():
+    import numpy as np
+
+    return dict(np.load(ROOT / "tests" / "golden" / "rms_quant_vectors.npz"))

@@ -15,6 +15,8 @@ Reference functions exercised (file:line in the reference):
   norm_hadamard_reference.norm_hadamard_quantize_reference   norm_hadamard_reference.py:67-94
   gated_residual_reference.gated_residual_reference   gated_residual_reference.py:21-60
   qk_rope_reference.bf16_round_reference / qk_rope_reference   qk_rope_reference.py:24-134
+  rms_quant_reference.rms_quantize_reference   rms_quant_reference.py:24-89
+      (written to rms_quant_vectors.npz; `--only rms` regenerates that file alone)
 """
 
 from __future__ import annotations
@@ -45,6 +47,71 @@ def _import_reference():
     return numerics, hadamard_reference, norm_hadamard_reference, gated_residual_reference, qk_rope_reference
 
 
+def make_rms() -> int:
+    """RMS scale-folding cases (rms_quant_reference.rms_quantize_reference)."""
+    _import_reference()
+    from m5kernels import hadamard_reference as had
+    from m5kernels import rms_quant_reference as rq
+
+    out = {}
+    cases = []
+
+    def add(name, x, gamma, signs, block, eps=1e-5):
+        x = np.asarray(x, dtype=np.float32)
+        gamma = np.asarray(gamma, dtype=np.float32)
+        signs = np.asarray(signs, dtype=np.int8)
+        r = rq.rms_quantize_reference(x.astype(np.float64), gamma.astype(np.float64), signs, block,
+                                      eps=eps)
+        pre = f"rms_{name}_"
+        out[pre + "x"], out[pre + "gamma"], out[pre + "signs"] = x, gamma, signs
+        out[pre + "block"], out[pre + "eps"] = np.int64(block), np.float64(eps)
+        for key in ("quantized", "scales", "inverse_rms", "unscaled_scales"):
+            out[pre + key] = r[key]
+        cases.append(name)
+
+    rng = np.random.default_rng(2021)
+    # H256 over three blocks, bf16-valued rows, signed gamma
+    add("h256", bf16_value(bf16_bits(rng.standard_normal((5, 768), dtype=np.float32))),
+        rng.uniform(-1.7, 1.7, 768), had.hadamard_signs(768, 61), 256)
+    # no rotation, ragged K
+    add("plain769", rng.standard_normal((5, 769), dtype=np.float32), rng.uniform(-1.7, 1.7, 769),
+        had.hadamard_signs(769, 61), 1)
+    # outlier columns under H128
+    x = rng.standard_normal((4, 384), dtype=np.float32)
+    x[:, ::37] *= 100
+    add("outliers", x, rng.uniform(-1, 1, 384), had.hadamard_signs(384, 5), 128)
+    # the peak must follow gamma and the rotation, not max |X|
+    x = rng.standard_normal((3, 512), dtype=np.float32)
+    x[:, 0] = 100
+    gamma = rng.uniform(-1.7, 1.7, 512).astype(np.float32)
+    gamma[0] = 1e-3
+    gamma[1::31] *= 100
+    add("weighted_peak", x, gamma, had.hadamard_signs(512, 7), 64)
+    # tiny rows: epsilon dominates the RMS, codes unchanged
+    add("tiny", rng.standard_normal((3, 256), dtype=np.float32) * np.float32(1e-9),
+        rng.uniform(-1, 1, 256), had.hadamard_signs(256, 3), 32)
+    # large epsilon
+    add("eps1", rng.standard_normal((3, 512), dtype=np.float32), rng.uniform(-1, 1, 512),
+        had.hadamard_signs(512, 11), 128, eps=1.0)
+    # exact INT8 ties (peak 127 makes the quantizer step one)
+    add("ties", [[127, 2.5, 3.5, -2.5, -3.5, 0, -127, 1.5]], np.ones(8), np.ones(8), 1)
+    # a zero row among others, and an all-zero gamma
+    x = rng.standard_normal((3, 256), dtype=np.float32)
+    x[1] = 0
+    add("zero_row", x, rng.uniform(-1, 1, 256), had.hadamard_signs(256, 13), 256)
+    add("zero_gamma", np.full((3, 768), 2.0), np.zeros(768), had.hadamard_signs(768, 9), 256)
+    # integer rows with unit gamma: q = rint(127 x / peak) directly
+    for width in (17, 257):
+        vals = np.resize(np.arange(-127, 128, dtype=np.float32), (3, width))
+        add(f"int{width}", vals, np.ones(width), np.ones(width), 1)
+    out["rms_cases"] = np.array(cases)
+
+    path = HERE / "rms_quant_vectors.npz"
+    np.savez_compressed(path, **out)
+    print(f"wrote {path} ({path.stat().st_size} bytes, {len(cases)} cases)")
+    return 0
+
+
 def bf16_bits(x) -> np.ndarray:
     """float32 -> bf16 bits (nearest even), as uint16."""
     b = np.asarray(x, dtype=np.float32).view(np.uint32)
@@ -56,6 +123,9 @@ def bf16_value(bits) -> np.ndarray:
 
 
 def main() -> int:
+    if sys.argv[1:] == ["--only", "rms"]:
+        return make_rms()
+    make_rms()
     numerics, had, nh, gr, qk = _import_reference()
     out = {}
 

@@ -103,3 +103,38 @@ def test_cli_shapes_and_doctor_without_gpu(capsys):
     assert "c2.ffn_down.m4096" in out
     rc = cli.main(["doctor"])
     assert rc == (0 if torch.cuda.is_available() else 1)
+
+
+def test_rms_case_semantics_are_validated_before_any_device_work():
+    from m5kernels_b200 import engine
+
+    base = dict(id="r", op="rms_quant_gemm", m=8, n=8, k=512)
+    ok = engine.validate_rms_config(base, "cuda-b200-rms-folded", "int8", "normal")
+    assert ok["block_size"] == 1 and ok["gamma"] == "identity" and ok["threads"] == 256
+    for bad, err in [
+        (dict(base, shift=1), NotImplementedError),
+        (dict(base, rms_quant=dict(block_size=128)), NotImplementedError),
+        (dict(base, rms_quant=dict(gamma="learned")), NotImplementedError),
+        (dict(base, rms_quant=dict(threads=64)), NotImplementedError),
+        (dict(base, rms_quant=dict(epsilon=0)), ValueError),
+        (dict(base, rms_quant=dict(epsilon=1e-300)), ValueError),
+        (dict(base, rms_quant=dict(sign_seed=-1)), ValueError),
+        (dict(base, rms_quant=dict(norm="layer")), NotImplementedError),
+        (dict(base, k=300, rms_quant=dict(block_size=256)), NotImplementedError),
+    ]:
+        with pytest.raises(err):
+            engine.validate_rms_config(bad, "cuda-b200-rms-folded", "int8", "normal")
+    with pytest.raises(NotImplementedError):
+        engine.validate_rms_config(base, "cuda-b200-rms-folded", "fp8", "normal")
+    with pytest.raises(NotImplementedError):
+        engine.validate_rms_config(base, "cuda-b200", "int8", "normal")
+
+
+def test_rms_suite_mirrors_the_reference_manifest():
+    from m5kernels_b200 import workloads
+
+    cases = workloads.load("rms_quant")["cases"]
+    assert [c["id"] for c in cases] == [
+        "rms.plain.m4096", "rms.weighted.m4096", "rms.weighted_h256.m4096",
+        "rms.plain.m9914", "rms.weighted.m9914", "rms.weighted_h256.m9914"]
+    assert all((c["n"], c["k"]) == (7168, 5376) for c in cases)

@@ -31,3 +31,25 @@ def test_gemm_case_fp8_and_outliers(engine, precision):
     c = dict(id="t", op="gemm", m=300, n=520, k=1024, weight_std=0.02)
     r = engine.run_case(c, "cuda-b200", precision, distribution="outliers", warmup=1, repeat=2)
     assert r["status"] == "ok", r.get("reason")
+
+
+@pytest.mark.parametrize("backend", ["cuda-b200-rms-folded", "cuda-b200-rms-direct"])
+@pytest.mark.parametrize("distribution", ["normal", "outliers", "zeros"])
+@pytest.mark.parametrize("block,gamma,sign_seed", [(1, "identity", None), (256, "random", 3)])
+def test_rms_quant_gemm_backends(engine, backend, distribution, block, gamma, sign_seed):
+    c = dict(id="t.rms", op="rms_quant_gemm", m=300, n=384, k=1280,
+             rms_quant=dict(block_size=block, gamma=gamma, sign_seed=sign_seed))
+    r = engine.run_case(c, backend, "int8", distribution=distribution, warmup=1, repeat=2)
+    assert r["status"] == "ok", (r.get("reason"), r.get("activation_implementation_error"))
+    assert r["transform_pass"] and r["activation_max_code_difference"] <= 1
+    assert set(r["stages"]) == {"activation_prepare", "online_activation_plus_gemm",
+                                "offline_weight_prepare"}
+
+
+def test_rms_folded_and_direct_share_inputs(engine):
+    c = dict(id="t.rms", op="rms_quant_gemm", m=256, n=256, k=768,
+             rms_quant=dict(block_size=256, gamma="random", sign_seed=1))
+    a = engine.run_case(c, "cuda-b200-rms-folded", "int8", warmup=1, repeat=2)
+    b = engine.run_case(c, "cuda-b200-rms-direct", "int8", warmup=1, repeat=2)
+    assert a["status"] == b["status"] == "ok"
+    assert a["gamma_sha256"] == b["gamma_sha256"]
