@@ -138,6 +138,40 @@ M5B_API int m5b_rms_quantize(const void* x, int x_dtype, int64_t rows, int64_t k
                              int fold_scale, float epsilon, int8_t* q, float* scales,
                              void* stream);
 
+/* Staged comparators: one stage of the fused kernels on its own, with the same
+ * FP32 operations in the same order, so that a staged pipeline reproduces the
+ * fused result bit for bit (fusion-gain baselines and staged == fused checks).
+ *
+ * m5b_unfused_norm: y = norm(x) * gamma * (1 + scale[map]) + shift[map] with
+ * the statistics and modulation of m5b_fused_norm_hadamard_quantize, no
+ * signs, rotation or quantization.  y is [rows, k] in x_dtype when
+ * round_output != 0 (fp32 when x is fp32), else fp32.
+ * Replaces src/m5kernels/norm_hadamard.py:321-348 (unfused_norm). */
+M5B_API int m5b_unfused_norm(const void* x, int x_dtype, int64_t rows, int64_t k,
+                             const void* gamma, int gamma_dtype, const void* scale,
+                             int scale_dtype, const void* shift, int shift_dtype,
+                             const int32_t* row_map, int64_t table_rows, int norm, float epsilon,
+                             int round_output, void* y, void* stream);
+
+/* m5b_gated_residual_add: out = cast(R + branch * gate[gate_map]) (one FP32
+ * fused multiply-add, then RNE to x_dtype), the residual_out of
+ * m5b_fused_gated_residual_norm_hadamard_quantize.  residual, branch and out
+ * share x_dtype; gate is [k], or [gate_rows, k] with gate_row_map[rows].
+ * Replaces src/m5kernels/norm_hadamard.py:280-300 (gated_residual_add). */
+M5B_API int m5b_gated_residual_add(const void* residual, const void* branch, int x_dtype,
+                                   int64_t rows, int64_t k, const void* gate, int gate_dtype,
+                                   const int32_t* gate_row_map, int64_t gate_rows, void* out,
+                                   void* stream);
+
+/* m5b_qk_norm_rope: the Q/K post-processing of m5b_projection_qk_rope applied
+ * to a stored bf16 projection [m, n] (n % 128 == 0): per (row, head)
+ * r = 1/sqrt(mean(z^2) + eps), u = z * r * gamma, split-half RoPE on j < 2R,
+ * out bf16 [n/128, m, 128].  projected and out 16-byte aligned.
+ * Replaces src/m5kernels/qk_rope.py:185-203 (qk_norm_rope). */
+M5B_API int m5b_qk_norm_rope(const void* projected, int64_t m, int64_t n, const void* gamma,
+                             const void* cos, const void* sin, int rope_half, float epsilon,
+                             void* out, void* stream);
+
 /* C[m, n] = epilogue(A[m, k] . B[n, k]^T) on tcgen05 tensor cores.
  *   mode INT8: int8 operands, INT32 accumulation; FP8: E4M3 operands, FP32
  *   accumulation (k % 128 == 0); BF16 / FP16: FP32 accumulation.

@@ -378,6 +378,82 @@ int m5b_rms_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, const 
   return run_row_prep(a, x_dtype, block_size == 1 ? 0 : block_size, OUT_INT8, stream);
 }
 
+int m5b_unfused_norm(const void* x, int x_dtype, int64_t rows, int64_t k, const void* gamma,
+                     int gamma_dtype, const void* scale, int scale_dtype, const void* shift,
+                     int shift_dtype, const int32_t* row_map, int64_t table_rows, int norm,
+                     float epsilon, int round_output, void* y, void* stream) {
+  RowPrepArgs a;
+  int rc = prep_common(a, x, x_dtype, rows, k);
+  if (rc) return rc;
+  rc = norm_setup(a, gamma, gamma_dtype, scale, scale_dtype, shift, shift_dtype, row_map,
+                  table_rows, norm, epsilon, round_output);
+  if (rc) return rc;
+  if (!y) return fail(M5B_EINVAL, "output pointer is NULL");
+  a.y = static_cast<float*>(y);
+  // rounded rows of a 16-bit input leave in that dtype, everything else as fp32
+  const int out = (round_output && x_dtype != M5B_F32) ? OUT_ROW : OUT_F32;
+  return run_row_prep(a, x_dtype, 0, out, stream);
+}
+
+int m5b_gated_residual_add(const void* residual, const void* branch, int x_dtype, int64_t rows,
+                           int64_t k, const void* gate, int gate_dtype,
+                           const int32_t* gate_row_map, int64_t gate_rows, void* out,
+                           void* stream) {
+  int rc = check_rows(rows, k);
+  if (rc) return rc;
+  if (!float_dtype(x_dtype)) return fail(M5B_EINVAL, "residual must have floating dtype");
+  if (!residual || !branch || !gate || !out)
+    return fail(M5B_EINVAL, "residual, branch, gate and out are required");
+  if (!float_dtype(gate_dtype)) return fail(M5B_EINVAL, "gate must have floating dtype");
+  if (gate_row_map && gate_rows <= 0)
+    return fail(M5B_EINVAL, "mapped gate must have nonempty shape [P,K]");
+  GatedAddArgs g{};
+  g.residual = residual;
+  g.branch = branch;
+  g.gate = gate;
+  g.gate_dtype = gate_dtype;
+  g.gate_row_map = gate_row_map;
+  g.rows = rows;
+  g.K = k;
+  g.out = out;
+  g.vec_ok = (k % 8) == 0 && aligned(residual, 16) && aligned(branch, 16) && aligned(gate, 16) &&
+             aligned(out, 16);
+  cudaError_t e = launch_gated_add(g, x_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gated residual launch");
+  return ok();
+}
+
+int m5b_qk_norm_rope(const void* projected, int64_t m, int64_t n, const void* gamma,
+                     const void* cos, const void* sin, int rope_half, float epsilon, void* out,
+                     void* stream) {
+  if (m <= 0 || n <= 0 || n % 128)
+    return fail(M5B_EINVAL, "projection must have nonempty [M,N] shape with whole 128-wide heads");
+  if (m > 0x7fffffffLL || n > 0x7fffffffLL)
+    return fail(M5B_EUNSUPPORTED, "matrix dimensions exceed 2^31-1");
+  if (rope_half < 1 || rope_half > 64)
+    return fail(M5B_EINVAL, "cos must have shape [M,rope_half] with rope_half in [1,64]");
+  if (!(epsilon > 0.0f) || !std::isfinite(epsilon))
+    return fail(M5B_EINVAL, "epsilon must be a positive finite real scalar");
+  if (!projected || !gamma || !cos || !sin || !out)
+    return fail(M5B_EINVAL, "projected, gamma, cos, sin and out are required");
+  if (!aligned(projected, 16) || !aligned(out, 16))
+    return fail(M5B_EINVAL, "projection and output base addresses must be 16-byte aligned");
+  QkNormArgs q{};
+  q.projected = projected;
+  q.M = m;
+  q.N = n;
+  q.gamma = gamma;
+  q.cos = cos;
+  q.sin = sin;
+  q.rope_half = rope_half;
+  q.eps = epsilon;
+  q.out = out;
+  q.fast = rope_half % 8 == 0 && aligned(gamma, 16) && aligned(cos, 16) && aligned(sin, 16);
+  cudaError_t e = launch_qk_norm_rope(q, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "Q/K normalization launch");
+  return ok();
+}
+
 // A CTA pair (cta_group::2, 256 x 256 tiles) when the problem has at least
 // one full pair tile of rows and more than 128 output columns.
 static bool use_pair(int epi, int64_t m, int64_t n) {

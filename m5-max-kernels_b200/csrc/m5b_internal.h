@@ -51,7 +51,9 @@ inline cudaError_t launch_shape(const void* kern, int threads, int smem,
 }
 
 enum NormKind : int { NORM_NONE = 0, NORM_RMS = 1, NORM_LAYER = 2 };
-enum RowOut : int { OUT_INT8 = 0, OUT_E4M3 = 1, OUT_F32 = 2 };
+// OUT_ROW: the (modulated) row itself in the input dtype, no rotation -- the
+// staged norm + modulation comparator; OUT_F32 writes fp32 rows.
+enum RowOut : int { OUT_INT8 = 0, OUT_E4M3 = 1, OUT_F32 = 2, OUT_ROW = 3 };
 // RMS scale folding (codes from (X gamma) D H, inverse RMS in the row scale)
 // and its direct counterpart (normalize first); both INT8 only.
 enum RmsQuant : int { RMSQ_NONE = 0, RMSQ_FOLD = 1, RMSQ_DIRECT = 2 };
@@ -79,7 +81,7 @@ struct RowPrepArgs {
   int params_vec;              // gamma / scale / shift / gate rows allow 16-byte loads
   void* q;                     // [rows, K] int8 or E4M3 codes
   float* s;                    // [rows] per-row scales
-  float* y;                    // [rows, K] fp32 rotated values (OUT_F32)
+  float* y;                    // [rows, K] fp32 rotated values (OUT_F32), or input-dtype rows (OUT_ROW)
   void* r_out;                 // [rows, K] updated residual (gated)
   unsigned int* status;        // device status word (bounded-wait errors)
 };
@@ -101,6 +103,32 @@ cudaError_t launch_quant_rows(const RowPrepArgs& a, const RowMaps& m, int x_dtyp
                               cudaStream_t stream);
 cudaError_t launch_row_prep(const RowPrepArgs& a, const RowMaps& maps, int x_dtype, int block,
                             int out, cudaStream_t stream);
+
+// Staged comparators (staged.cu).
+struct GatedAddArgs {
+  const void* residual;        // [rows, K]
+  const void* branch;          // [rows, K], the residual's dtype
+  const void* gate;            // [K] or [P, K]
+  int gate_dtype;
+  const int32_t* gate_row_map; // [rows] gate table index, or null
+  int64_t rows, K;
+  int vec_ok;                  // K % 8 == 0 and every pointer 16-byte aligned
+  void* out;                   // [rows, K] updated residual, the residual's dtype
+};
+cudaError_t launch_gated_add(const GatedAddArgs& a, int x_dtype, cudaStream_t stream);
+
+struct QkNormArgs {
+  const void* projected;       // [M, N] bf16, N % 128 == 0, 16-byte aligned
+  int64_t M, N;
+  const void* gamma;           // [128] bf16
+  const void* cos;             // [M, rope_half] bf16
+  const void* sin;             // [M, rope_half] bf16
+  int rope_half;
+  float eps;
+  int fast;                    // rope_half % 8 == 0 and 16-byte aligned tables
+  void* out;                   // [N / 128, M, 128] bf16, 16-byte aligned
+};
+cudaError_t launch_qk_norm_rope(const QkNormArgs& a, cudaStream_t stream);
 
 // GEMM epilogues.  C[m, n] for the plain epilogues, [N/128, M, 128] for QK.
 enum Epilogue : int {

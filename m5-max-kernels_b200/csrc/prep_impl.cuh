@@ -599,7 +599,24 @@ __global__ void __launch_bounds__(512)
       for (int i = 0; i < kChunk; ++i) v[i] = __fmul_rn(v[i], a.inv_sqrt_block);
     }
 
-    if constexpr (OUT == OUT_F32) {
+    if constexpr (OUT == OUT_ROW && sizeof(T) == 2) {
+      // staged comparator: the modulated row in the input dtype (B == 0)
+      T* yrow = reinterpret_cast<T*>(a.y) + row * K;
+      if (fullchunk && vec) {
+#pragma unroll
+        for (int i = 0; i < kChunk; i += 8) {
+          uint4 raw;
+          T* h = reinterpret_cast<T*>(&raw);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(v[i + e]);
+          *reinterpret_cast<uint4*>(yrow + j0 + i) = raw;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i)
+          if (in(i)) yrow[j0 + i] = from_f32<T>(v[i]);
+      }
+    } else if constexpr (OUT == OUT_F32 || OUT == OUT_ROW) {
       float* yrow = a.y + row * K;
       if (fullchunk && vec) {
 #pragma unroll
@@ -766,6 +783,7 @@ static cudaError_t launch_o(const RowPrepArgs& a, const RowMaps& m, int block, i
     case OUT_INT8: return launch_b<T, OUT_INT8>(a, m, block, stream);
     case OUT_E4M3: return launch_b<T, OUT_E4M3>(a, m, block, stream);
     case OUT_F32: return launch_b<T, OUT_F32>(a, m, block, stream);
+    case OUT_ROW: return block == 0 ? launch_t<T, 0, OUT_ROW>(a, m, stream) : cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }

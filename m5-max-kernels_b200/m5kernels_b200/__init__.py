@@ -4,8 +4,9 @@ The `cuda-b200` backend of the m5kernels operator contracts:
     quantize, gemm                     (twin of m5kernels.metal)
     rotate, hadamard_quantize          (twin of m5kernels.hadamard)
     fused_norm_hadamard_quantize,
-    fused_gated_residual_norm_hadamard_quantize   (twin of m5kernels.norm_hadamard)
-    projection_qk_rope                 (twin of m5kernels.qk_rope)
+    fused_gated_residual_norm_hadamard_quantize,
+    gated_residual_add, unfused_norm   (twin of m5kernels.norm_hadamard)
+    projection_qk_rope, qk_norm_rope   (twin of m5kernels.qk_rope)
     rms_quantize                       (twin of m5kernels.rms_quant)
     linear                             (the online quantize -> gemm stage in one call)
 All of them run hand-written CUDA kernels from libm5b200.so through its C ABI
@@ -15,12 +16,14 @@ All of them run hand-written CUDA kernels from libm5b200.so through its C ABI
 from .cuda import gemm, quantize
 from .hadamard import SUPPORTED_BLOCK_SIZES, hadamard_quantize, rotate
 from .linear import linear
-from .norm_hadamard import fused_gated_residual_norm_hadamard_quantize, fused_norm_hadamard_quantize
-from .qk_rope import projection_qk_rope, rope_tables
+from .norm_hadamard import (fused_gated_residual_norm_hadamard_quantize,
+                            fused_norm_hadamard_quantize, gated_residual_add, unfused_norm)
+from .qk_rope import projection_qk_rope, qk_norm_rope, rope_tables
 from .rms_quant import rms_quantize
 
 __all__ = [
     "gemm", "quantize", "rotate", "hadamard_quantize", "SUPPORTED_BLOCK_SIZES",
     "fused_norm_hadamard_quantize", "fused_gated_residual_norm_hadamard_quantize",
-    "projection_qk_rope", "rope_tables", "linear", "rms_quantize",
+    "projection_qk_rope", "rope_tables", "linear", "rms_quantize", "gated_residual_add",
+    "unfused_norm", "qk_norm_rope",
 ]

@@ -40,6 +40,9 @@ _SIGNATURES = {
         [P, P, I, I64, I64, P, I, P, I64, P, I, P, I, P, I, P, I64, P, I, I, F, I, I, P, P, P,
          P], I),
     "m5b_rms_quantize": ([P, I, I64, I64, P, P, I, I, F, P, P, P], I),
+    "m5b_unfused_norm": ([P, I, I64, I64, P, I, P, I, P, I, P, I64, I, F, I, P, P], I),
+    "m5b_gated_residual_add": ([P, P, I, I64, I64, P, I, P, I64, P, P], I),
+    "m5b_qk_norm_rope": ([P, I64, I64, P, P, P, I, F, P, P], I),
     "m5b_gemm": ([P, P, I64, I64, I64, I, P, P, P, I, P, P, I64, P, P, P, I64, P], I),
     "m5b_projection_qk_rope": ([P, P, I64, I64, I64, I, P, P, P, P, P, I, F, P, P], I),
     "m5b_linear_workspace_bytes": ([I64, I64], I64),

@@ -1,5 +1,12 @@
 """One-kernel normalization, modulation, block rotation and quantization on B200.
 
+Also the staged comparators of the same module (src/m5kernels/norm_hadamard.py:
+280-348): `gated_residual_add` (the R' update alone) and `unfused_norm` (norm +
+modulation alone).  Each runs the fused kernels' FP32 operations in the same
+order, so gated_residual_add -> fused_norm_hadamard_quantize equals the fused
+gated kernel bit for bit, and unfused_norm -> hadamard_quantize equals
+fused_norm_hadamard_quantize.
+
 Twin of m5kernels.norm_hadamard (src/m5kernels/norm_hadamard.py:122-265):
 the modulation contract is norm(X) * gamma * (1 + scale) + shift in FP32,
 optionally rounded to X's dtype after the complete expression; signs are
@@ -160,3 +167,61 @@ def fused_gated_residual_norm_hadamard_quantize(
         _lib.NORM[norm], float(epsilon), 1 if round_output == "input" else 0, _lib.MODE[mode],
         ptr(q), ptr(s), ptr(r_out), _lib.stream_handle(dev)))
     return q, s, r_out
+
+
+def _validate_threads_tag(threads, tag):
+    if isinstance(threads, bool) or not isinstance(threads, Integral):
+        raise ValueError("threads must be an integer")
+    if threads not in (128, 256):
+        raise NotImplementedError("supported threadgroup sizes are 128 and 256")
+    if not isinstance(tag, str) or re.fullmatch(r"[A-Za-z_][A-Za-z_0-9]*", tag) is None:
+        raise ValueError("tag must be a valid nonempty identifier")
+
+
+def gated_residual_add(residual, branch, gate, *, gate_row_map=None, threads=256, tag="default"):
+    """Stage the gated residual update alone: cast_R(R + branch * gate[gate_row_map]).
+
+    One FP32 fused multiply-add per element, then round to the residual dtype
+    -- the R' that fused_gated_residual_norm_hadamard_quantize writes.  Twin of
+    src/m5kernels/norm_hadamard.py:280-300.
+    """
+    _validate_gate(residual, branch, gate, gate_row_map)
+    _validate_threads_tag(threads, tag)
+    if branch.dtype != residual.dtype:
+        raise NotImplementedError("branch and residual must share one dtype on cuda-b200")
+    dev = _lib.require_cuda(residual, branch, gate, gate_row_map)
+    residual, branch, gate = (t.contiguous() for t in (residual, branch, gate))
+    gate_row_map = gate_row_map.contiguous() if gate_row_map is not None else None
+    rows, k = residual.shape
+    out = torch.empty_like(residual)
+    code = _lib.DTYPE_CODE
+    check(_lib.lib().m5b_gated_residual_add(
+        ptr(residual), ptr(branch), code[residual.dtype], rows, k, ptr(gate), code[gate.dtype],
+        ptr(gate_row_map), gate.shape[0] if gate_row_map is not None else 0, ptr(out),
+        _lib.stream_handle(dev)))
+    return out
+
+
+def unfused_norm(x, gamma, scale, shift, *, norm="rms", epsilon=1e-5, round_output="input",
+                 threads=256, row_map=None):
+    """Return norm + modulation only, with the fused path's rounding contract.
+
+    y = norm(x) * gamma * (1 + scale[row_map]) + shift[row_map] in FP32 with the
+    statistics of fused_norm_hadamard_quantize; x's dtype when round_output is
+    "input", else float32.  No rotation, no packing.  Twin of
+    src/m5kernels/norm_hadamard.py:321-348.
+    """
+    norm = _validate_common(x, gamma, scale, shift, norm, epsilon, round_output, threads, row_map)
+    dev = _lib.require_cuda(x, gamma, scale, shift, row_map)
+    x, gamma, scale, shift = (t.contiguous() for t in (x, gamma, scale, shift))
+    row_map = row_map.contiguous() if row_map is not None else None
+    rows, k = x.shape
+    dtype = x.dtype if round_output == "input" else torch.float32
+    y = torch.empty((rows, k), dtype=dtype, device=dev)
+    code = _lib.DTYPE_CODE
+    check(_lib.lib().m5b_unfused_norm(
+        ptr(x), code[x.dtype], rows, k, ptr(gamma), code[gamma.dtype], ptr(scale),
+        code[scale.dtype], ptr(shift), code[shift.dtype], ptr(row_map),
+        scale.shape[0] if row_map is not None else 0, _lib.NORM[norm], float(epsilon),
+        1 if round_output == "input" else 0, ptr(y), _lib.stream_handle(dev)))
+    return y

@@ -6,13 +6,17 @@ epilogue rounds the projection to BF16, computes the row's RMS over the
 head's 128 channels, applies gamma and rotates the pairs (j, j + R) for j < R,
 and writes the head-major [H, M, 128] BF16 output.  Boundaries: BF16
 projection, FP32 RMS/gamma/RoPE, BF16 output (no BF16 norm intermediate).
+
+`qk_norm_rope` is the staged comparator (src/m5kernels/qk_rope.py:185-203):
+the same post-processing applied to a stored BF16 projection, bit-identical to
+the fused epilogue, so gemm(..., bf16) -> qk_norm_rope == projection_qk_rope.
 """
 
 from __future__ import annotations
 
 import math
 import struct
-from numbers import Real
+from numbers import Integral, Real
 
 import torch
 
@@ -87,6 +91,28 @@ def projection_qk_rope(a, b, gamma, cos, sin, mode="int8", tile=(32, 128, 4, 1),
     check(_lib.lib().m5b_projection_qk_rope(
         ptr(a), ptr(b), m, n, a.shape[1], _lib.MODE[mode], ptr(a_scales), ptr(b_scales),
         ptr(gamma), ptr(cos), ptr(sin), rope_half, eps, ptr(out), _lib.stream_handle(dev)))
+    return out
+
+
+def qk_norm_rope(projected, gamma, cos, sin, *, epsilon=1e-5, threads=128):
+    """Standalone post-process from BF16 [M, N] to BF16 [heads, M, 128]."""
+    if not isinstance(projected, torch.Tensor) or projected.dim() != 2 or projected.dtype != torch.bfloat16:
+        raise ValueError("projected must be a bfloat16 [M,N] matrix")
+    m, n = projected.shape
+    rope_half, eps = _validate_norm(m, n, gamma, cos, sin, epsilon)
+    if isinstance(threads, bool) or not isinstance(threads, Integral):
+        raise ValueError("threads must be an integer")
+    if threads not in (128, 256):
+        raise NotImplementedError("standalone Q/K normalization supports 128 or 256 threads")
+    dev = _lib.require_cuda(projected, gamma, cos, sin)
+    projected = projected.contiguous()
+    if projected.data_ptr() % 16:
+        projected = projected.clone()
+    gamma, cos, sin = gamma.contiguous(), cos.contiguous(), sin.contiguous()
+    out = torch.empty((n // HEAD_DIM, m, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    check(_lib.lib().m5b_qk_norm_rope(
+        ptr(projected), m, n, ptr(gamma), ptr(cos), ptr(sin), rope_half, eps, ptr(out),
+        _lib.stream_handle(dev)))
     return out
 
 

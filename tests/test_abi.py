@@ -25,7 +25,8 @@ def test_header_declares_the_operator_contracts():
     for required in ("m5b_quantize", "m5b_rotate", "m5b_hadamard_quantize",
                      "m5b_fused_norm_hadamard_quantize",
                      "m5b_fused_gated_residual_norm_hadamard_quantize", "m5b_gemm",
-                     "m5b_projection_qk_rope", "m5b_last_error", "m5b_device_status"):
+                     "m5b_projection_qk_rope", "m5b_last_error", "m5b_device_status",
+                     "m5b_unfused_norm", "m5b_gated_residual_add", "m5b_qk_norm_rope"):
         assert required in names
 
 
@@ -64,6 +65,18 @@ def test_contract_errors_come_back_through_the_abi_without_a_gpu():
     assert rc == _lib.EUNSUPPORTED and b"FP8" in lib.m5b_last_error()
     with pytest.raises(NotImplementedError, match="FP8"):
         _lib.check(rc)
+    # staged comparators
+    rc = lib.m5b_qk_norm_rope(ctypes.c_void_p(16), 4, 200, ctypes.c_void_p(16), ctypes.c_void_p(16),
+                              ctypes.c_void_p(16), 64, 1e-5, ctypes.c_void_p(16), None)
+    assert rc == _lib.EINVAL and b"128-wide heads" in lib.m5b_last_error()
+    rc = lib.m5b_gated_residual_add(ctypes.c_void_p(16), ctypes.c_void_p(16), _lib.BF16, 0, 64,
+                                    ctypes.c_void_p(16), _lib.BF16, None, 0, ctypes.c_void_p(16),
+                                    None)
+    assert rc == _lib.EINVAL and b"nonempty" in lib.m5b_last_error()
+    rc = lib.m5b_unfused_norm(ctypes.c_void_p(16), _lib.BF16, 4, 64, ctypes.c_void_p(16), _lib.F32,
+                              ctypes.c_void_p(16), _lib.F32, ctypes.c_void_p(16), _lib.F32, None, 0,
+                              3, 1e-5, 1, ctypes.c_void_p(16), None)
+    assert rc == _lib.EINVAL and b"norm must be" in lib.m5b_last_error()
 
 
 def test_operators_refuse_cpu_tensors():
@@ -74,6 +87,14 @@ def test_operators_refuse_cpu_tensors():
         m.quantize(torch.ones(4, 64), "int8")
     with pytest.raises(ExtensionMissing):
         m.rotate(torch.ones(4, 64), 32, torch.ones(64, dtype=torch.int8))
+    with pytest.raises(ExtensionMissing):
+        m.gated_residual_add(torch.ones(4, 64), torch.ones(4, 64), torch.ones(64))
+    with pytest.raises(ExtensionMissing):
+        m.unfused_norm(torch.ones(4, 64), torch.ones(64), torch.ones(64), torch.ones(64))
+    with pytest.raises(ExtensionMissing):
+        m.qk_norm_rope(torch.ones(4, 128, dtype=torch.bfloat16),
+                       torch.ones(128, dtype=torch.bfloat16),
+                       torch.ones(4, 64, dtype=torch.bfloat16), torch.ones(4, 64, dtype=torch.bfloat16))
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
