@@ -194,7 +194,9 @@ def run_secondary(args, world, rank, local):
     above L2), and the SETS steps are captured once as a CUDA graph that is
     replayed: the times are device times of the kernels, without the Python
     launch path between them.  For qk_c5 the prep and the Q/K projection are
-    also timed on their own.
+    also timed on their own, and the staged comparators (prep_c4:
+    gated_residual_add then the fused prep; qk_c5: bf16 projection then
+    qk_norm_rope) give the fusion gain = staged time / fused time.
     """
     import torch
 
@@ -225,9 +227,15 @@ def run_secondary(args, world, rank, local):
             gamma = torch.ones(k, dtype=torch.bfloat16, device=dev)
             rmap = (torch.arange(m, device=dev, dtype=torch.int32) // (m // p)).to(torch.int32)
             signs = torch.ones(k, dtype=torch.int8, device=dev)
+
+            def staged():  # the two-launch comparator: R' update, then the fused prep
+                upd = m5.gated_residual_add(res, br, gate, gate_row_map=rmap)
+                return m5.fused_norm_hadamard_quantize(upd, gamma, scale, shift, signs, 128,
+                                                       norm="layer", epsilon=1e-6, row_map=rmap)
+
             return (lambda: m5.fused_gated_residual_norm_hadamard_quantize(  # noqa: E731
                 res, br, gate, gamma, scale, shift, signs, 128, norm="layer", epsilon=1e-6,
-                gate_row_map=rmap, row_map=rmap)), {}
+                gate_row_map=rmap, row_map=rmap)), {"staged": staged}
         if args.workload == "rms_q":
             m, k, n = 4096, 5376, 7168
             x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
@@ -264,6 +272,10 @@ def run_secondary(args, world, rank, local):
             "prep": lambda: m5.hadamard_quantize(x, 256, signs, "int8"),  # noqa: E731
             "qk_gemm": lambda: m5.projection_qk_rope(  # noqa: E731
                 q0, wq, gamma, cos, sin, "int8", a_scales=s0, b_scales=ws),
+            # staged comparator: bf16 projection stored, then the standalone post-process
+            "qk_staged": lambda: m5.qk_norm_rope(  # noqa: E731
+                m5.gemm(q0, wq, "int8", a_scales=s0, b_scales=ws, output_dtype=torch.bfloat16),
+                gamma, cos, sin),
         }
 
     SETS = 2
@@ -315,6 +327,9 @@ def run_secondary(args, world, rank, local):
         line["parts_ms"] = part_ms
         if "qk_gemm" in part_ms:
             line["qk_gemm_tops"] = nbytes / (part_ms["qk_gemm"] * 1e-3) / 1e12
+            line["qk_fusion_gain"] = part_ms["qk_staged"] / part_ms["qk_gemm"]
+        if "staged" in part_ms:
+            line["fusion_gain"] = part_ms["staged"] / ms
         if args.workload == "rms_q":
             prep_bytes = 4096 * (3 * 5376 + 4)
             line["prep_gbs"] = prep_bytes / (part_ms["prep"] * 1e-3) / 1e9

@@ -603,6 +603,23 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
     g.bias = bias;
     g.bias_row_map = bias_row_map;
   }
+  // 16-bit outputs leave through a tensor map: 32 x 32 boxes staged per
+  // epilogue warp with the 64-byte swizzle; the map clips the M and N tails.
+  CUtensorMap to{};
+  if ((out_dtype == M5B_BF16 || out_dtype == M5B_F16) && n % 8 == 0 && aligned(out, 16)) {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(n) * 2};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt =
+        out_dtype == M5B_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = g_encode(&to, dt, 2, out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(M5B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    g.tma_store = 1;
+    return gemm_launch(ta, tb, tbh, g, bn, pair, stream, &to);
+  }
   return gemm_launch(ta, tb, tbh, g, bn, pair, stream);
 }
 

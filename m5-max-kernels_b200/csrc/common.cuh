@@ -247,12 +247,27 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
       "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// Tiled TMA store of a 2D box from shared memory (bulk-group completion).
+// Out-of-range parts of the box are clipped by the tensor map.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src,
+                                             int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 // The shared memory read by this thread's committed bulk stores may be reused.
 __device__ __forceinline__ void bulk_wait_group_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// All but the most recent of this thread's committed bulk store groups have
+// read their shared memory.
+__device__ __forceinline__ void bulk_wait_group_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 // This thread's committed bulk stores are complete.
 __device__ __forceinline__ void bulk_wait_group0() {

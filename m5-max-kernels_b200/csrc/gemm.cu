@@ -14,9 +14,12 @@
 //              (kind::i8 -> s32, kind::f8f6f4 E4M3 -> f32, kind::f16 -> f32),
 //              M=128, N=BN, K=32 bytes per instruction; tcgen05.commit frees a
 //              ring slot when its MMAs retire.
-//   warps 2-5  epilogue: tcgen05.ld of the accumulator (thread = one output
-//              row), scale / bias / gate / RMS+RoPE in registers, direct
-//              vectorised global stores.
+//   warps 2-5  epilogue (2-9 on CTA-pair tiles, each warp then draining half
+//              of the tile's columns): tcgen05.ld of the accumulator (thread =
+//              one output row), scale / bias / gate / RMS+RoPE in registers;
+//              16-bit outputs are staged per warp in shared memory (32 rows x
+//              32 columns, 64-byte swizzle, double-buffered) and leave with
+//              tiled TMA stores, other outputs with direct vector stores.
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
 // the MMAs of tile i+1.  Tiles are walked in grouped-M order, CTA b taking
 // tiles b, b + grid, ...  No TMA multicast is used anywhere.
@@ -56,13 +59,16 @@ struct GemmCfg {
   static constexpr int STAGES = QK ? (PAIR ? 4 : 5) : (STAGE_BYTES <= 32 * 1024 ? 6 : 4);
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
-  // Epilogue warps: 4, or 8 for Q/K pair tiles (each warp drains one of the
-  // tile's two heads for its 32 rows).
-  static constexpr int EPI_WARPS = (QK && PAIR) ? 8 : 4;
+  // Epilogue warps: 4, or 8 for pair tiles (each warp drains one of the tile's
+  // two heads (Q/K), or half of its columns, for its 32 rows).
+  static constexpr int EPI_WARPS = PAIR ? 8 : 4;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  // 128 rows x 128 bf16 channels per head staged at once
-  static constexpr int QK_BYTES = QK ? (EPI_WARPS / 4) * kBM * 256 : 0;
+  // Q/K: 128 rows x 128 bf16 channels per head staged at once; otherwise two
+  // 2 KB buffers (32 rows x 32 16-bit columns) per epilogue warp.
+  static constexpr int QK_BYTES =
+      QK ? (EPI_WARPS / 4) * kBM * 256 : EPI_WARPS * 2 * 2048;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + QK_BYTES + BAR_BYTES + 16;
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA exceeds 227 KB");
 };
 
 __device__ __forceinline__ void tile_coords(int t, const GemmArgs& g, int& m_blk, int& n_blk) {
@@ -189,6 +195,62 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
   }
 }
 
+// The same epilogue for one thread's 32 consecutive columns, rounded to the
+// 16-bit output dtype and packed two per word (staged, then a TMA store).
+// Columns past N are computed from zero scale / bias / gate and clipped by
+// the store.
+template <int KIND>
+__device__ __forceinline__ void epilogue_pack16(const GemmArgs& g, const uint32_t (&r)[32],
+                                                int64_t row, int col0, float sa, uint32_t* pk) {
+  const int N = g.N;
+  const bool full = (col0 + 32 <= N);
+  const bool in_row = row < g.M;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float x = acc_value<KIND>(r[i]);
+    if (g.quantized) {
+      const int col = col0 + i;
+      const float sb = (full || col < N) ? __ldg(g.b_scales + (col < N ? col : 0)) : 0.0f;
+      x = __fmul_rn(__fmul_rn(x, sa), sb);
+    }
+    v[i] = x;
+  }
+  if (in_row) {
+    const int64_t base = row * int64_t(N) + col0;
+    if (g.epi == EPI_BIAS_VEC || g.epi == EPI_BIAS_TABLE) {
+      const int64_t boff = (g.epi == EPI_BIAS_TABLE) ? int64_t(g.bias_row_map[row]) * N : 0;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (full || col0 + i < N) v[i] = __fadd_rn(v[i], __ldg(g.bias + boff + col0 + i));
+    } else if (g.epi == EPI_GATE_VEC || g.epi == EPI_GATE_TABLE) {
+      const int64_t goff = (g.epi == EPI_GATE_TABLE) ? int64_t(g.gate_row_map[row]) * N : 0;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (full || col0 + i < N) {
+          const float branch = bf16_round(v[i]);
+          const float gate = bf16_load(g.gate, goff + col0 + i);
+          const float res = bf16_load(g.residual, base + i);
+          v[i] = __fmaf_rn(branch, gate, res);
+        }
+      }
+    }
+  }
+  if (g.out_dtype == DT_F16) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+  }
+}
+
 template <int KIND, int BN, bool QK, bool PAIR>
 __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -206,7 +268,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint8_t* qk_stage = sB + STAGES * Cfg::B_BYTES;  // 1024-aligned (QK only)
+  uint8_t* qk_stage = sB + STAGES * Cfg::B_BYTES;  // 1024-aligned epilogue staging
   uint64_t* full = reinterpret_cast<uint64_t*>(qk_stage + Cfg::QK_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
@@ -239,7 +301,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
     if (g.num_units > g.num_full) tma_prefetch_desc(&tmap_b_half);
-    if (QK && g.qk_fast) tma_prefetch_desc(&tmap_out);
+    if ((QK && g.qk_fast) || (!QK && g.tma_store)) tma_prefetch_desc(&tmap_out);
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -409,6 +471,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
       else
         mbar_arrive(&acc_empty[acc]);
     };
+    // plain epilogues: this warp's two staging buffers and their use count
+    uint8_t* out_stage = qk_stage + (warp - 2) * 4096;
+    uint32_t ostage = 0;
     int local = 0;
     for (int t = unit; t < num_units_total; t += units, ++local) {
       int m_blk, n_col;
@@ -426,17 +491,60 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const float sa = (g.quantized && row < g.M) ? __ldg(g.a_scales + row) : 1.0f;
       if constexpr (!QK) {
+        // This warp's 32-column chunks: all of the tile's, or with 8 warps
+        // the half matching ehalf.
         const int chunks = whole ? BN / 32 : BN / 64;
+        const int c_first = Cfg::EPI_WARPS == 8 ? ehalf * (chunks / 2) : 0;
+        const int c_end = Cfg::EPI_WARPS == 8 ? c_first + chunks / 2 : chunks;
+        if (g.tma_store) {
+          const int64_t row0 = row - lane;  // this warp's first row
 #pragma unroll 1
-        for (int c = 0; c < chunks; ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-          epilogue_chunk<KIND>(g, r, row, n_col + c * 32, sa);
+          for (int c = c_first; c < c_end; ++c) {
+            uint32_t r[32];
+            tmem_ld32(taddr + c * 32, r);
+            tmem_wait_ld();
+            if (c == c_end - 1) {  // the accumulator is drained: hand it back
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) release_acc(acc);
+            }
+            uint32_t pk[16];
+            epilogue_pack16<KIND>(g, r, row, n_col + c * 32, sa, pk);
+            uint8_t* buf = out_stage + (ostage & 1) * 2048;
+            if (lane == 0) bulk_wait_group_read1();  // the store two chunks back has read buf
+            __syncwarp();
+            // row `lane` of a 32 x 64-byte box; 64-byte swizzle: 16-byte
+            // chunk j sits at j ^ ((row >> 1) & 3)
+            const int sw = (lane >> 1) & 3;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ sw) << 4)) =
+                  make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0 && row0 < g.M && n_col + c * 32 < g.N) {
+              tma_store_2d(&tmap_out, buf, n_col + c * 32, static_cast<int32_t>(row0));
+              bulk_commit_group();
+            }
+            ++ostage;
+          }
+          if (c_first >= c_end) {  // no columns for this warp (cannot happen: chunks >= 2)
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) release_acc(acc);
+          }
+        } else {
+#pragma unroll 1
+          for (int c = c_first; c < c_end; ++c) {
+            uint32_t r[32];
+            tmem_ld32(taddr + c * 32, r);
+            tmem_wait_ld();
+            epilogue_chunk<KIND>(g, r, row, n_col + c * 32, sa);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) release_acc(acc);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) release_acc(acc);
       } else {
         // One or two 128-wide heads per unit.  Per head, pass 1: BF16
         // projection z, its square sum (sequential over the head's 128
@@ -601,10 +709,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
         }
       }
     }
-    if constexpr (QK) {
-      if (lane == 0) bulk_wait_group0();  // this warp's head stores are complete
-      __syncwarp();
-    }
+    if (lane == 0) bulk_wait_group0();  // this warp's TMA stores are complete
+    __syncwarp();
   }
 
   // ------------------------------------------------------------ teardown

@@ -159,6 +159,8 @@ struct GemmArgs {
   const void* sin;            // [M, R] bf16 (QK)
   int rope_half;
   int qk_fast;                // QK: rope_half % 8 == 0 and 16-byte aligned tables (vector path)
+  int tma_store;              // plain / bias / gate epilogues: 16-bit output leaves through
+                              // the output tensor map (32 x 32 boxes, 64-byte swizzle)
   float eps;
   int num_m_blocks, num_n_blocks, num_k_blocks;
   int group_m;
@@ -171,7 +173,8 @@ struct GemmArgs {
 };
 
 // `to`: the Q/K output map (3D {128, M, N/128} bf16, boxes {64, 32, 1}, 128-byte
-// swizzle); ignored by the other epilogues.
+// swizzle), or with g.tma_store the [M, N] output map of the other epilogues
+// (2D {N, M} bf16 / fp16, boxes {32, 32}, 64-byte swizzle).
 cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb_half,
                         const CUtensorMap& to, const GemmArgs& g, int bn, int grid, bool pair,
                         cudaStream_t stream);

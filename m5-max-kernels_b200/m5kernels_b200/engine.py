@@ -11,8 +11,11 @@ Backends (the `backend` string of run_case):
     gemm                      cuda-b200            online per-token quant + W8A8 / FP8 GEMM
                               cuda-b200-hadamard   online rotation + quant + GEMM (weights rotated offline)
     norm_hadamard_gemm        cuda-b200-norm-fused fused norm/modulation/rotation/INT8 prep + GEMM
+                              cuda-b200-norm-staged      unfused_norm -> rotate -> quantize + GEMM
     gated_norm_hadamard_gemm  cuda-b200-residual-fused   gated residual + the above, R' written once
+                              cuda-b200-residual-separate  gated_residual_add -> fused prep + GEMM
     qk_rope                   cuda-b200-qk-fused   H + INT8 prep + projection with RMSNorm + RoPE epilogue
+                              cuda-b200-qk-staged  H + INT8 prep + bf16 projection -> qk_norm_rope
     rms_quant_gemm            cuda-b200-rms-folded RMS prep with the inverse RMS folded into the scale + GEMM
                               cuda-b200-rms-direct RMS prep normalizing first + GEMM
 """
@@ -33,15 +36,16 @@ import torch
 from . import _lib
 from .cuda import gemm, quantize
 from .hadamard import hadamard_quantize, rotate
-from .norm_hadamard import fused_gated_residual_norm_hadamard_quantize, fused_norm_hadamard_quantize
-from .qk_rope import projection_qk_rope, rope_tables
+from .norm_hadamard import (fused_gated_residual_norm_hadamard_quantize,
+                            fused_norm_hadamard_quantize, gated_residual_add, unfused_norm)
+from .qk_rope import projection_qk_rope, qk_norm_rope, rope_tables
 from .rms_quant import rms_quantize
 
 BACKENDS = {
     "gemm": ("cuda-b200", "cuda-b200-hadamard"),
-    "norm_hadamard_gemm": ("cuda-b200-norm-fused",),
-    "gated_norm_hadamard_gemm": ("cuda-b200-residual-fused",),
-    "qk_rope": ("cuda-b200-qk-fused",),
+    "norm_hadamard_gemm": ("cuda-b200-norm-fused", "cuda-b200-norm-staged"),
+    "gated_norm_hadamard_gemm": ("cuda-b200-residual-fused", "cuda-b200-residual-separate"),
+    "qk_rope": ("cuda-b200-qk-fused", "cuda-b200-qk-staged"),
     "rms_quant_gemm": ("cuda-b200-rms-folded", "cuda-b200-rms-direct"),
 }
 
@@ -236,9 +240,11 @@ def prepare_gemm(c, backend, precision, seed, distribution, tile):
 
 def prepare_norm_hadamard_gemm(c, backend, precision, seed, distribution, tile):
     gated = c["op"] == "gated_norm_hadamard_gemm"
-    want = "cuda-b200-residual-fused" if gated else "cuda-b200-norm-fused"
-    if backend != want or precision != "int8":
-        raise NotImplementedError(f"supported backend/precision pairs: [('{want}', 'int8')]")
+    allowed = BACKENDS[c["op"]]
+    if backend not in allowed or precision != "int8":
+        raise NotImplementedError(
+            f"supported backend/precision pairs: {sorted((b, 'int8') for b in allowed)}")
+    fused_path = backend in ("cuda-b200-norm-fused", "cuda-b200-residual-fused")
     from .reference_checks import norm_reference_rows
 
     dev = torch.device("cuda")
@@ -282,30 +288,48 @@ def prepare_norm_hadamard_gemm(c, backend, precision, seed, distribution, tile):
     if gated:
         bd, gtd, grmd = T(branch), T(gate), T(gate_row_map)
 
-        def prep():
+        def prep_fused():
             return fused_gated_residual_norm_hadamard_quantize(
                 xd, bd, gtd, gd, scd, shd, sgd, block, norm=norm, epsilon=eps,
                 gate_row_map=grmd, row_map=rmd)
+
+        def prep_staged():  # the fair two-launch baseline (norm_hadamard_gemm.py:261-276)
+            updated = gated_residual_add(xd, bd, gtd, gate_row_map=grmd)
+            q, s = fused_norm_hadamard_quantize(updated, gd, scd, shd, sgd, block, norm=norm,
+                                                epsilon=eps, row_map=rmd)
+            return q, s, updated
     else:
 
-        def prep():
+        def prep_fused():
             return fused_norm_hadamard_quantize(xd, gd, scd, shd, sgd, block, norm=norm,
                                                 epsilon=eps, row_map=rmd)
+
+        def prep_staged():  # norm -> rotate -> quantize as three launches (:225-226)
+            y = unfused_norm(xd, gd, scd, shd, norm=norm, epsilon=eps, row_map=rmd)
+            return quantize(rotate(y, block, sgd), "int8")
+
+    prep = prep_fused if fused_path else prep_staged
 
     prepared = prep()
     aq, sa = prepared[:2]
     refs = norm_reference_rows(x, gamma, scale, shift, row_map, ri, norm, eps, block, signs,
                                branch=branch if gated else None, gate=gate if gated else None,
                                gate_row_map=gate_row_map if gated else None)
+    # The other path of the pair must give the same codes, scales (and R') bit for bit.
+    other = (prep_staged if fused_path else prep_fused)()
+    paired_exact = all(bool(torch.equal(u, v)) for u, v in zip(prepared, other))
     meta = dict(mac_operations=2 * m * n * k, sample_rows=ri.tolist(), sample_cols=ci.tolist(),
                 norm=norm, epsilon=eps, block_size=block, samples=samples, gated=gated,
-                compute_path="fused_row_prep + tcgen05_int8_gemm")
+                compute_path=("fused_row_prep" if fused_path else
+                              ("gated_residual_add + fused_row_prep" if gated else
+                               "unfused_norm + rotate + quantize")) + " + tcgen05_int8_gemm",
+                paired_path_exact=paired_exact)
     # activation checks against the float64 reference on sampled rows (reference gates)
     codes = aq[torch.as_tensor(ri, device=dev)].cpu().numpy().astype(np.int16)
     scales = sa[torch.as_tensor(ri, device=dev)].cpu().numpy()
     code_diff = float(np.abs(codes - refs["codes"].astype(np.int16)).max())
     scale_err = metrics(scales, refs["scales"])
-    transform_pass = code_diff <= 1 and scale_err["relative_l2"] <= 0.008
+    transform_pass = code_diff <= 1 and scale_err["relative_l2"] <= 0.008 and paired_exact
     if gated:
         r_rows = prepared[2][torch.as_tensor(ri, device=dev)].cpu()
         residual_exact = bool(torch.equal(r_rows, refs["residual_bf16"]))
@@ -340,8 +364,8 @@ def prepare_norm_hadamard_gemm(c, backend, precision, seed, distribution, tile):
 
 
 def prepare_qk_rope(c, backend, precision, seed, distribution, tile):
-    if backend != "cuda-b200-qk-fused" or precision != "int8":
-        raise NotImplementedError("qk_rope supports cuda-b200-qk-fused with INT8 only")
+    if backend not in BACKENDS["qk_rope"] or precision != "int8":
+        raise NotImplementedError("qk_rope supports cuda-b200-qk-fused/cuda-b200-qk-staged with INT8 only")
     from .reference_checks import qk_reference_rows
 
     dev = torch.device("cuda")
@@ -370,14 +394,25 @@ def prepare_qk_rope(c, backend, precision, seed, distribution, tile):
     original = qk_reference_rows(_f64(x[ridx]) @ _f64(w[torch.as_tensor(cols, device=dev)]).T,
                                  gamma, cos[ridx], sin[ridx], eps, len(heads))
 
-    def fn():
-        return projection_qk_rope(aq, bq, gamma, cos, sin, "int8", tile, a_scales=sa,
-                                  b_scales=sb, epsilon=eps)
-
-    def online():
-        q, s = prep()
+    def fused(q, s):
         return projection_qk_rope(q, bq, gamma, cos, sin, "int8", tile, a_scales=s, b_scales=sb,
                                   epsilon=eps)
+
+    def staged(q, s):  # bf16 projection stored, then the standalone post-process
+        projected = gemm(q, bq, "int8", tile, a_scales=s, b_scales=sb,
+                         output_dtype=torch.bfloat16)
+        return qk_norm_rope(projected, gamma, cos, sin, epsilon=eps)
+
+    selected = fused if backend == "cuda-b200-qk-fused" else staged
+    # Same exact integer dot, FP32 dequantization order and post-processing:
+    # the paired paths must agree on every output, not only the sampled rows.
+    paired_exact = bool(torch.equal(fused(aq, sa), staged(aq, sa)))
+
+    def fn():
+        return selected(aq, sa)
+
+    def online():
+        return selected(*prep())
 
     def check(y):
         return _f64(y[hidx][:, ridx, :]).reshape(-1)
@@ -385,7 +420,10 @@ def prepare_qk_rope(c, backend, precision, seed, distribution, tile):
     meta = dict(mac_operations=2 * m * n * k, sample_rows=rows.tolist(),
                 sample_heads=heads.tolist(), rope_half=half, theta=theta, epsilon=eps,
                 block_size=block, output_layout="head-major [H,M,128]",
-                compute_path="fused_hadamard_quant + tcgen05_int8_qk_rope")
+                compute_path=("fused_hadamard_quant + tcgen05_int8_qk_rope"
+                              if backend == "cuda-b200-qk-fused" else
+                              "fused_hadamard_quant + tcgen05_int8_gemm(bf16) + qk_norm_rope"),
+                paired_path_exact=paired_exact, transform_pass=paired_exact)
     return fn, check, expected.reshape(-1), original.reshape(-1), {
         "activation_prepare": prep, "online_activation_plus_gemm": online}, meta
 

@@ -53,3 +53,19 @@ def test_rms_folded_and_direct_share_inputs(engine):
     b = engine.run_case(c, "cuda-b200-rms-direct", "int8", warmup=1, repeat=2)
     assert a["status"] == b["status"] == "ok"
     assert a["gamma_sha256"] == b["gamma_sha256"]
+
+
+@pytest.mark.parametrize("op,backends", [
+    ("norm_hadamard_gemm", ("cuda-b200-norm-fused", "cuda-b200-norm-staged")),
+    ("gated_norm_hadamard_gemm", ("cuda-b200-residual-fused", "cuda-b200-residual-separate")),
+    ("qk_rope", ("cuda-b200-qk-fused", "cuda-b200-qk-staged")),
+])
+def test_staged_and_fused_backends_agree_exactly(engine, op, backends):
+    """Each fused backend has a staged comparator with bit-identical results."""
+    c = dict(id="t.pair", op=op, m=520, n=384, k=2048,
+             fusion=dict(norm="layer", epsilon=1e-6, block_size=128, samples=2))
+    results = [engine.run_case(c, b, "int8", warmup=1, repeat=2) for b in backends]
+    for r in results:
+        assert r["status"] == "ok", (r["backend"], r.get("reason"))
+        assert r["paired_path_exact"] is True
+    assert results[0]["compute_path"] != results[1]["compute_path"]
