@@ -234,6 +234,23 @@ M5B_API int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int6
                            const void* gamma, const void* cos, const void* sin, int rope_half,
                            float epsilon, void* out, void* stream);
 
+/* Grouped Q/K/V projection: b is [heads, 3, 128, k] (rows in [head, stream,
+ * channel] order, streams Q, K, V), b_scales [heads * 384].  One GEMM; per
+ * 128-column block, z = bf16(v) as in m5b_projection_qk_rope, then
+ *   Q: RMSNorm with gamma_q + split-half RoPE -> q_out [heads, m, 128]
+ *   K: RMSNorm with gamma_k + split-half RoPE -> k_out [heads, m, 128]
+ *   V: z unchanged (no RMS, no RoPE)          -> v_out [heads, m, 128]
+ * all bf16 head-major.  Replaces the native grouped QKV projection of the
+ * reference's H3 integration (integrations/h3/qkv-candidate.md:30-43, the
+ * h3_gpu_m5_grouped_qkv_linear_rope_int8 API; per-stream contract of
+ * integrations/h3/qkv_reference.h:15-36, layout docs/qk-rope-fusion.md:12). */
+M5B_API int m5b_projection_qkv_rope(const void* a, const void* b, int64_t m, int64_t heads,
+                                    int64_t k, int mode, const float* a_scales,
+                                    const float* b_scales, const void* gamma_q,
+                                    const void* gamma_k, const void* cos, const void* sin,
+                                    int rope_half, float epsilon, void* q_out, void* k_out,
+                                    void* v_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

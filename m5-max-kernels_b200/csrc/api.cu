@@ -520,7 +520,8 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMa
 
 static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
                        GemmArgs& g, int bn, bool pair, void* stream,
-                       const CUtensorMap* to = nullptr) {
+                       const CUtensorMap* to = nullptr, const CUtensorMap* to_k = nullptr,
+                       const CUtensorMap* to_v = nullptr) {
   unsigned int* status = nullptr;
   int sms = 0;
   int rc = device_state(&status, &sms);
@@ -536,8 +537,9 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     g.num_units = g.num_full + 2 * rem;
   }
   const int grid = (g.num_units < slots ? g.num_units : slots) * (pair ? 2 : 1);
-  cudaError_t e = launch_gemm(ta, tb, tbh, to ? *to : tbh, g, bn, grid, pair,
-                              static_cast<cudaStream_t>(stream));
+  const CUtensorMap& o = to ? *to : tbh;
+  cudaError_t e = launch_gemm(ta, tb, tbh, o, to_k ? *to_k : o, to_v ? *to_v : o, g, bn, grid,
+                              pair, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
   return ok();
 }
@@ -623,10 +625,28 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
   return gemm_launch(ta, tb, tbh, g, bn, pair, stream);
 }
 
-int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
-                           int mode, const float* a_scales, const float* b_scales,
-                           const void* gamma, const void* cos, const void* sin, int rope_half,
-                           float epsilon, void* out, void* stream) {
+// Head-major output map [heads, M, 128] bf16 as a 3D {128, M, heads} map; boxes
+// of 64 channels x 32 rows (one epilogue warp's rows), 128-byte swizzle; rows
+// past M clipped.
+static int head_major_map(CUtensorMap* map, void* out, int64_t m, int64_t heads) {
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(m), static_cast<cuuint64_t>(heads)};
+  cuuint64_t strides[2] = {256, static_cast<cuuint64_t>(m) * 256};
+  cuuint32_t box[3] = {64, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(M5B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return M5B_OK;
+}
+
+// Shared body of the Q/K and grouped Q/K/V projections.  n = projection
+// columns (heads * 128, or heads * 3 * 128 grouped).
+static int qk_projection(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
+                         const float* a_scales, const float* b_scales, const void* gamma,
+                         const void* gamma_k, const void* cos, const void* sin, int rope_half,
+                         float epsilon, void* out, void* out_k, void* out_v, bool grouped,
+                         void* stream) {
   if (mode != M5B_MODE_INT8 && mode != M5B_MODE_BF16)
     return fail(M5B_EUNSUPPORTED, "Q/K projection fusion supports INT8 or BF16 only");
   if (m <= 0 || n <= 0 || n % 128)
@@ -638,16 +658,19 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
   if (!(epsilon > 0.0f) || !std::isfinite(epsilon))
     return fail(M5B_EINVAL, "epsilon must be a positive finite real scalar");
   if (!gamma || !cos || !sin || !out) return fail(M5B_EINVAL, "gamma, cos, sin and out are required");
+  if (grouped && (!gamma_k || !out_k || !out_v))
+    return fail(M5B_EINVAL, "grouped Q/K/V requires gamma_k and the K and V outputs");
   const bool quant = mode == M5B_MODE_INT8;
   if (quant && (!a_scales || !b_scales))
     return fail(M5B_EINVAL, "INT8 requires float32 a_scales[M] and b_scales[N]");
   if (!quant && (a_scales || b_scales))
     return fail(M5B_EINVAL, "BF16 projection does not accept quantization scales");
-  if (!aligned(out, 16)) return fail(M5B_EINVAL, "output base address must be 16-byte aligned");
+  if (!aligned(out, 16) || (grouped && (!aligned(out_k, 16) || !aligned(out_v, 16))))
+    return fail(M5B_EINVAL, "output base address must be 16-byte aligned");
   GemmArgs g{};
   g.epi = EPI_QK;
   const bool pair = use_pair(EPI_QK, m, n);
-  const int bn = pair ? 256 : 128;  // one or two 128-wide heads per tile
+  const int bn = pair ? 256 : 128;  // one or two 128-wide column blocks per tile
   CUtensorMap ta, tb, tbh;
   int rc = gemm_common(g, ta, tb, tbh, a, b, m, n, k, mode, bn, pair);
   if (rc) return rc;
@@ -661,23 +684,43 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
   g.sin = sin;
   g.rope_half = rope_half;
   g.eps = epsilon;
+  g.grouped = grouped ? 1 : 0;
+  g.gamma_k = gamma_k;
+  g.out_k = out_k;
+  g.out_v = out_v;
   // Vector path with TMA head-block stores: channel pairs (a, a + R) in whole
   // 16-byte chunks and 16-byte aligned tables.
-  g.qk_fast = rope_half % 8 == 0 && aligned(gamma, 16) && aligned(cos, 16) && aligned(sin, 16);
-  CUtensorMap to{};
+  g.qk_fast = rope_half % 8 == 0 && aligned(gamma, 16) && aligned(cos, 16) && aligned(sin, 16) &&
+              (!grouped || aligned(gamma_k, 16));
+  const int64_t heads = grouped ? n / 384 : n / 128;
+  CUtensorMap to{}, to_k{}, to_v{};
   if (g.qk_fast) {
-    // Head-major output [N/128, M, 128] bf16 as a 3D map; boxes of 64 channels x
-    // 32 rows (one epilogue warp's rows), 128-byte swizzle; rows past M clipped.
-    cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(m), static_cast<cuuint64_t>(n / 128)};
-    cuuint64_t strides[2] = {256, static_cast<cuuint64_t>(m) * 256};
-    cuuint32_t box[3] = {64, 32, 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = g_encode(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(M5B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    rc = head_major_map(&to, out, m, heads);
+    if (!rc && grouped) rc = head_major_map(&to_k, out_k, m, heads);
+    if (!rc && grouped) rc = head_major_map(&to_v, out_v, m, heads);
+    if (rc) return rc;
   }
-  return gemm_launch(ta, tb, tbh, g, bn, pair, stream, &to);
+  return gemm_launch(ta, tb, tbh, g, bn, pair, stream, &to, grouped ? &to_k : nullptr,
+                     grouped ? &to_v : nullptr);
+}
+
+int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
+                           int mode, const float* a_scales, const float* b_scales,
+                           const void* gamma, const void* cos, const void* sin, int rope_half,
+                           float epsilon, void* out, void* stream) {
+  return qk_projection(a, b, m, n, k, mode, a_scales, b_scales, gamma, nullptr, cos, sin,
+                       rope_half, epsilon, out, nullptr, nullptr, false, stream);
+}
+
+int m5b_projection_qkv_rope(const void* a, const void* b, int64_t m, int64_t heads, int64_t k,
+                            int mode, const float* a_scales, const float* b_scales,
+                            const void* gamma_q, const void* gamma_k, const void* cos,
+                            const void* sin, int rope_half, float epsilon, void* q_out,
+                            void* k_out, void* v_out, void* stream) {
+  if (heads <= 0 || heads > (int64_t(1) << 20))
+    return fail(M5B_EINVAL, "heads must be a positive count of 128-wide heads");
+  return qk_projection(a, b, m, heads * 384, k, mode, a_scales, b_scales, gamma_q, gamma_k, cos,
+                       sin, rope_half, epsilon, q_out, k_out, v_out, true, stream);
 }
 
 int64_t m5b_linear_workspace_bytes(int64_t m, int64_t k) {

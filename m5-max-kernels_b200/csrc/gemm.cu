@@ -256,7 +256,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_b_half,
-                   const __grid_constant__ CUtensorMap tmap_out, const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tmap_out,
+                   const __grid_constant__ CUtensorMap tmap_out_k,
+                   const __grid_constant__ CUtensorMap tmap_out_v, const GemmArgs g) {
   using Cfg = GemmCfg<BN, QK, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int K_ELEMS = (KIND == KIND_BF16 || KIND == KIND_F16) ? 64 : 128;
@@ -302,6 +304,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     tma_prefetch_desc(&tmap_b);
     if (g.num_units > g.num_full) tma_prefetch_desc(&tmap_b_half);
     if ((QK && g.qk_fast) || (!QK && g.tma_store)) tma_prefetch_desc(&tmap_out);
+    if (QK && g.qk_fast && g.grouped) {
+      tma_prefetch_desc(&tmap_out_k);
+      tma_prefetch_desc(&tmap_out_v);
+    }
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -579,7 +585,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
         const int64_t row0 = row - lane;  // this warp's first row
 #pragma unroll 1
         for (int hh = h_first; hh < heads_here; hh += h_step) {
-          const int head = n_col / 128 + hh;
+          // 128-column block of the projection; grouped Q/K/V weights order
+          // the blocks [head, stream], one output tensor per stream.
+          const int hb = n_col / 128 + hh;
+          const int head = g.grouped ? hb / 3 : hb;
+          const int stream_id = g.grouped ? hb - 3 * head : 0;  // 0 Q, 1 K, 2 V
+          const bool norm_rope = stream_id != 2;  // V: projection and layout only
           if (lane == 0) bulk_wait_group_read0();  // the previous store has read the staging
           __syncwarp();
           float sumsq = 0.0f;
@@ -596,7 +607,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
                 const int e = q * 8 + 2 * i;
                 float z0 = acc_value<KIND>(r[e]), z1 = acc_value<KIND>(r[e + 1]);
                 if (g.quantized) {
-                  const int col = head * 128 + c * 32 + e;
+                  const int col = hb * 128 + c * 32 + e;
                   z0 = __fmul_rn(__fmul_rn(z0, sa), __ldg(g.b_scales + col));
                   z1 = __fmul_rn(__fmul_rn(z1, sa), __ldg(g.b_scales + col + 1));
                 }
@@ -618,10 +629,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
           const float inv =
               __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, 128.0f), g.eps)));
           const int R = g.rope_half;
-          const __nv_bfloat16* gm = reinterpret_cast<const __nv_bfloat16*>(g.gamma);
+          const __nv_bfloat16* gm =
+              reinterpret_cast<const __nv_bfloat16*>(stream_id == 1 ? g.gamma_k : g.gamma);
+          const CUtensorMap* omap =
+              stream_id == 0 ? &tmap_out : (stream_id == 1 ? &tmap_out_k : &tmap_out_v);
+          void* obase = stream_id == 0 ? g.out : (stream_id == 1 ? g.out_k : g.out_v);
           if (g.qk_fast) {
             // R % 8 == 0: channel a pairs with a + R, both whole 16-byte chunks.
-            if (row < g.M) {
+            if (row < g.M && norm_rope) {
               const int RC = R >> 3;
               const uint4* cs4 =
                   reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(g.cos) + row * R);
@@ -669,8 +684,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             fence_proxy_async_shared();
             __syncwarp();
             if (lane == 0 && row0 < g.M) {
-              tma_store_3d(&tmap_out, wstage, 0, static_cast<int32_t>(row0), head);
-              tma_store_3d(&tmap_out, wstage + 4096, 64, static_cast<int32_t>(row0), head);
+              tma_store_3d(omap, wstage, 0, static_cast<int32_t>(row0), head);
+              tma_store_3d(omap, wstage + 4096, 64, static_cast<int32_t>(row0), head);
               bulk_commit_group();
             }
           } else if (row < g.M) {
@@ -682,7 +697,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             const __nv_bfloat16* cs = reinterpret_cast<const __nv_bfloat16*>(g.cos) + row * R;
             const __nv_bfloat16* sn = reinterpret_cast<const __nv_bfloat16*>(g.sin) + row * R;
             __nv_bfloat16* yrow =
-                reinterpret_cast<__nv_bfloat16*>(g.out) + (int64_t(head) * g.M + row) * 128;
+                reinterpret_cast<__nv_bfloat16*>(obase) + (int64_t(head) * g.M + row) * 128;
 #pragma unroll 1
             for (int j0 = 0; j0 < 128; j0 += 8) {
               uint4 pk;
@@ -690,6 +705,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const int j = j0 + e;
+                if (!norm_rope) {  // V stream: the BF16 projection itself
+                  h[e] = __float2bfloat16_rn(zat(j));
+                  continue;
+                }
                 const float uj = __fmul_rn(__fmul_rn(zat(j), inv), __bfloat162float(gm[j]));
                 float out = uj;
                 if (j < 2 * R) {
@@ -729,8 +748,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
 
 template <int KIND, int BN, bool QK, bool PAIR>
 static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
-                            const CUtensorMap& to, const GemmArgs& g, int grid,
-                            cudaStream_t stream) {
+                            const CUtensorMap& to, const CUtensorMap& tok, const CUtensorMap& tov,
+                            const GemmArgs& g, int grid, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, QK, PAIR>;
   auto kern = gemm_tc_kernel<KIND, BN, QK, PAIR>;
   static std::atomic<long long> shape[kMaxLaunchDevices];
@@ -752,7 +771,7 @@ static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tbh, to, g);
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tbh, to, tok, tov, g);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -760,16 +779,17 @@ static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const 
 int gemm_block_n(const GemmArgs& g) { return g.N <= 128 ? 128 : 256; }
 
 cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
-                        const CUtensorMap& to, const GemmArgs& g, int bn, int grid, bool pair,
-                        cudaStream_t stream) {
+                        const CUtensorMap& to, const CUtensorMap& tok, const CUtensorMap& tov,
+                        const GemmArgs& g, int bn, int grid, bool pair, cudaStream_t stream) {
   const bool qk = g.epi == EPI_QK;
-#define M5B_KIND_CASE(KIND_)                                                               \
-  case KIND_:                                                                              \
-    if (qk) return pair ? launch_k<KIND_, 256, true, true>(ta, tb, tbh, to, g, grid, stream)   \
-                        : launch_k<KIND_, 128, true, false>(ta, tb, tbh, to, g, grid, stream); \
-    if (pair) return launch_k<KIND_, 256, false, true>(ta, tb, tbh, to, g, grid, stream);      \
-    if (bn == 128) return launch_k<KIND_, 128, false, false>(ta, tb, tbh, to, g, grid, stream); \
-    return launch_k<KIND_, 256, false, false>(ta, tb, tbh, to, g, grid, stream);
+#define M5B_ARGS ta, tb, tbh, to, tok, tov, g, grid, stream
+#define M5B_KIND_CASE(KIND_)                                                  \
+  case KIND_:                                                                 \
+    if (qk) return pair ? launch_k<KIND_, 256, true, true>(M5B_ARGS)          \
+                        : launch_k<KIND_, 128, true, false>(M5B_ARGS);        \
+    if (pair) return launch_k<KIND_, 256, false, true>(M5B_ARGS);             \
+    if (bn == 128) return launch_k<KIND_, 128, false, false>(M5B_ARGS);       \
+    return launch_k<KIND_, 256, false, false>(M5B_ARGS);
   switch (g.kind) {
     M5B_KIND_CASE(KIND_I8)
     M5B_KIND_CASE(KIND_F8)
@@ -778,6 +798,7 @@ cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
     default: return cudaErrorInvalidValue;
   }
 #undef M5B_KIND_CASE
+#undef M5B_ARGS
 }
 
 }  // namespace m5b

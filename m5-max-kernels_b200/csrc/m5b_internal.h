@@ -159,6 +159,10 @@ struct GemmArgs {
   const void* sin;            // [M, R] bf16 (QK)
   int rope_half;
   int qk_fast;                // QK: rope_half % 8 == 0 and 16-byte aligned tables (vector path)
+  int grouped;                // QK: W rows are [head, stream (Q, K, V), 128]; three outputs
+  const void* gamma_k;        // [128] bf16 K-stream gamma (grouped)
+  void* out_k;                // grouped: K output [H, M, 128] bf16
+  void* out_v;                // grouped: V output [H, M, 128] bf16 (projection only)
   int tma_store;              // plain / bias / gate epilogues: 16-bit output leaves through
                               // the output tensor map (32 x 32 boxes, 64-byte swizzle)
   float eps;
@@ -175,9 +179,10 @@ struct GemmArgs {
 // `to`: the Q/K output map (3D {128, M, N/128} bf16, boxes {64, 32, 1}, 128-byte
 // swizzle), or with g.tma_store the [M, N] output map of the other epilogues
 // (2D {N, M} bf16 / fp16, boxes {32, 32}, 64-byte swizzle).
+// `to_k`, `to_v`: the grouped Q/K/V path's K and V output maps (as `to`).
 cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb_half,
-                        const CUtensorMap& to, const GemmArgs& g, int bn, int grid, bool pair,
-                        cudaStream_t stream);
+                        const CUtensorMap& to, const CUtensorMap& to_k, const CUtensorMap& to_v,
+                        const GemmArgs& g, int bn, int grid, bool pair, cudaStream_t stream);
 int gemm_block_n(const GemmArgs& g);
 
 }  // namespace m5b

@@ -7,6 +7,7 @@ The `cuda-b200` backend of the m5kernels operator contracts:
     fused_gated_residual_norm_hadamard_quantize,
     gated_residual_add, unfused_norm   (twin of m5kernels.norm_hadamard)
     projection_qk_rope, qk_norm_rope   (twin of m5kernels.qk_rope)
+    projection_qkv_rope                (grouped Q/K/V layout of the H3 integration)
     rms_quantize                       (twin of m5kernels.rms_quant)
     linear                             (the online quantize -> gemm stage in one call)
 All of them run hand-written CUDA kernels from libm5b200.so through its C ABI
@@ -18,12 +19,13 @@ from .hadamard import SUPPORTED_BLOCK_SIZES, hadamard_quantize, rotate
 from .linear import linear
 from .norm_hadamard import (fused_gated_residual_norm_hadamard_quantize,
                             fused_norm_hadamard_quantize, gated_residual_add, unfused_norm)
-from .qk_rope import projection_qk_rope, qk_norm_rope, rope_tables
+from .qk_rope import (grouped_qkv_weights, projection_qk_rope, projection_qkv_rope, qk_norm_rope,
+                      rope_tables)
 from .rms_quant import rms_quantize
 
 __all__ = [
     "gemm", "quantize", "rotate", "hadamard_quantize", "SUPPORTED_BLOCK_SIZES",
     "fused_norm_hadamard_quantize", "fused_gated_residual_norm_hadamard_quantize",
     "projection_qk_rope", "rope_tables", "linear", "rms_quantize", "gated_residual_add",
-    "unfused_norm", "qk_norm_rope",
+    "unfused_norm", "qk_norm_rope", "projection_qkv_rope", "grouped_qkv_weights",
 ]

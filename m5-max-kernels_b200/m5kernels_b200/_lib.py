@@ -45,6 +45,7 @@ _SIGNATURES = {
     "m5b_qk_norm_rope": ([P, I64, I64, P, P, P, I, F, P, P], I),
     "m5b_gemm": ([P, P, I64, I64, I64, I, P, P, P, I, P, P, I64, P, P, P, I64, P], I),
     "m5b_projection_qk_rope": ([P, P, I64, I64, I64, I, P, P, P, P, P, I, F, P, P], I),
+    "m5b_projection_qkv_rope": ([P, P, I64, I64, I64, I, P, P, P, P, P, P, I, F, P, P, P, P], I),
     "m5b_linear_workspace_bytes": ([I64, I64], I64),
     "m5b_linear": ([P, I, I64, I64, I, P, P, P, I64, I, P, I, P, I64, P], I),
     "m5b_linear_noalloc": ([P, I, I64, I64, I, P, P, P, I64, I, P, I, P], I),

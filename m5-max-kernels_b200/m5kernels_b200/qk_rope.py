@@ -7,6 +7,9 @@ head's 128 channels, applies gamma and rotates the pairs (j, j + R) for j < R,
 and writes the head-major [H, M, 128] BF16 output.  Boundaries: BF16
 projection, FP32 RMS/gamma/RoPE, BF16 output (no BF16 norm intermediate).
 
+`projection_qkv_rope` runs the grouped Q/K/V weight layout [head, stream, 128]
+of the reference's H3 integration in one GEMM with three head-major outputs.
+
 `qk_norm_rope` is the staged comparator (src/m5kernels/qk_rope.py:185-203):
 the same post-processing applied to a stored BF16 projection, bit-identical to
 the fused epilogue, so gemm(..., bf16) -> qk_norm_rope == projection_qk_rope.
@@ -92,6 +95,70 @@ def projection_qk_rope(a, b, gamma, cos, sin, mode="int8", tile=(32, 128, 4, 1),
         ptr(a), ptr(b), m, n, a.shape[1], _lib.MODE[mode], ptr(a_scales), ptr(b_scales),
         ptr(gamma), ptr(cos), ptr(sin), rope_half, eps, ptr(out), _lib.stream_handle(dev)))
     return out
+
+
+def projection_qkv_rope(a, b, gamma_q, gamma_k, cos, sin, mode="int8", *, a_scales=None,
+                        b_scales=None, epsilon=1e-5):
+    """Grouped Q/K/V projection: return BF16 (q, k, v), each [heads, M, 128].
+
+    b holds the native grouped weight order [heads, 3, 128, K] (flattened to
+    [heads*384, K]): per head the Q, K and V channel blocks.  Q and K get
+    per-head RMSNorm with their own gamma and split-half RoPE; V is the BF16
+    projection in head-major layout.  Counterpart of the grouped QKV path of
+    the reference's H3 integration (integrations/h3/qkv-candidate.md:30-43,
+    qkv_reference.h:15-36).
+    """
+    if mode not in ("int8", "bf16"):
+        raise NotImplementedError("grouped Q/K/V projection supports INT8 or BF16 only")
+    if a.dim() != 2 or b.dim() != 2 or 0 in a.shape or 0 in b.shape:
+        raise ValueError("A and B must be nonempty matrices")
+    m, k = a.shape
+    n, kb = b.shape
+    if k != kb:
+        raise ValueError("K mismatch")
+    if n % (3 * HEAD_DIM):
+        raise ValueError("grouped weights must have [heads, 3, 128, K] rows")
+    heads = n // (3 * HEAD_DIM)
+    expected = torch.int8 if mode == "int8" else torch.bfloat16
+    if a.dtype != expected or b.dtype != expected:
+        raise ValueError(f"A and B must both have {mode} dtype")
+    if mode == "int8":
+        if k > 131071:
+            raise NotImplementedError("INT32 worst-case overflow bound exceeded for signed INT8")
+        if (a_scales is None or b_scales is None or tuple(a_scales.shape) != (m,)
+                or tuple(b_scales.shape) != (n,) or a_scales.dtype != torch.float32
+                or b_scales.dtype != torch.float32):
+            raise ValueError("INT8 requires float32 a_scales[M] and b_scales[N]")
+    elif a_scales is not None or b_scales is not None:
+        raise ValueError("BF16 projection does not accept quantization scales")
+    rope_half, eps = _validate_norm(m, HEAD_DIM, gamma_q, cos, sin, epsilon)
+    if tuple(gamma_k.shape) != (HEAD_DIM,) or gamma_k.dtype != torch.bfloat16:
+        raise ValueError("gamma must be a shared bfloat16 vector of length 128")
+    dev = _lib.require_cuda(a, b, gamma_q, gamma_k, cos, sin, a_scales, b_scales)
+    elem = 1 if mode == "int8" else 2
+    pad = (-k) % (16 // elem)
+    a, b = a.contiguous(), b.contiguous()
+    if pad:
+        a = torch.nn.functional.pad(a, (0, pad))
+        b = torch.nn.functional.pad(b, (0, pad))
+    gamma_q, gamma_k = gamma_q.contiguous(), gamma_k.contiguous()
+    cos, sin = cos.contiguous(), sin.contiguous()
+    a_scales = a_scales.contiguous() if a_scales is not None else None
+    b_scales = b_scales.contiguous() if b_scales is not None else None
+    outs = [torch.empty((heads, m, HEAD_DIM), dtype=torch.bfloat16, device=dev) for _ in range(3)]
+    check(_lib.lib().m5b_projection_qkv_rope(
+        ptr(a), ptr(b), m, heads, a.shape[1], _lib.MODE[mode], ptr(a_scales), ptr(b_scales),
+        ptr(gamma_q), ptr(gamma_k), ptr(cos), ptr(sin), rope_half, eps, ptr(outs[0]),
+        ptr(outs[1]), ptr(outs[2]), _lib.stream_handle(dev)))
+    return tuple(outs)
+
+
+def grouped_qkv_weights(wq, wk, wv):
+    """Interleave separate [H*128, K] Q, K, V weights into the grouped [H*3*128, K] order."""
+    if not (wq.shape == wk.shape == wv.shape) or wq.dim() != 2 or wq.shape[0] % HEAD_DIM:
+        raise ValueError("Q, K and V weights must share one [H*128, K] shape")
+    h, k = wq.shape[0] // HEAD_DIM, wq.shape[1]
+    return torch.stack([w.reshape(h, HEAD_DIM, k) for w in (wq, wk, wv)], dim=1).reshape(-1, k)
 
 
 def qk_norm_rope(projected, gamma, cos, sin, *, epsilon=1e-5, threads=128):

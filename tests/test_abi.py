@@ -26,7 +26,8 @@ def test_header_declares_the_operator_contracts():
                      "m5b_fused_norm_hadamard_quantize",
                      "m5b_fused_gated_residual_norm_hadamard_quantize", "m5b_gemm",
                      "m5b_projection_qk_rope", "m5b_last_error", "m5b_device_status",
-                     "m5b_unfused_norm", "m5b_gated_residual_add", "m5b_qk_norm_rope"):
+                     "m5b_unfused_norm", "m5b_gated_residual_add", "m5b_qk_norm_rope",
+                     "m5b_projection_qkv_rope"):
         assert required in names
 
 
@@ -77,6 +78,10 @@ def test_contract_errors_come_back_through_the_abi_without_a_gpu():
                               ctypes.c_void_p(16), _lib.F32, ctypes.c_void_p(16), _lib.F32, None, 0,
                               3, 1e-5, 1, ctypes.c_void_p(16), None)
     assert rc == _lib.EINVAL and b"norm must be" in lib.m5b_last_error()
+    rc = lib.m5b_projection_qkv_rope(ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 0, 128, 0,
+                                     None, None, None, None, None, None, 48, 1e-5, None, None,
+                                     None, None)
+    assert rc == _lib.EINVAL and b"heads" in lib.m5b_last_error()
 
 
 def test_operators_refuse_cpu_tensors():
