@@ -340,6 +340,96 @@ def run_secondary(args, world, rank, local):
     return 0
 
 
+def run_colpar(args, world, rank, local):
+    """Column-parallel FFN-up (BASELINE's C5 variant): M=4096, K=4096, N=16384.
+
+    Each rank holds N / world output channels of W (INT8, offline) and the
+    same bf16 activations; a step quantizes A and produces the full [M, N]
+    bf16 output on EVERY rank.  Fused: m5b_gemm_allgather stores each output
+    tile into all ranks' outputs over NVLink (CUDA-IPC peer mappings), between
+    two one-element all-reduces.  Baseline: local GEMM into [M, N/world], NCCL
+    all_gather_into_tensor, permute into [M, N].  Total work is fixed
+    (strong scaling); times are CUDA events on the stream, max over ranks.
+    """
+    import torch
+    import torch.distributed as dist
+
+    import m5kernels_b200 as m5
+    from m5kernels_b200 import sharding
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    m, k, n = 4096, 4096, 16384
+    c0, c1 = sharding.shard_columns(n, world, rank)
+    g = torch.Generator(device=dev).manual_seed(5)  # same activations on every rank
+    x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+    gw = torch.Generator(device=dev).manual_seed(100 + rank)
+    w = (0.02 * torch.randn(c1 - c0, k, device=dev, generator=gw)).to(torch.bfloat16)
+    wq, sw = m5.quantize(w, "int8")
+    del w
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    gather = sharding.ColumnParallelGather(out) if world > 1 else None
+
+    def fused():
+        q, s = m5.quantize(x, "int8")
+        if gather is not None:
+            gather.step(q, wq, s, sw)
+        else:
+            m5.gemm_allgather(q, wq, out, 0, (), "int8", a_scales=s, b_scales=sw)
+
+    def baseline():
+        q, s = m5.quantize(x, "int8")
+        y = m5.gemm(q, wq, "int8", a_scales=s, b_scales=sw, output_dtype=torch.bfloat16)
+        if world > 1:
+            return sharding.gather_columns(y, world)
+        return y
+
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        return sharding.max_over_ranks(ms, device=dev)
+
+    with ClockSampler(local) as clocks:
+        fused_ms = timed(fused)
+        base_ms = timed(baseline)
+    ops = 2.0 * m * n * k
+    peer_bytes = (world - 1) * m * (c1 - c0) * 2
+    line = {"workload": "colpar_ffn_up", "n_gpus": world, "ms": fused_ms,
+            "value": ops / (fused_ms * 1e-3) / 1e12, "unit": "TOPS", "scaling": "strong",
+            "config": {"M": m, "K": k, "N": n, "N_per_rank": c1 - c0},
+            "kernel": "quant_rows + gemm_tc_kernel<i8,256,pair> (all-gather epilogue)",
+            "nccl_baseline_ms": base_ms, "nccl_baseline_value": ops / (base_ms * 1e-3) / 1e12,
+            "speedup_vs_nccl": base_ms / fused_ms, "steps": args.steps,
+            "nvlink_bytes_out_per_rank": peer_bytes,
+            "nvlink_gbs_per_rank": peer_bytes / (fused_ms * 1e-3) / 1e9 if world > 1 else 0.0,
+            "clocks": clocks.summary()}
+    if gather is not None:
+        gather.barrier()
+        gather.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return 0
@@ -545,7 +635,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="ffn_down",
-                    choices=["ffn_down", "prep_c3", "prep_c4", "qk_c5", "rms_q"],
+                    choices=["ffn_down", "prep_c3", "prep_c4", "qk_c5", "rms_q", "colpar"],
                     help="ffn_down is the headline; the others time one other BASELINE config")
     ap.add_argument("--profile", action="store_true",
                     help="profiling run: timed steps and per-kernel timing only (no e2e, no CPU leg)")
@@ -555,6 +645,8 @@ def main(argv=None):
     world, rank, local = _dist()
     if args.impl == "reference":
         return run_reference(args, world, rank)
+    if args.workload == "colpar":
+        return run_colpar(args, world, rank, local)
     if args.workload != "ffn_down":
         return run_secondary(args, world, rank, local)
     return run_b200(args, world, rank, local)

@@ -190,6 +190,34 @@ M5B_API int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t
              const void* residual, const void* gate, const int32_t* gate_row_map,
              int64_t gate_rows, void* stream);
 
+/* Column-parallel projection with the all-gather fused into the epilogue.
+ * This rank holds n output channels of W (b [n, k], b_scales [n]); its
+ * result columns are columns [col_offset, col_offset + n) of the [m, n_total]
+ * bf16 output that every rank holds.  Each output tile is stored to `out`
+ * (this GPU) and to each of the n_peers buffers in peer_outs (the other
+ * ranks' outputs, mapped into this process with m5b_ipc_import) with NVLink
+ * peer stores, so after every rank's call has completed (order the ranks
+ * with a stream-ordered barrier, e.g. a one-element NCCL all-reduce) every
+ * output holds all n_total columns.  mode INT8 / FP8 (with scales) or BF16;
+ * n % 32 == 0, col_offset % 32 == 0, n_total % 8 == 0, n_peers <= 7.
+ * Replaces the optional column-parallel FFN-up variant's GEMM +
+ * all_gather_into_tensor (the reference itself is
+ * single-GPU: metal.py:237-348 per rank). */
+M5B_API int m5b_gemm_allgather(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
+                               int mode, const float* a_scales, const float* b_scales, void* out,
+                               int64_t n_total, int64_t col_offset, void* const* peer_outs,
+                               int n_peers, void* stream);
+
+/* CUDA IPC of an output buffer (plain peer mapping, no multicast object).
+ * m5b_ipc_export writes the 64-byte handle of the allocation holding `ptr`
+ * and ptr's byte offset inside it; m5b_ipc_import maps another process's
+ * handle and returns the buffer's address in this process; m5b_ipc_release
+ * unmaps it.  Helpers of m5b_gemm_allgather; no counterpart in the
+ * reference. */
+M5B_API int m5b_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+M5B_API int m5b_ipc_import(const void* handle, int64_t offset, void** ptr_out);
+M5B_API int m5b_ipc_release(void* ptr, int64_t offset);
+
 /* Workspace bytes m5b_linear needs for activations [m, k]: the per-token
  * codes (m * k bytes, 256-byte aligned) followed by the fp32 scales. */
 M5B_API int64_t m5b_linear_workspace_bytes(int64_t m, int64_t k);

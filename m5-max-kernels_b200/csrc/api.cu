@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -518,6 +519,21 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMa
   return M5B_OK;
 }
 
+// Row-major [m, n] 16-bit output as a 2D map {n, m}: 32 x 32 boxes, 64-byte swizzle.
+static int output_map(CUtensorMap* map, void* out, int out_dtype, int64_t m, int64_t n) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(n) * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      out_dtype == M5B_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = g_encode(map, dt, 2, out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(M5B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return M5B_OK;
+}
+
 static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
                        GemmArgs& g, int bn, bool pair, void* stream,
                        const CUtensorMap* to = nullptr, const CUtensorMap* to_k = nullptr,
@@ -609,20 +625,104 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
   // epilogue warp with the 64-byte swizzle; the map clips the M and N tails.
   CUtensorMap to{};
   if ((out_dtype == M5B_BF16 || out_dtype == M5B_F16) && n % 8 == 0 && aligned(out, 16)) {
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(n) * 2};
-    cuuint32_t box[2] = {32, 32};
-    cuuint32_t estr[2] = {1, 1};
-    const CUtensorMapDataType dt =
-        out_dtype == M5B_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUresult r = g_encode(&to, dt, 2, out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(M5B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    rc = output_map(&to, out, out_dtype, m, n);
+    if (rc) return rc;
     g.tma_store = 1;
+    g.ldo = n;
     return gemm_launch(ta, tb, tbh, g, bn, pair, stream, &to);
   }
   return gemm_launch(ta, tb, tbh, g, bn, pair, stream);
+}
+
+int m5b_gemm_allgather(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
+                       const float* a_scales, const float* b_scales, void* out, int64_t n_total,
+                       int64_t col_offset, void* const* peer_outs, int n_peers, void* stream) {
+  if (mode != M5B_MODE_INT8 && mode != M5B_MODE_FP8 && mode != M5B_MODE_BF16)
+    return fail(M5B_EUNSUPPORTED, "the all-gather GEMM supports int8, fp8 and bf16 operands");
+  if (m <= 0 || n <= 0 || n_total <= 0) return fail(M5B_EINVAL, "A and B must be nonempty matrices");
+  if (n % 32 || col_offset % 32 || col_offset < 0 || col_offset + n > n_total || n_total % 8)
+    return fail(M5B_EUNSUPPORTED,
+                "column shards must be multiples of 32 columns inside a row of n_total %% 8 == 0");
+  if (n_total > 0x7fffffffLL) return fail(M5B_EUNSUPPORTED, "n_total exceeds 2^31-1");
+  if (n_peers < 0 || n_peers > 7) return fail(M5B_EUNSUPPORTED, "at most 7 peer outputs (8 ranks)");
+  if (n_peers > 0 && !peer_outs) return fail(M5B_EINVAL, "peer output pointers are NULL");
+  if (!out || !aligned(out, 16)) return fail(M5B_EINVAL, "output base address must be 16-byte aligned");
+  for (int q = 0; q < n_peers; ++q)
+    if (!peer_outs[q] || !aligned(peer_outs[q], 16))
+      return fail(M5B_EINVAL, "peer output base addresses must be 16-byte aligned");
+  const bool quant = mode != M5B_MODE_BF16;
+  if (quant && (!a_scales || !b_scales)) return fail(M5B_EINVAL, "scales required");
+  if (!quant && (a_scales || b_scales))
+    return fail(M5B_EINVAL, "float GEMM modes do not accept quantization scales");
+  GemmArgs g{};
+  g.epi = EPI_PLAIN;
+  g.N = static_cast<int>(n);
+  const int bn = gemm_block_n(g);
+  const bool pair = use_pair(EPI_PLAIN, m, n);
+  CUtensorMap ta, tb, tbh;
+  int rc = gemm_common(g, ta, tb, tbh, a, b, m, n, k, mode, bn, pair);
+  if (rc) return rc;
+  g.quantized = quant ? 1 : 0;
+  g.a_scales = a_scales;
+  g.b_scales = b_scales;
+  g.out = out;
+  g.out_dtype = M5B_BF16;
+  CUtensorMap to{};
+  rc = output_map(&to, out, M5B_BF16, m, n_total);
+  if (rc) return rc;
+  g.tma_store = 1;
+  g.ldo = n_total;
+  g.col_off = static_cast<int>(col_offset);
+  g.n_peers = n_peers;
+  for (int q = 0; q < n_peers; ++q) g.peer_out[q] = peer_outs[q];
+  return gemm_launch(ta, tb, tbh, g, bn, pair, stream, &to);
+}
+
+// ---------------------------------------------------------------- CUDA IPC
+// Peer ranks' output buffers are mapped with CUDA IPC (no multicast object).
+// A handle names the whole cudaMalloc allocation; offset locates the buffer
+// inside it (caching allocators hand out sub-blocks of larger segments).
+static PFN_cuMemGetAddressRange_v3020 g_addr_range = nullptr;
+static std::once_flag g_addr_range_once;
+
+int m5b_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out) {
+  if (!ptr || !handle_out || !offset_out) return fail(M5B_EINVAL, "pointer arguments are NULL");
+  std::call_once(g_addr_range_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_addr_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  });
+  if (!g_addr_range) return fail(M5B_ECUDA, "cuMemGetAddressRange is unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = g_addr_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return fail(M5B_ECUDA, "cuMemGetAddressRange failed (%d)", int(r));
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return ok();
+}
+
+int m5b_ipc_import(const void* handle, int64_t offset, void** ptr_out) {
+  if (!handle || !ptr_out || offset < 0) return fail(M5B_EINVAL, "invalid IPC import arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *ptr_out = static_cast<uint8_t*>(base) + offset;
+  return ok();
+}
+
+int m5b_ipc_release(void* ptr, int64_t offset) {
+  if (!ptr || offset < 0) return fail(M5B_EINVAL, "invalid IPC release arguments");
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return ok();
 }
 
 // Head-major output map [heads, M, 128] bf16 as a 3D {128, M, heads} map; boxes

@@ -529,8 +529,26 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             fence_proxy_async_shared();
             __syncwarp();
             if (lane == 0 && row0 < g.M && n_col + c * 32 < g.N) {
-              tma_store_2d(&tmap_out, buf, n_col + c * 32, static_cast<int32_t>(row0));
+              tma_store_2d(&tmap_out, buf, g.col_off + n_col + c * 32, static_cast<int32_t>(row0));
               bulk_commit_group();
+            }
+            if (g.n_peers > 0 && n_col + c * 32 < g.N) {
+              // Column-parallel all-gather: the same 32 x 32 block into every
+              // peer rank's output over NVLink, 16-byte stores, four lanes per
+              // 64-byte row segment (the staging reads are generic-proxy
+              // reads beside the TMA store's, both only read).
+#pragma unroll
+              for (int p = lane; p < 128; p += 32) {
+                const int rr = p >> 2, j = p & 3;
+                if (row0 + rr < g.M) {
+                  const uint4 v =
+                      *reinterpret_cast<const uint4*>(buf + rr * 64 + ((j ^ ((rr >> 1) & 3)) << 4));
+                  const int64_t off =
+                      (row0 + rr) * g.ldo + g.col_off + n_col + c * 32 + j * 8;  // elements
+                  for (int q = 0; q < g.n_peers; ++q)
+                    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(g.peer_out[q]) + off) = v;
+                }
+              }
             }
             ++ostage;
           }
@@ -729,6 +747,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
       }
     }
     if (lane == 0) bulk_wait_group0();  // this warp's TMA stores are complete
+    if (g.n_peers > 0) __threadfence_system();  // peer stores performed before the grid ends
     __syncwarp();
   }
 

@@ -165,6 +165,14 @@ struct GemmArgs {
   void* out_v;                // grouped: V output [H, M, 128] bf16 (projection only)
   int tma_store;              // plain / bias / gate epilogues: 16-bit output leaves through
                               // the output tensor map (32 x 32 boxes, 64-byte swizzle)
+  // Column-parallel all-gather (tma_store path, bf16): this rank's N columns
+  // are columns [col_off, col_off + N) of [M, ldo] outputs, written to the
+  // local output (tensor map) and to every peer rank's output (peer_out,
+  // NVLink peer stores).
+  int col_off;
+  int64_t ldo;
+  int n_peers;
+  void* peer_out[7];
   float eps;
   int num_m_blocks, num_n_blocks, num_k_blocks;
   int group_m;

@@ -14,7 +14,7 @@ All of them run hand-written CUDA kernels from libm5b200.so through its C ABI
 (include/m5b200.h); there is no CPU fallback.
 """
 
-from .cuda import gemm, quantize
+from .cuda import gemm, gemm_allgather, quantize
 from .hadamard import SUPPORTED_BLOCK_SIZES, hadamard_quantize, rotate
 from .linear import linear
 from .norm_hadamard import (fused_gated_residual_norm_hadamard_quantize,
@@ -24,7 +24,7 @@ from .qk_rope import (grouped_qkv_weights, projection_qk_rope, projection_qkv_ro
 from .rms_quant import rms_quantize
 
 __all__ = [
-    "gemm", "quantize", "rotate", "hadamard_quantize", "SUPPORTED_BLOCK_SIZES",
+    "gemm", "gemm_allgather", "quantize", "rotate", "hadamard_quantize", "SUPPORTED_BLOCK_SIZES",
     "fused_norm_hadamard_quantize", "fused_gated_residual_norm_hadamard_quantize",
     "projection_qk_rope", "rope_tables", "linear", "rms_quantize", "gated_residual_add",
     "unfused_norm", "qk_norm_rope", "projection_qkv_rope", "grouped_qkv_weights",

@@ -171,3 +171,31 @@ def gemm(a, b, mode="bf16", tile=(64, 64, 4, 1), a_scales=None, b_scales=None,
         gate.shape[0] if (gate is not None and gate.dim() == 2) else 0,
         _lib.stream_handle(dev)))
     return out
+
+
+def gemm_allgather(a, b, out, col_offset, peer_outs=(), mode="int8", *, a_scales=None,
+                   b_scales=None):
+    """Store this shard's bf16 projection a @ b^T into columns [col_offset,
+    col_offset + N) of `out` [M, N_total] and of every tensor in `peer_outs`
+    (other ranks' outputs mapped into this process, or local buffers).
+
+    The column-parallel all-gather fused into the GEMM epilogue
+    (m5b_gemm_allgather); sharding.ColumnParallelGather runs it across ranks.
+    """
+    import ctypes
+
+    if mode not in ("int8", "fp8", "bf16"):
+        raise NotImplementedError("the all-gather GEMM supports int8, fp8 and bf16 operands")
+    if out.dim() != 2 or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 [M, N_total] tensor")
+    peers = list(peer_outs)
+    if len(peers) > 7:
+        raise NotImplementedError("at most 7 peer outputs (8 ranks)")
+    dev = _lib.require_cuda(a, b, out, a_scales, b_scales, *peers)
+    a, b = a.contiguous(), b.contiguous()
+    arr = (ctypes.c_void_p * 7)(*[p.data_ptr() for p in peers])
+    check(_lib.lib().m5b_gemm_allgather(
+        ptr(a), ptr(b), a.shape[0], b.shape[0], a.shape[1], _lib.MODE[mode], ptr(a_scales),
+        ptr(b_scales), ptr(out), out.shape[1], int(col_offset), arr, len(peers),
+        _lib.stream_handle(dev)))
+    return out

@@ -27,7 +27,8 @@ def test_header_declares_the_operator_contracts():
                      "m5b_fused_gated_residual_norm_hadamard_quantize", "m5b_gemm",
                      "m5b_projection_qk_rope", "m5b_last_error", "m5b_device_status",
                      "m5b_unfused_norm", "m5b_gated_residual_add", "m5b_qk_norm_rope",
-                     "m5b_projection_qkv_rope"):
+                     "m5b_projection_qkv_rope", "m5b_gemm_allgather", "m5b_ipc_export",
+                     "m5b_ipc_import", "m5b_ipc_release"):
         assert required in names
 
 
