@@ -184,9 +184,12 @@ def run_secondary(args, world, rank, local):
     prep_c3: online H128 rotation + per-token INT8 of the FFN-down activations
              (M=4096, K=16384; outlier distribution), HBM bytes 3K+4 per row.
     prep_c4: gated residual + LayerNorm (eps 1e-6, no affine) + AdaLN (2 samples
-             of 2048 tokens) + H128 + INT8 (M=4096, K=4096), bytes 7K+4 per row.
+             of 2048 tokens) + H128 + INT8 (M=4096, K=4096), bytes 7K+4 per row;
+             also the whole C4 step with the Q projection (N=4096, W rotated
+             offline).
     qk_c5:   H256 + INT8 online prep and the Q/K projection with RMSNorm + RoPE
-             (M=9914, K=4096, 32 heads x 128, theta 10000, R=64).
+             (M=9914, K=4096, 32 heads x 128, theta 10000, R=64), token-sharded
+             over the ranks (strong scaling, no collective).
     rms_q:   RMS scale-folding prep (random gamma, H256, INT8) + W8A8 GEMM on the
              reference's rms-quant Q shape (M=4096, K=5376, N=7168).
 
@@ -202,11 +205,22 @@ def run_secondary(args, world, rank, local):
 
     import m5kernels_b200 as m5
 
+    from m5kernels_b200 import sharding
+
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     stream = torch.cuda.current_stream(dev)
     peaks = _peaks()
+    # qk_c5 is token-sharded: rank r owns a contiguous block of the 9914 rows
+    # (weights replicated, no collective); the other workloads run whole per rank.
+    r0, r1 = sharding.shard_rows(9914, world, rank)
+    m_c5 = r1 - r0
 
     def make_set():
         """One input set: (step function, {part name: function})."""
@@ -233,9 +247,26 @@ def run_secondary(args, world, rank, local):
                 return m5.fused_norm_hadamard_quantize(upd, gamma, scale, shift, signs, 128,
                                                        norm="layer", epsilon=1e-6, row_map=rmap)
 
+            w = (0.02 * torch.randn(k, k, device=dev, generator=g)).to(torch.bfloat16)
+            wq, ws = m5.hadamard_quantize(w, 128, signs, "int8")  # offline, untimed
+            del w
+            q0, s0, _ = m5.fused_gated_residual_norm_hadamard_quantize(
+                res, br, gate, gamma, scale, shift, signs, 128, norm="layer", epsilon=1e-6,
+                gate_row_map=rmap, row_map=rmap)
+
+            def full_step():  # BASELINE C4: the fused prep, then the Q projection
+                q, s, _ = m5.fused_gated_residual_norm_hadamard_quantize(
+                    res, br, gate, gamma, scale, shift, signs, 128, norm="layer", epsilon=1e-6,
+                    gate_row_map=rmap, row_map=rmap)
+                return m5.gemm(q, wq, "int8", a_scales=s, b_scales=ws,
+                               output_dtype=torch.bfloat16)
+
             return (lambda: m5.fused_gated_residual_norm_hadamard_quantize(  # noqa: E731
                 res, br, gate, gamma, scale, shift, signs, 128, norm="layer", epsilon=1e-6,
-                gate_row_map=rmap, row_map=rmap)), {"staged": staged}
+                gate_row_map=rmap, row_map=rmap)), {
+                    "staged": staged, "prep_plus_q_gemm": full_step,
+                    "q_gemm": lambda: m5.gemm(q0, wq, "int8", a_scales=s0, b_scales=ws,  # noqa: E731
+                                              output_dtype=torch.bfloat16)}
         if args.workload == "rms_q":
             m, k, n = 4096, 5376, 7168
             x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
@@ -255,7 +286,7 @@ def run_secondary(args, world, rank, local):
                 "gemm": lambda: m5.gemm(q0, wq, "int8", a_scales=s0, b_scales=ws,  # noqa: E731
                                         output_dtype=torch.bfloat16),
             }
-        m, k, n = 9914, 4096, 4096  # qk_c5
+        m, k, n = m_c5, 4096, 4096  # qk_c5: this rank's rows of M = 9914
         x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
         w = (0.02 * torch.randn(n, k, device=dev, generator=g)).to(torch.bfloat16)
         signs = torch.ones(k, dtype=torch.int8, device=dev)
@@ -288,7 +319,7 @@ def run_secondary(args, world, rank, local):
         nbytes, unit = 2.0 * 4096 * 7168 * 5376, "TOPS"
         kernel = "row_prep_kernel<bf16,256,int8> (rms fold) + gemm_tc_kernel<i8,256,plain,pair>"
     else:
-        nbytes, unit = 2.0 * 9914 * 4096 * 4096, "TOPS"
+        nbytes, unit = 2.0 * m_c5 * 4096 * 4096, "TOPS"
         kernel = "lean_kernel<bf16,256,int8,plain> + gemm_tc_kernel<i8,256,qk,pair>"
 
     def graph_ms(fns):
@@ -312,8 +343,14 @@ def run_secondary(args, world, rank, local):
         del graph
         return e0.elapsed_time(e1) / (replays * len(fns))
 
-    ms = graph_ms([st for st, _ in sets])
-    part_ms = {name: graph_ms([parts[name] for _, parts in sets]) for name in sets[0][1]}
+    if world > 1:
+        dist.barrier()
+    ms = sharding.max_over_ranks(graph_ms([st for st, _ in sets]), device=dev)
+    part_ms = {name: sharding.max_over_ranks(graph_ms([parts[name] for _, parts in sets]),
+                                             device=dev)
+               for name in sets[0][1]}
+    if args.workload == "qk_c5":  # whole job: every rank's rows over the slowest rank
+        nbytes = 2.0 * 9914 * 4096 * 4096
     if unit == "GB/s":
         value = nbytes / (ms * 1e-3) / 1e9
         frac = value / peaks["hbm_gbs"]
@@ -321,8 +358,15 @@ def run_secondary(args, world, rank, local):
         value = nbytes / (ms * 1e-3) / 1e12
         frac = value / (2.0 * peaks["bf16"])
     line = {"workload": args.workload, "kernel": kernel, "ms": ms, "value": value, "unit": unit,
-            "frac_of_measured_peak": frac, "steps": args.steps,
-            "timing": f"CUDA graph replay, {SETS} input sets rotating"}
+            "frac_of_measured_peak": frac, "steps": args.steps, "n_gpus": world,
+            "timing": f"CUDA graph replay, {SETS} input sets rotating; max over ranks"}
+    if args.workload == "qk_c5":
+        line.update(scaling="strong", rows_per_rank=[sharding.shard_rows(9914, world, r)[1]
+                                                     - sharding.shard_rows(9914, world, r)[0]
+                                                     for r in range(world)])
+        if world > 1:
+            frac = value / (2.0 * peaks["bf16"] * world)
+            line["frac_of_measured_peak"] = frac
     if part_ms:
         line["parts_ms"] = part_ms
         if "qk_gemm" in part_ms:
@@ -330,6 +374,11 @@ def run_secondary(args, world, rank, local):
             line["qk_fusion_gain"] = part_ms["qk_staged"] / part_ms["qk_gemm"]
         if "staged" in part_ms:
             line["fusion_gain"] = part_ms["staged"] / ms
+        if "prep_plus_q_gemm" in part_ms:  # C4 step: prep + Q projection (M=K=N=4096)
+            q_ops = 2.0 * 4096 ** 3
+            line["step_ms"] = part_ms["prep_plus_q_gemm"]
+            line["step_tops"] = q_ops / (part_ms["prep_plus_q_gemm"] * 1e-3) / 1e12
+            line["q_gemm_tops"] = q_ops / (part_ms["q_gemm"] * 1e-3) / 1e12
         if args.workload == "rms_q":
             prep_bytes = 4096 * (3 * 5376 + 4)
             line["prep_gbs"] = prep_bytes / (part_ms["prep"] * 1e-3) / 1e9
@@ -337,6 +386,9 @@ def run_secondary(args, world, rank, local):
             line["gemm_tops"] = nbytes / (part_ms["gemm"] * 1e-3) / 1e12
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 
