@@ -314,13 +314,13 @@ def run_secondary(args, world, rank, local):
     if args.workload == "prep_c3":
         nbytes, unit, kernel = 4096 * (3 * 16384 + 4), "GB/s", "lean_kernel<bf16,128,int8,plain>"
     elif args.workload == "prep_c4":
-        nbytes, unit, kernel = 4096 * (7 * 4096 + 4), "GB/s", "lean_kernel<bf16,128,int8,norm_gated>"
+        nbytes, unit, kernel = 4096 * (7 * 4096 + 4), "GB/s", "rows16_kernel<bf16,128,int8,norm_gated>"
     elif args.workload == "rms_q":
         nbytes, unit = 2.0 * 4096 * 7168 * 5376, "TOPS"
-        kernel = "row_prep_kernel<bf16,256,int8> (rms fold) + gemm_tc_kernel<i8,256,plain,pair>"
+        kernel = "rows16_kernel<bf16,256,int8,rms> (fold) + gemm_tc_kernel<i8,256,plain,pair>"
     else:
         nbytes, unit = 2.0 * m_c5 * 4096 * 4096, "TOPS"
-        kernel = "lean_kernel<bf16,256,int8,plain> + gemm_tc_kernel<i8,256,qk,pair>"
+        kernel = "rows16_kernel<bf16,256,int8,plain> + gemm_tc_kernel<i8,256,qk,pair>"
 
     def graph_ms(fns):
         for _ in range(args.warmup):

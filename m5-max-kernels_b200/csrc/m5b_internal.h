@@ -103,6 +103,10 @@ cudaError_t launch_quant_rows(const RowPrepArgs& a, const RowMaps& m, int x_dtyp
                               cudaStream_t stream);
 cudaError_t launch_row_prep(const RowPrepArgs& a, const RowMaps& maps, int x_dtype, int block,
                             int out, cudaStream_t stream);
+// Register-streamed kernel of rows16_impl.cuh (16-bit rows of 1024..8192).
+bool rows16_applicable(const RowPrepArgs& a, int x_dtype, int block, int out);
+cudaError_t launch_rows16(const RowPrepArgs& a, int x_dtype, int block, int out,
+                          cudaStream_t stream);
 
 // Staged comparators (staged.cu).
 struct GatedAddArgs {

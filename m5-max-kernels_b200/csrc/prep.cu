@@ -26,6 +26,9 @@ cudaError_t launch_row_prep(const RowPrepArgs& a, const RowMaps& m, int x_dtype,
   // Plain per-token quantization needs no register-resident row: two
   // streaming passes (quant.cu) keep many more rows in flight per SM.
   if (quant_rows_applicable(a, x_dtype, block, out)) return launch_quant_rows(a, m, x_dtype, out, stream);
+  // Rows of 1024..8192 16-bit elements: one row per CTA, 16 elements per
+  // thread streamed through registers (rows16_impl.cuh).
+  if (rows16_applicable(a, x_dtype, block, out)) return launch_rows16(a, x_dtype, block, out, stream);
   switch (x_dtype) {
     case DT_BF16: return launch_row_prep_bf16(a, m, block, out, stream);
     case DT_F16: return launch_row_prep_f16(a, m, block, out, stream);
