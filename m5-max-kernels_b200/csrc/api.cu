@@ -543,6 +543,7 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   int rc = device_state(&status, &sms);
   if (rc) return rc;
   g.status = status;
+  g.sb_vec = (g.b_scales && aligned(g.b_scales, 16)) ? 1 : 0;
   const int tiles = g.num_m_blocks * g.num_n_blocks;
   const int slots = pair ? sms / 2 : sms;  // persistent CTAs (pairs)
   g.num_full = tiles;

@@ -195,13 +195,35 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
   }
 }
 
+// The per-channel scales b_scales[col0 .. col0 + 31] of one 32-column chunk
+// (0 past N): eight 16-byte loads, the same address in every lane of the
+// warp, issued before the chunk's TMEM load so their latency overlaps it.
+__device__ __forceinline__ void load_col_scales(const GemmArgs& g, int col0, float* sb) {
+  if (!g.quantized) return;
+  if (g.sb_vec && col0 + 32 <= g.N) {
+    const float4* p = reinterpret_cast<const float4*>(g.b_scales + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 t = __ldg(p + i);
+      sb[4 * i] = t.x;
+      sb[4 * i + 1] = t.y;
+      sb[4 * i + 2] = t.z;
+      sb[4 * i + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) sb[i] = col0 + i < g.N ? __ldg(g.b_scales + col0 + i) : 0.0f;
+  }
+}
+
 // The same epilogue for one thread's 32 consecutive columns, rounded to the
 // 16-bit output dtype and packed two per word (staged, then a TMA store).
 // Columns past N are computed from zero scale / bias / gate and clipped by
-// the store.
+// the store.  sb: the chunk's column scales (load_col_scales).
 template <int KIND>
 __device__ __forceinline__ void epilogue_pack16(const GemmArgs& g, const uint32_t (&r)[32],
-                                                int64_t row, int col0, float sa, uint32_t* pk) {
+                                                int64_t row, int col0, float sa, const float* sb,
+                                                uint32_t* pk) {
   const int N = g.N;
   const bool full = (col0 + 32 <= N);
   const bool in_row = row < g.M;
@@ -209,11 +231,7 @@ __device__ __forceinline__ void epilogue_pack16(const GemmArgs& g, const uint32_
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     float x = acc_value<KIND>(r[i]);
-    if (g.quantized) {
-      const int col = col0 + i;
-      const float sb = (full || col < N) ? __ldg(g.b_scales + (col < N ? col : 0)) : 0.0f;
-      x = __fmul_rn(__fmul_rn(x, sa), sb);
-    }
+    if (g.quantized) x = __fmul_rn(__fmul_rn(x, sa), sb[i]);
     v[i] = x;
   }
   if (in_row) {
@@ -506,6 +524,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
           const int64_t row0 = row - lane;  // this warp's first row
 #pragma unroll 1
           for (int c = c_first; c < c_end; ++c) {
+            float sbc[32];
+            load_col_scales(g, n_col + c * 32, sbc);
             uint32_t r[32];
             tmem_ld32(taddr + c * 32, r);
             tmem_wait_ld();
@@ -515,7 +535,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
               if (lane == 0) release_acc(acc);
             }
             uint32_t pk[16];
-            epilogue_pack16<KIND>(g, r, row, n_col + c * 32, sa, pk);
+            epilogue_pack16<KIND>(g, r, row, n_col + c * 32, sa, sbc, pk);
             uint8_t* buf = out_stage + (ostage & 1) * 2048;
             if (lane == 0) bulk_wait_group_read1();  // the store two chunks back has read buf
             __syncwarp();
@@ -614,6 +634,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
           float sumsq = 0.0f;
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
+            float sbc[32];
+            load_col_scales(g, hb * 128 + c * 32, sbc);  // N % 128 == 0: whole chunks
             uint32_t r[32];
             tmem_ld32(taddr + hh * 128 + c * 32, r);
             tmem_wait_ld();
@@ -625,9 +647,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
                 const int e = q * 8 + 2 * i;
                 float z0 = acc_value<KIND>(r[e]), z1 = acc_value<KIND>(r[e + 1]);
                 if (g.quantized) {
-                  const int col = hb * 128 + c * 32 + e;
-                  z0 = __fmul_rn(__fmul_rn(z0, sa), __ldg(g.b_scales + col));
-                  z1 = __fmul_rn(__fmul_rn(z1, sa), __ldg(g.b_scales + col + 1));
+                  z0 = __fmul_rn(__fmul_rn(z0, sa), sbc[e]);
+                  z1 = __fmul_rn(__fmul_rn(z1, sa), sbc[e + 1]);
                 }
                 const __nv_bfloat162 zz = __floats2bfloat162_rn(z0, z1);
                 const float f0 = __low2float(zz), f1 = __high2float(zz);

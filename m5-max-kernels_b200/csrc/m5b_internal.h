@@ -151,6 +151,7 @@ struct GemmArgs {
   int quantized;              // apply a_scales / b_scales
   const float* a_scales;      // [M]
   const float* b_scales;      // [N]
+  int sb_vec;                 // b_scales 16-byte aligned: whole chunks load as float4
   void* out;                  // output
   int out_dtype;              // DT_BF16 / DT_F16 / DT_F32 (plain epilogues)
   const float* bias;          // [N] or [P, N]
