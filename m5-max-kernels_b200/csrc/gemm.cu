@@ -54,9 +54,8 @@ struct GemmCfg {
   static constexpr int B_BYTES = B_ROWS * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TILE_M = PAIR ? 2 * kBM : kBM;
-  // (Q/K pair tiles keep 4 stages: their 64 KB of staging would otherwise
-  // leave the L1 almost no room for the epilogue's table loads.)
-  static constexpr int STAGES = QK ? (PAIR ? 4 : 5) : (STAGE_BYTES <= 32 * 1024 ? 6 : 4);
+  // (Q/K pair tiles: 5 stages beside their 64 KB of staging.)
+  static constexpr int STAGES = QK ? 5 : (STAGE_BYTES <= 32 * 1024 ? 6 : 4);
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
   // Epilogue warps: 4, or 8 for pair tiles (each warp drains one of the tile's
@@ -631,6 +630,24 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
           const bool norm_rope = stream_id != 2;  // V: projection and layout only
           if (lane == 0) bulk_wait_group_read0();  // the previous store has read the staging
           __syncwarp();
+          // This row's cos / sin chunks (16 bytes each, R % 8 == 0 path): issued
+          // before the accumulator drain so the loads (one row per lane) are in
+          // flight while pass 1 runs.
+          uint4 cpre[8], spre[8];
+          if (g.qk_fast && norm_rope && row < g.M) {
+            const int RC = g.rope_half >> 3;
+            const uint4* cs4 = reinterpret_cast<const uint4*>(
+                reinterpret_cast<const __nv_bfloat16*>(g.cos) + row * g.rope_half);
+            const uint4* sn4 = reinterpret_cast<const uint4*>(
+                reinterpret_cast<const __nv_bfloat16*>(g.sin) + row * g.rope_half);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              if (q < RC) {
+                cpre[q] = __ldg(cs4 + q);
+                spre[q] = __ldg(sn4 + q);
+              }
+            }
+          }
           float sumsq = 0.0f;
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
@@ -677,17 +694,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             // R % 8 == 0: channel a pairs with a + R, both whole 16-byte chunks.
             if (row < g.M && norm_rope) {
               const int RC = R >> 3;
-              const uint4* cs4 =
-                  reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(g.cos) + row * R);
-              const uint4* sn4 =
-                  reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(g.sin) + row * R);
               const uint4* gm4 = reinterpret_cast<const uint4*>(gm);
-#pragma unroll 1
-              for (int q = 0; q < RC; ++q) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                if (q >= RC) break;
                 uint4 zl = *reinterpret_cast<const uint4*>(chunk(q));
                 uint4 zh = *reinterpret_cast<const uint4*>(chunk(q + RC));
                 const uint4 gl = __ldg(gm4 + q), gh = __ldg(gm4 + q + RC);
-                const uint4 c8 = __ldg(cs4 + q), s8 = __ldg(sn4 + q);
+                const uint4 c8 = cpre[q], s8 = spre[q];
                 __nv_bfloat16* zlh = reinterpret_cast<__nv_bfloat16*>(&zl);
                 __nv_bfloat16* zhh = reinterpret_cast<__nv_bfloat16*>(&zh);
                 const __nv_bfloat16* glh = reinterpret_cast<const __nv_bfloat16*>(&gl);
