@@ -182,7 +182,9 @@ def run_secondary(args, world, rank, local):
     """Other BASELINE configurations (not the headline line): time one workload.
 
     prep_c3: online H128 rotation + per-token INT8 of the FFN-down activations
-             (M=4096, K=16384; outlier distribution), HBM bytes 3K+4 per row.
+             (M=4096, K=16384; outlier distribution), HBM bytes 3K+4 per row; also
+             the whole C3 step (prep + FFN-down GEMM, W rotated offline) in INT8
+             and in E4M3 (per-token / per-channel scales, FP32 accumulation).
     prep_c4: gated residual + LayerNorm (eps 1e-6, no affine) + AdaLN (2 samples
              of 2048 tokens) + H128 + INT8 (M=4096, K=4096), bytes 7K+4 per row;
              also the whole C4 step with the Q projection (N=4096, W rotated
@@ -225,13 +227,28 @@ def run_secondary(args, world, rank, local):
     def make_set():
         """One input set: (step function, {part name: function})."""
         if args.workload == "prep_c3":
-            m, k = 4096, 16384
+            m, k, n = 4096, 16384, 4096
             x = torch.randn(m, k, device=dev, generator=g)
             cols = torch.randperm(k, device=dev, generator=g)[: k // 100]
             x[:, cols] *= 50
             x = x.to(torch.bfloat16)
             signs = torch.ones(k, dtype=torch.int8, device=dev)
-            return (lambda: m5.hadamard_quantize(x, 128, signs, "int8")), {}
+            w = (0.02 * torch.randn(n, k, device=dev, generator=g)).to(torch.bfloat16)
+            # W rotated offline and quantized per output channel, INT8 and E4M3
+            wq8, ws8 = m5.hadamard_quantize(w, 128, signs, "int8")
+            wqf, wsf = m5.hadamard_quantize(w, 128, signs, "fp8")
+            del w
+
+            def step(mode, wq, ws):
+                def run():
+                    q, s = m5.hadamard_quantize(x, 128, signs, mode)
+                    return m5.gemm(q, wq, mode, a_scales=s, b_scales=ws,
+                                   output_dtype=torch.bfloat16)
+                return run
+
+            return (lambda: m5.hadamard_quantize(x, 128, signs, "int8")), {  # noqa: E731
+                "step_int8": step("int8", wq8, ws8), "step_fp8": step("fp8", wqf, wsf),
+                "prep_fp8": lambda: m5.hadamard_quantize(x, 128, signs, "fp8")}  # noqa: E731
         if args.workload == "prep_c4":
             m, k, p = 4096, 4096, 2
             res = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
@@ -374,6 +391,11 @@ def run_secondary(args, world, rank, local):
             line["qk_fusion_gain"] = part_ms["qk_staged"] / part_ms["qk_gemm"]
         if "staged" in part_ms:
             line["fusion_gain"] = part_ms["staged"] / ms
+        if "step_int8" in part_ms:  # C3 whole step: H128 prep + FFN-down GEMM, INT8 and E4M3
+            c3_ops = 2.0 * 4096 * 4096 * 16384
+            line["step_int8_tops"] = c3_ops / (part_ms["step_int8"] * 1e-3) / 1e12
+            line["step_fp8_tops"] = c3_ops / (part_ms["step_fp8"] * 1e-3) / 1e12
+            line["prep_fp8_gbs"] = nbytes / (part_ms["prep_fp8"] * 1e-3) / 1e9
         if "prep_plus_q_gemm" in part_ms:  # C4 step: prep + Q projection (M=K=N=4096)
             q_ops = 2.0 * 4096 ** 3
             line["step_ms"] = part_ms["prep_plus_q_gemm"]

@@ -141,6 +141,33 @@ __device__ __forceinline__ uint8_t e4m3_code(float v, float scale) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(z, __NV_SATFINITE, __NV_E4M3));
 }
 
+// E4M3 codes of four values (v[0..3] -> bytes 0..3 of the word), two at a
+// time with the paired conversion (the .x value lands in the low byte).
+// Exactness: with a power-of-two scale (exact reciprocal) v * inv is the
+// quotient itself; otherwise v * inv * (1 -+ 2^-18) bracket RN(v / scale),
+// and the conversion is monotone, so a pair whose lower and upper bracket
+// codes agree has those codes; a pair where they differ is divided exactly.
+// `fast` is false for scales below 2^-100 (every value divided exactly).
+__device__ __forceinline__ uint32_t e4m3_pair_code(float a, float b, float scale, float inv,
+                                                   bool fast, bool exact_inv) {
+  if (fast) {
+    const float2 t = __fmul2_rn(make_float2(a, b), make_float2(inv, inv));
+    if (exact_inv) return __nv_cvt_float2_to_fp8x2(t, __NV_SATFINITE, __NV_E4M3);
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(
+        __fmul2_rn(t, make_float2(1.0f - 0x1p-18f, 1.0f - 0x1p-18f)), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(
+        __fmul2_rn(t, make_float2(1.0f + 0x1p-18f, 1.0f + 0x1p-18f)), __NV_SATFINITE, __NV_E4M3);
+    if (lo == hi) return lo;
+  }
+  return __nv_cvt_float2_to_fp8x2(make_float2(__fdiv_rn(a, scale), __fdiv_rn(b, scale)),
+                                  __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ uint32_t e4m3_word(const float* v, float scale, float inv, bool fast) {
+  const bool exact_inv = (__float_as_uint(scale) & 0x007FFFFFu) == 0u;
+  return e4m3_pair_code(v[0], v[1], scale, inv, fast, exact_inv) |
+         (e4m3_pair_code(v[2], v[3], scale, inv, fast, exact_inv) << 16);
+}
+
 // ---------------------------------------------------------------------------
 // Device status word: error codes recorded by bounded waits.
 // ---------------------------------------------------------------------------

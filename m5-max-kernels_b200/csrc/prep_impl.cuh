@@ -670,13 +670,7 @@ __global__ void __launch_bounds__(512)
           for (int w0 = 0; w0 < kChunk / 4; w0 += 4) {
             uint32_t words[4];
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              const float* p = v + 4 * (w0 + w);
-              words[w] = quant_e4m3(p[0], scale, rinv, fast) |
-                         (quant_e4m3(p[1], scale, rinv, fast) << 8) |
-                         (quant_e4m3(p[2], scale, rinv, fast) << 16) |
-                         (quant_e4m3(p[3], scale, rinv, fast) << 24);
-            }
+            for (int w = 0; w < 4; ++w) words[w] = e4m3_word(v + 4 * (w0 + w), scale, rinv, fast);
             *reinterpret_cast<uint4*>(qrow + j0 + 4 * w0) =
                 make_uint4(words[0], words[1], words[2], words[3]);
           }

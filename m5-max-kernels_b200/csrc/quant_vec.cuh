@@ -135,20 +135,6 @@ static __device__ __forceinline__ uint32_t code_i8_exact(float v, float scale) {
   return static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu;
 }
 
-static __device__ __forceinline__ uint32_t code_e4m3(float v, float scale, float inv, bool fast) {
-  if (fast) {
-    const float t = __fmul_rn(v, inv);
-    if ((__float_as_uint(scale) & 0x007FFFFFu) == 0u)  // exact reciprocal: t == v / scale
-      return static_cast<uint32_t>(__nv_cvt_float_to_fp8(t, __NV_SATFINITE, __NV_E4M3));
-    const __nv_fp8x2_storage_t two = __nv_cvt_float2_to_fp8x2(
-        make_float2(__fmul_rn(t, 1.0f - 0x1p-18f), __fmul_rn(t, 1.0f + 0x1p-18f)), __NV_SATFINITE,
-        __NV_E4M3);
-    if ((two & 0xFFu) == (two >> 8)) return two & 0xFFu;
-  }
-  return static_cast<uint32_t>(
-      __nv_cvt_float_to_fp8(__fdiv_rn(v, scale), __NV_SATFINITE, __NV_E4M3));
-}
-
 // Codes of one 16-byte vector into `words` (V/4 words).
 template <typename T, int OUT>
 __device__ __forceinline__ void vec_codes(const uint4& raw, float scale, float inv, bool fast,
@@ -158,11 +144,7 @@ __device__ __forceinline__ void vec_codes(const uint4& raw, float scale, float i
   if constexpr (OUT == OUT_E4M3) {
     unpack<T>(raw, v);
 #pragma unroll
-    for (int w = 0; w < V / 4; ++w)
-      words[w] = code_e4m3(v[4 * w], scale, inv, fast) |
-                 (code_e4m3(v[4 * w + 1], scale, inv, fast) << 8) |
-                 (code_e4m3(v[4 * w + 2], scale, inv, fast) << 16) |
-                 (code_e4m3(v[4 * w + 3], scale, inv, fast) << 24);
+    for (int w = 0; w < V / 4; ++w) words[w] = e4m3_word(v + 4 * w, scale, inv, fast);
   } else {
     if (fast) {
       if (pack_i8_vec<T>(raw, i8_bracket(inv, scale), words) != 0u) {

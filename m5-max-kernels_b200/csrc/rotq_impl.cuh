@@ -540,11 +540,10 @@ __global__ void __launch_bounds__(kThreads, MODE == kPlain ? 2 : 1)
           uint32_t words[4];
           if constexpr (OUT == OUT_E4M3) {
 #pragma unroll
-            for (int w = 0; w < 4; ++w)
-              words[w] = quant_e4m3(p[2 * w].x, scale, rinv, fast) |
-                         (quant_e4m3(p[2 * w].y, scale, rinv, fast) << 8) |
-                         (quant_e4m3(p[2 * w + 1].x, scale, rinv, fast) << 16) |
-                         (quant_e4m3(p[2 * w + 1].y, scale, rinv, fast) << 24);
+            for (int w = 0; w < 4; ++w) {
+              const float q4[4] = {p[2 * w].x, p[2 * w].y, p[2 * w + 1].x, p[2 * w + 1].y};
+              words[w] = e4m3_word(q4, scale, rinv, fast);
+            }
           } else if (fast) {
             const I8Bracket br = i8_bracket(rinv, scale);
             uint32_t acc = 0u;

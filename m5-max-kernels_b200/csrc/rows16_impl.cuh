@@ -485,11 +485,7 @@ __global__ void __launch_bounds__(MAXT, 65536 / (MAXT * 64))
           const bool fast = scale >= 0x1p-100f;
           if constexpr (OUT == OUT_E4M3) {
 #pragma unroll
-            for (int w = 0; w < 4; ++w)
-              words[w] = quant_e4m3(vv[4 * w], scale, rinv, fast) |
-                         (quant_e4m3(vv[4 * w + 1], scale, rinv, fast) << 8) |
-                         (quant_e4m3(vv[4 * w + 2], scale, rinv, fast) << 16) |
-                         (quant_e4m3(vv[4 * w + 3], scale, rinv, fast) << 24);
+            for (int w = 0; w < 4; ++w) words[w] = e4m3_word(vv + 4 * w, scale, rinv, fast);
           } else if (fast) {
             quant_i8_fast16(vv, scale, rinv, words);
           } else {
