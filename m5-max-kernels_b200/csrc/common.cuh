@@ -168,6 +168,58 @@ __device__ __forceinline__ uint32_t e4m3_word(const float* v, float scale, float
          (e4m3_pair_code(v[2], v[3], scale, inv, fast, exact_inv) << 16);
 }
 
+// Q/K post-processing on packed pairs (GEMM epilogue and the staged kernel).
+// A packed bf16 pair as two floats (exact).
+__device__ __forceinline__ float2 bf16x2_f2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+__device__ __forceinline__ uint32_t f2_bf16x2(float2 v) {
+  const __nv_bfloat162 h = __float22bfloat162_rn(v);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t u4w(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// Split-half RoPE of one 16-byte chunk pair; the same IEEE operations per
+// element as the scalar form:
+//   ul = (zl * inv) * gl, uh = (zh * inv) * gh      (packed pairs)
+//   zl' = bf16(ul * c - uh * s), zh' = bf16(uh * c + ul * s)   (scalar)
+// Packed-pair products are used only where a product feeds another product:
+// a packed multiply feeding a packed add was observed to be contracted into
+// a fused multiply-add (one rounding instead of two), which the scalar
+// __fmul_rn / __fadd_rn / __fsub_rn intrinsics never are.
+__device__ __forceinline__ void rope_chunk16(uint4& zl, uint4& zh, const uint4& gl,
+                                             const uint4& gh, const uint4& c8, const uint4& s8,
+                                             float inv) {
+  const float2 inv2 = make_float2(inv, inv);
+  uint32_t ol[4], oh[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float2 ul = __fmul2_rn(__fmul2_rn(bf16x2_f2(u4w(zl, p)), inv2), bf16x2_f2(u4w(gl, p)));
+    const float2 uh = __fmul2_rn(__fmul2_rn(bf16x2_f2(u4w(zh, p)), inv2), bf16x2_f2(u4w(gh, p)));
+    const float2 c = bf16x2_f2(u4w(c8, p));
+    const float2 sv = bf16x2_f2(u4w(s8, p));
+    const float2 lo = make_float2(__fsub_rn(__fmul_rn(ul.x, c.x), __fmul_rn(uh.x, sv.x)),
+                                  __fsub_rn(__fmul_rn(ul.y, c.y), __fmul_rn(uh.y, sv.y)));
+    const float2 hi = make_float2(__fadd_rn(__fmul_rn(uh.x, c.x), __fmul_rn(ul.x, sv.x)),
+                                  __fadd_rn(__fmul_rn(uh.y, c.y), __fmul_rn(ul.y, sv.y)));
+    ol[p] = f2_bf16x2(lo);
+    oh[p] = f2_bf16x2(hi);
+  }
+  zl = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+  zh = make_uint4(oh[0], oh[1], oh[2], oh[3]);
+}
+// Unrotated channels: bf16((z * inv) * g) on packed pairs.
+__device__ __forceinline__ uint4 norm_chunk16(const uint4& z, const uint4& g8, float inv) {
+  const float2 inv2 = make_float2(inv, inv);
+  uint32_t o[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p)
+    o[p] = f2_bf16x2(__fmul2_rn(__fmul2_rn(bf16x2_f2(u4w(z, p)), inv2), bf16x2_f2(u4w(g8, p))));
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // ---------------------------------------------------------------------------
 // Device status word: error codes recorded by bounded waits.
 // ---------------------------------------------------------------------------

@@ -96,7 +96,6 @@ __device__ __forceinline__ float bf16_load(const void* base, int64_t i) {
 __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }
-
 // Plain / bias / gate epilogue for one thread's 32 consecutive columns.
 template <int KIND>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t (&r)[32],
@@ -228,10 +227,12 @@ __device__ __forceinline__ void epilogue_pack16(const GemmArgs& g, const uint32_
   const bool in_row = row < g.M;
   float v[32];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    float x = acc_value<KIND>(r[i]);
-    if (g.quantized) x = __fmul_rn(__fmul_rn(x, sa), sb[i]);
-    v[i] = x;
+  for (int i = 0; i < 32; i += 2) {  // packed pairs: two IEEE multiplies per element
+    float2 x = make_float2(acc_value<KIND>(r[i]), acc_value<KIND>(r[i + 1]));
+    if (g.quantized)
+      x = __fmul2_rn(__fmul2_rn(x, make_float2(sa, sa)), make_float2(sb[i], sb[i + 1]));
+    v[i] = x.x;
+    v[i + 1] = x.y;
   }
   if (in_row) {
     const int64_t base = row * int64_t(N) + col0;
@@ -662,12 +663,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const int e = q * 8 + 2 * i;
-                float z0 = acc_value<KIND>(r[e]), z1 = acc_value<KIND>(r[e + 1]);
-                if (g.quantized) {
-                  z0 = __fmul_rn(__fmul_rn(z0, sa), sbc[e]);
-                  z1 = __fmul_rn(__fmul_rn(z1, sa), sbc[e + 1]);
-                }
-                const __nv_bfloat162 zz = __floats2bfloat162_rn(z0, z1);
+                float2 z = make_float2(acc_value<KIND>(r[e]), acc_value<KIND>(r[e + 1]));
+                if (g.quantized)
+                  z = __fmul2_rn(__fmul2_rn(z, make_float2(sa, sa)),
+                                 make_float2(sbc[e], sbc[e + 1]));
+                const __nv_bfloat162 zz = __float22bfloat162_rn(z);
                 const float f0 = __low2float(zz), f1 = __high2float(zz);
                 sumsq = __fmaf_rn(f0, f0, sumsq);
                 sumsq = __fmaf_rn(f1, f1, sumsq);
@@ -700,39 +700,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
                 if (q >= RC) break;
                 uint4 zl = *reinterpret_cast<const uint4*>(chunk(q));
                 uint4 zh = *reinterpret_cast<const uint4*>(chunk(q + RC));
-                const uint4 gl = __ldg(gm4 + q), gh = __ldg(gm4 + q + RC);
-                const uint4 c8 = cpre[q], s8 = spre[q];
-                __nv_bfloat16* zlh = reinterpret_cast<__nv_bfloat16*>(&zl);
-                __nv_bfloat16* zhh = reinterpret_cast<__nv_bfloat16*>(&zh);
-                const __nv_bfloat16* glh = reinterpret_cast<const __nv_bfloat16*>(&gl);
-                const __nv_bfloat16* ghh = reinterpret_cast<const __nv_bfloat16*>(&gh);
-                const __nv_bfloat16* ch = reinterpret_cast<const __nv_bfloat16*>(&c8);
-                const __nv_bfloat16* sh = reinterpret_cast<const __nv_bfloat16*>(&s8);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                  const float ul = __fmul_rn(__fmul_rn(__bfloat162float(zlh[e]), inv),
-                                             __bfloat162float(glh[e]));
-                  const float uh = __fmul_rn(__fmul_rn(__bfloat162float(zhh[e]), inv),
-                                             __bfloat162float(ghh[e]));
-                  const float cv = __bfloat162float(ch[e]), sv = __bfloat162float(sh[e]);
-                  zlh[e] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(ul, cv), __fmul_rn(uh, sv)));
-                  zhh[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(uh, cv), __fmul_rn(ul, sv)));
-                }
+                rope_chunk16(zl, zh, __ldg(gm4 + q), __ldg(gm4 + q + RC), cpre[q], spre[q], inv);
                 *reinterpret_cast<uint4*>(chunk(q)) = zl;
                 *reinterpret_cast<uint4*>(chunk(q + RC)) = zh;
               }
 #pragma unroll 1
-              for (int q = 2 * RC; q < 16; ++q) {
-                uint4 z = *reinterpret_cast<const uint4*>(chunk(q));
-                const uint4 g8 = __ldg(gm4 + q);
-                __nv_bfloat16* zh = reinterpret_cast<__nv_bfloat16*>(&z);
-                const __nv_bfloat16* gh = reinterpret_cast<const __nv_bfloat16*>(&g8);
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                  zh[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(__bfloat162float(zh[e]), inv),
-                                                        __bfloat162float(gh[e])));
-                *reinterpret_cast<uint4*>(chunk(q)) = z;
-              }
+              for (int q = 2 * RC; q < 16; ++q)
+                *reinterpret_cast<uint4*>(chunk(q)) =
+                    norm_chunk16(*reinterpret_cast<const uint4*>(chunk(q)), __ldg(gm4 + q), inv);
             }
             fence_proxy_async_shared();
             __syncwarp();

@@ -194,39 +194,16 @@ __global__ void __launch_bounds__(kQkThreads)
         for (int q = 0; q < RC; ++q) {
           uint4 zl = *reinterpret_cast<const uint4*>(qk_chunk(stage, lane, q));
           uint4 zh = *reinterpret_cast<const uint4*>(qk_chunk(stage, lane, q + RC));
-          const uint4 gl = __ldg(gm4 + q), gh = __ldg(gm4 + q + RC);
-          const uint4 c8 = __ldg(cs4 + q), s8 = __ldg(sn4 + q);
-          __nv_bfloat16* zlh = reinterpret_cast<__nv_bfloat16*>(&zl);
-          __nv_bfloat16* zhh = reinterpret_cast<__nv_bfloat16*>(&zh);
-          const __nv_bfloat16* glh = reinterpret_cast<const __nv_bfloat16*>(&gl);
-          const __nv_bfloat16* ghh = reinterpret_cast<const __nv_bfloat16*>(&gh);
-          const __nv_bfloat16* ch = reinterpret_cast<const __nv_bfloat16*>(&c8);
-          const __nv_bfloat16* sh = reinterpret_cast<const __nv_bfloat16*>(&s8);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float ul =
-                __fmul_rn(__fmul_rn(__bfloat162float(zlh[e]), inv), __bfloat162float(glh[e]));
-            const float uh =
-                __fmul_rn(__fmul_rn(__bfloat162float(zhh[e]), inv), __bfloat162float(ghh[e]));
-            const float cv = __bfloat162float(ch[e]), sv = __bfloat162float(sh[e]);
-            zlh[e] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(ul, cv), __fmul_rn(uh, sv)));
-            zhh[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(uh, cv), __fmul_rn(ul, sv)));
-          }
+          rope_chunk16(zl, zh, __ldg(gm4 + q), __ldg(gm4 + q + RC), __ldg(cs4 + q),
+                       __ldg(sn4 + q), inv);
           *reinterpret_cast<uint4*>(qk_chunk(stage, lane, q)) = zl;
           *reinterpret_cast<uint4*>(qk_chunk(stage, lane, q + RC)) = zh;
         }
 #pragma unroll 1
-        for (int q = 2 * RC; q < 16; ++q) {
-          uint4 z = *reinterpret_cast<const uint4*>(qk_chunk(stage, lane, q));
-          const uint4 g8 = __ldg(gm4 + q);
-          __nv_bfloat16* zh = reinterpret_cast<__nv_bfloat16*>(&z);
-          const __nv_bfloat16* gh = reinterpret_cast<const __nv_bfloat16*>(&g8);
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            zh[e] = __float2bfloat16_rn(
-                __fmul_rn(__fmul_rn(__bfloat162float(zh[e]), inv), __bfloat162float(gh[e])));
-          *reinterpret_cast<uint4*>(qk_chunk(stage, lane, q)) = z;
-        }
+        for (int q = 2 * RC; q < 16; ++q)
+          *reinterpret_cast<uint4*>(qk_chunk(stage, lane, q)) =
+              norm_chunk16(*reinterpret_cast<const uint4*>(qk_chunk(stage, lane, q)),
+                           __ldg(gm4 + q), inv);
       }
       __syncwarp();
       // ---- the finished block: rows row0.. of head `head`, contiguous
