@@ -155,7 +155,25 @@ __device__ __forceinline__ float quad_chunk_sum(const float2* v, float mean, int
 }
 
 // Row total of per-quad chunk sums in the canonical tree.  `part` holds one
-// float per warp (this reduction's own buffer); one CTA barrier.
+// float per warp (this reduction's own buffer); one CTA barrier.  After the
+// barrier lane l forms old warp l's sum (four new warps, pairwise) and the
+// sixteen old-warp sums (zero-padded) are combined pairwise by a xor
+// butterfly over lanes 0-15 -- the same pairing as a sequential pairwise
+// tree -- and broadcast from lane 0.
+__device__ __forceinline__ float old_warp_sum(const float* part, int l, int nwarps, int old_warps) {
+  if (l >= old_warps) return 0.0f;
+  const float p0 = 4 * l < nwarps ? part[4 * l] : 0.0f;
+  const float p1 = 4 * l + 1 < nwarps ? part[4 * l + 1] : 0.0f;
+  const float p2 = 4 * l + 2 < nwarps ? part[4 * l + 2] : 0.0f;
+  const float p3 = 4 * l + 3 < nwarps ? part[4 * l + 3] : 0.0f;
+  return __fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3));
+}
+__device__ __forceinline__ float pairwise16(float o) {
+#pragma unroll
+  for (int off = 1; off < 16; off <<= 1) o = __fadd_rn(o, __shfl_xor_sync(kFull, o, off));
+  return __shfl_sync(kFull, o, 0);
+}
+
 __device__ __forceinline__ float row_total(float c, float* part, int warp, int lane, int nwarps,
                                            int old_warps) {
   c = __fadd_rn(c, __shfl_xor_sync(kFull, c, 4));
@@ -163,24 +181,7 @@ __device__ __forceinline__ float row_total(float c, float* part, int warp, int l
   c = __fadd_rn(c, __shfl_xor_sync(kFull, c, 16));
   if (lane == 0) part[warp] = c;
   __syncthreads();
-  float o[16];
-#pragma unroll
-  for (int w = 0; w < 16; ++w) {
-    if (w < old_warps) {
-      const float p0 = 4 * w < nwarps ? part[4 * w] : 0.0f;
-      const float p1 = 4 * w + 1 < nwarps ? part[4 * w + 1] : 0.0f;
-      const float p2 = 4 * w + 2 < nwarps ? part[4 * w + 2] : 0.0f;
-      const float p3 = 4 * w + 3 < nwarps ? part[4 * w + 3] : 0.0f;
-      o[w] = __fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3));
-    } else {
-      o[w] = 0.0f;
-    }
-  }
-#pragma unroll
-  for (int step = 1; step < 16; step <<= 1)
-#pragma unroll
-    for (int w = 0; w + step < 16; w += 2 * step) o[w] = __fadd_rn(o[w], o[w + step]);
-  return o[0];
+  return pairwise16(old_warp_sum(part, lane & 15, nwarps, old_warps));
 }
 
 __device__ __forceinline__ float row_max(float m, float* part, int warp, int lane, int nwarps) {
@@ -188,8 +189,10 @@ __device__ __forceinline__ float row_max(float m, float* part, int warp, int lan
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
   if (lane == 0) part[warp] = m;
   __syncthreads();
-  float t = part[0];
-  for (int w = 1; w < nwarps; ++w) t = fmaxf(t, part[w]);
+  // both half-warps reduce the same 16 partials (nwarps <= 16: rows of <= 8192)
+  float t = (lane & 15) < nwarps ? part[lane & 15] : 0.0f;
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) t = fmaxf(t, __shfl_xor_sync(kFull, t, off));
   return t;
 }
 
@@ -206,26 +209,11 @@ __device__ __forceinline__ float2 row_total_max(float c, float m, float* part, f
     part_max[warp] = m;
   }
   __syncthreads();
-  float o[16];
+  const float total = pairwise16(old_warp_sum(part, lane & 15, nwarps, old_warps));
+  float t = (lane & 15) < nwarps ? part_max[lane & 15] : 0.0f;
 #pragma unroll
-  for (int w = 0; w < 16; ++w) {
-    if (w < old_warps) {
-      const float p0 = 4 * w < nwarps ? part[4 * w] : 0.0f;
-      const float p1 = 4 * w + 1 < nwarps ? part[4 * w + 1] : 0.0f;
-      const float p2 = 4 * w + 2 < nwarps ? part[4 * w + 2] : 0.0f;
-      const float p3 = 4 * w + 3 < nwarps ? part[4 * w + 3] : 0.0f;
-      o[w] = __fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3));
-    } else {
-      o[w] = 0.0f;
-    }
-  }
-#pragma unroll
-  for (int step = 1; step < 16; step <<= 1)
-#pragma unroll
-    for (int w = 0; w + step < 16; w += 2 * step) o[w] = __fadd_rn(o[w], o[w + step]);
-  float t = part_max[0];
-  for (int w = 1; w < nwarps; ++w) t = fmaxf(t, part_max[w]);
-  return make_float2(o[0], t);
+  for (int off = 8; off > 0; off >>= 1) t = fmaxf(t, __shfl_xor_sync(kFull, t, off));
+  return make_float2(total, t);
 }
 
 // ---------------------------------------------------------------- transforms
