@@ -121,22 +121,23 @@ __device__ __forceinline__ float quad_chunk_sum(const float2* v, float mean, int
 #pragma unroll
   for (int p = 0; p < 4; ++p) A[p] = f2(0.0f);
   const float2 nm = f2(-mean);
+  // Branch-free: every lane adds its elements at every stage, but only lane
+  // q == s holds the chain's accumulators at stage s (the others' results are
+  // replaced by the shuffle that follows), so the chain is unchanged.
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
-    if (q == s) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < 2; ++h) {
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const float2 x = v[4 * h + p];
-          if constexpr (KIND == 0) {
-            A[p] = __fadd2_rn(A[p], x);
-          } else if constexpr (KIND == 1) {
-            A[p] = __ffma2_rn(x, x, A[p]);
-          } else {
-            const float2 d = __fadd2_rn(x, nm);
-            A[p] = __ffma2_rn(d, d, A[p]);
-          }
+      for (int p = 0; p < 4; ++p) {
+        const float2 x = v[4 * h + p];
+        if constexpr (KIND == 0) {
+          A[p] = __fadd2_rn(A[p], x);
+        } else if constexpr (KIND == 1) {
+          A[p] = __ffma2_rn(x, x, A[p]);
+        } else {
+          const float2 d = __fadd2_rn(x, nm);
+          A[p] = __ffma2_rn(d, d, A[p]);
         }
       }
     }
