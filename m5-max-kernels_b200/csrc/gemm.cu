@@ -552,19 +552,24 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
               tma_store_2d(&tmap_out, buf, g.col_off + n_col + c * 32, static_cast<int32_t>(row0));
               bulk_commit_group();
             }
-            if (g.n_peers > 0 && n_col + c * 32 < g.N) {
-              // Column-parallel all-gather: the same 32 x 32 block into every
-              // peer rank's output over NVLink, 16-byte stores, four lanes per
-              // 64-byte row segment (the staging reads are generic-proxy
-              // reads beside the TMA store's, both only read).
+            if (g.n_peers > 0 && ((c - c_first) & 1)) {
+              // Column-parallel all-gather, after every second chunk: the two
+              // staged 32 x 32 blocks (this chunk's buffer and the previous
+              // one's) go to every peer rank's output over NVLink as 128-byte
+              // row segments, eight lanes per row, 16-byte stores.  (Staging
+              // reads are generic-proxy reads beside the TMA stores', both
+              // only read; the previous buffer is refilled only after these.)
+              // Every warp drains an even number of chunks per tile.
+              const uint8_t* bufs[2] = {out_stage + ((ostage - 1) & 1) * 2048, buf};
+              const int col_pair = n_col + (c - 1) * 32;
 #pragma unroll
-              for (int p = lane; p < 128; p += 32) {
-                const int rr = p >> 2, j = p & 3;
-                if (row0 + rr < g.M) {
-                  const uint4 v =
-                      *reinterpret_cast<const uint4*>(buf + rr * 64 + ((j ^ ((rr >> 1) & 3)) << 4));
-                  const int64_t off =
-                      (row0 + rr) * g.ldo + g.col_off + n_col + c * 32 + j * 8;  // elements
+              for (int p = lane; p < 256; p += 32) {
+                const int rr = p >> 3, h = (p >> 2) & 1, j = p & 3;
+                const int col = col_pair + h * 32 + j * 8;
+                if (row0 + rr < g.M && col < g.N) {
+                  const uint4 v = *reinterpret_cast<const uint4*>(bufs[h] + rr * 64 +
+                                                                  ((j ^ ((rr >> 1) & 3)) << 4));
+                  const int64_t off = (row0 + rr) * g.ldo + g.col_off + col;  // elements
                   for (int q = 0; q < g.n_peers; ++q)
                     *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(g.peer_out[q]) + off) = v;
                 }
