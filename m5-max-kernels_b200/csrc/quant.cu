@@ -42,8 +42,10 @@ __device__ __forceinline__ float cta_peak(float peak, float* red) {
 }
 
 // VPT > 0: each thread holds VPT vectors of the row in registers (one HBM
-// read).  VPT == 0: two streaming passes for very wide rows.
-template <typename T, int OUT, int VPT>
+// read).  VPT == 0: two streaming passes for very wide rows.  EXACT: the row
+// is exactly VPT * kThreads vectors (K = 2048 * 2^k for 16-bit inputs), so no
+// vector needs a bounds guard.
+template <typename T, int OUT, int VPT, bool EXACT>
 __global__ void __launch_bounds__(kThreads)
     quant_rows_kernel(const T* __restrict__ x, int64_t rows, int64_t K, uint8_t* __restrict__ q,
                       float* __restrict__ s) {
@@ -63,7 +65,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int j = tid + i * kThreads;
-        raw[i] = j < nvec ? __ldg(xr + j) : make_uint4(0, 0, 0, 0);
+        raw[i] = (EXACT || j < nvec) ? __ldg(xr + j) : make_uint4(0, 0, 0, 0);
       }
       Peak<T> pk;
 #pragma unroll
@@ -85,7 +87,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
           const int j = tid + i * kThreads;
-          if (j < nvec) {
+          if (EXACT || j < nvec) {
             uint32_t words[V / 4];
             const uint32_t acc = pack_i8_vec<T>(raw[i], br, words);
             store_codes<T>(qr, j, words);
@@ -148,11 +150,13 @@ __global__ void __launch_bounds__(kThreads)
 
 template <typename T, int OUT, int VPT>
 cudaError_t launch_quant_v(const RowPrepArgs& a, cudaStream_t stream) {
-  auto kern = quant_rows_kernel<T, OUT, VPT>;
-  static std::atomic<long long> shape[kMaxLaunchDevices];
+  const bool exact = VPT > 0 && a.K / kVec<T> == int64_t(VPT) * kThreads;
+  auto kern = exact ? quant_rows_kernel<T, OUT, VPT, VPT != 0>
+                    : quant_rows_kernel<T, OUT, VPT, false>;
+  static std::atomic<long long> shape[2][kMaxLaunchDevices];
   int dev = 0, sms = 0, per_sm = 0;
-  cudaError_t e =
-      launch_shape(reinterpret_cast<const void*>(kern), kThreads, 0, shape, &dev, &sms, &per_sm);
+  cudaError_t e = launch_shape(reinterpret_cast<const void*>(kern), kThreads, 0, shape[exact],
+                               &dev, &sms, &per_sm);
   if (e != cudaSuccess) return e;
   int64_t grid = int64_t(sms) * per_sm;
   if (grid > a.rows) grid = a.rows;
