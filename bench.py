@@ -683,7 +683,7 @@ def run_b200(args, world, rank, local):
                          "unit": "TFLOP/s", "frac": gemm_tops / int8_peak, "traffic": traffic,
                          "kernel": "gemm_tc_kernel<i8,256,pair>",
                          "peak_source": f"2 x {peaks['source']} dense bf16 ({peaks['bf16']} TF/s)"},
-            "prep": {"kernel": "quant_rows_kernel<bf16,int8,VPT=8>", "ms": prep_ms,
+            "prep": {"kernel": "quant_rows_kernel<bf16,int8,VPT=8,exact>", "ms": prep_ms,
                      "achieved_gbs": prep_gbs, "peak_gbs": peaks["hbm_gbs"],
                      "frac": prep_gbs / peaks["hbm_gbs"], "bytes": prep_bytes},
             "gemm_ms": gemm_ms,
