@@ -42,8 +42,11 @@ def ops():
 @pytest.mark.parametrize("mode", ["int8", "fp8"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("kind", ["normal", "zeros", "outliers", "rowzero"])
+# K = 2048 * 2^k (16-bit) and 1024 * 2^k (fp32) run the exact-fit quantize instances (every
+# thread's vectors in bounds, no guards); the others keep the per-vector bounds checks.
 @pytest.mark.parametrize("shape", [(7, 256), (3, 257), (1, 33), (9, 5376), (4, 16384), (5, 5384),
-                                   (3, 200), (2, 32768), (300, 1024)])
+                                   (3, 200), (2, 32768), (300, 1024), (6, 2048), (3, 4096),
+                                   (5, 8192)])
 def test_quantize_matches_reference_bit_exact(ops, mode, dtype, kind, shape):
     x = _x(*shape, dtype, kind)
     q, s = ops.quantize(x.to(DEV), mode)
