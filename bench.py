@@ -2,25 +2,30 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Workload (FFN-down at M=4096): A bf16 [4096, 16384] ~N(0,1)
-per GPU, W bf16 [4096, 16384] ~N(0, 0.02) quantized offline per output
-channel (symmetric INT8, amax/127).  One step = online per-token INT8
-quantization of A (row-prep kernel) + tcgen05 W8A8 GEMM with the fused
-(acc * sa) * sw -> bf16 epilogue.  Metric: 2*M*N*K / step time, in TOPS,
-summed over ranks (tokens are sharded: each rank owns its own M=4096 rows,
-weights replicated, no collective -> weak scaling).
+Workload (FFN-down at M=4096): A bf16 [4096, 16384] ~N(0,1),
+W bf16 [4096, 16384] ~N(0, 0.02) quantized offline per output channel
+(symmetric INT8, amax/127).  One step = online per-token INT8 quantization of
+A + the tcgen05 W8A8 GEMM with the fused (acc * sa) * sw -> bf16 epilogue.
+Tokens are sharded: with N GPUs each rank owns a contiguous block of the
+4096 rows (4096 / N), weights are replicated, no collective -- the same total
+work at every N (strong scaling).  Metric: 2*M*N*K / step time in TOPS for
+the whole job, the step time being the slowest rank's.
 
-Three independent (A, W) sets are rotated so that no step reuses an operand
-from L2 (A alone is 134 MB > 126 MB L2).  Timing: CUDA events on the launching
-stream, barrier + synchronize around the K timed steps, max over ranks.
-`e2e` repeats the step through the public API from pinned host memory: H2D of
-A, the two kernels, D2H of the bf16 output, every step.
+Each rank rotates independent operand sets (their total footprint is well
+above the 126 MB L2), so no step finds its operands in L2.  The W warm-up
+steps run eagerly; the K timed steps are captured once as a CUDA graph (two
+kernel launches and three timing events per step) and replayed, bracketed by
+a barrier and a device synchronize on both sides; times are CUDA events on
+the launching stream, max over ranks.  `e2e` repeats the step through the
+public C ABI (m5b_linear_ex) from pinned host memory: H2D of this rank's
+activations, the two kernels, D2H of the bf16 output, every step.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import sys
@@ -33,10 +38,17 @@ for _p in (ROOT, ROOT / "m5-max-kernels_b200"):
     if str(_p) not in sys.path:
         sys.path.insert(0, str(_p))
 
-M, K, N = 4096, 16384, 4096
-SETS = 3
+M, K, N = 4096, 16384, 4096  # global rows of the job, reduction width, output channels
+L2_BYTES = 126 * 2**20
 METRIC = "W8A8 proj TOPS incl. online quant @M=4096 (% INT8 peak); prep HBM GB/s"
 WORKLOAD = "ffn_down_w8a8_online_quant_M4096_K16384_N4096"
+
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# the GEMM kernel, from ncu captures of this workload's per-rank shapes
+# (rows per rank -> bytes).  Recorded constants, not measured by this script.
+GEMM_TRAFFIC_BYTES = {4096: 342205184}
+GEMM_TRAFFIC_SOURCE = ("ncu capture (--set full, 1 launch) of gemm_tc_kernel<i8,256,pair> on the "
+                       "per-rank shape; recorded constant")
 
 
 def _peaks():
@@ -52,11 +64,12 @@ def _peaks():
 
 
 class ClockSampler:
-    """SM clock / throttle-reason sampling while the timed region runs.
+    """SM clock / throttle-reason sampling while the timed regions run.
 
-    Polls NVML every ~5 ms from a thread (the same counters as the
+    Polls NVML about every millisecond from a thread (the same counters as the
     `nvidia-smi --query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.*`
-    line, but fast enough for a timed region of a few milliseconds).
+    line, but fast enough for a timed region of a few milliseconds).  Samples
+    are kept only while `active` is set, i.e. inside the timed regions.
     """
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
@@ -66,6 +79,7 @@ class ClockSampler:
         self.index = index
         self.samples = []
         self._stop = threading.Event()
+        self.active = threading.Event()
         self.thread = None
         self.nvml = None
         self.max_mhz = None
@@ -87,13 +101,15 @@ class ClockSampler:
     def _run(self):
         nv = self.nvml
         while not self._stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
-                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                self.samples.append((sm, reasons))
-            except Exception:
-                pass
-            time.sleep(0.001)
+            if self.active.is_set():
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                    reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                    if self.active.is_set():
+                        self.samples.append((sm, reasons))
+                except Exception:
+                    pass
+            time.sleep(0.0005)
 
     def __exit__(self, *exc):
         self._stop.set()
@@ -114,20 +130,8 @@ class ClockSampler:
                 if bits & mask:
                     seen.add(name)
         return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(seen), "samples": len(self.samples)}
-
-
-def _profiled_traffic():
-    """DRAM bytes per GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum)
-    from the committed ncu summary of this workload, or None."""
-    import re
-
-    p = ROOT / "profiles" / "gemm_tc_i8_ffn_down_m4096.md"
-    try:
-        m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", p.read_text(), re.M)
-        return int(m.group(1)) if m else None
-    except OSError:
-        return None
+                "reasons": sorted(seen), "samples": len(self.samples),
+                "window": "device-timed and e2e regions"}
 
 
 def _dist():
@@ -137,13 +141,61 @@ def _dist():
     return world, rank, local
 
 
-def cpu_reference(steps: int, warmup: int, target_s: float = 12.0):
-    """The reference's CPU path on a bounded sample of the workload.
+def _rows(share: int, rank: int) -> tuple[int, int]:
+    """This rank's contiguous [start, stop) block of the job's M rows."""
+    base, extra = divmod(M, share)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
 
-    Per step: per-token INT8 quantization of `rows` activation rows with the
-    restated numerics.quantize_reference (float32 NumPy), the decoded float64
-    BLAS product against the INT8 weight (src/m5kernels/engine.py:173-175 —
-    the reference's own CPU GEMM), scale epilogue and BF16 rounding.
+
+def _operand_sets(m_local: int) -> int:
+    """Operand sets a rank rotates through: at least 3, and together at least
+    three times the L2 size, so a step's operands were evicted by the others'."""
+    per_set = m_local * K * 2 + N * K + m_local * K + m_local * N * 2
+    return max(3, min(8, math.ceil(3 * L2_BYTES / per_set)))
+
+
+def _config(world: int) -> dict:
+    m_local = _rows(world, 0)[1] - _rows(world, 0)[0]
+    sets = _operand_sets(m_local)
+    return {"workload": WORKLOAD, "global_M": M, "M_per_gpu": m_local, "K": K, "N": N,
+            "parallelism": f"token-sharded x{world} (weights replicated, no collective)",
+            "l2": f"inputs larger than L2: {sets} rotating operand sets per rank"}
+
+
+def _thread_env() -> dict:
+    env = {k: os.environ.get(k, "unset") for k in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS",
+                                                   "MKL_NUM_THREADS")}
+    try:
+        from threadpoolctl import threadpool_info
+
+        env["blas"] = [{"api": d.get("internal_api"), "threads": d.get("num_threads")}
+                       for d in threadpool_info() if d.get("user_api") == "blas"]
+    except Exception:
+        pass
+    return env
+
+
+def _bf16_rows(rng, rows):
+    """rows x K activations ~N(0,1) rounded to bf16 values, as float32."""
+    import numpy as np
+
+    a = rng.standard_normal((rows, K), dtype=np.float32)
+    u = a.view(np.uint32)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def cpu_reference(steps: int, warmup: int, budget_s: float = 150.0):
+    """The reference's CPU path of the headline workload, timed on the host cores.
+
+    Per step: per-token INT8 quantization of the activation rows with the
+    restated numerics.quantize_reference (float32 NumPy, numerics.py:29-46),
+    the decoded float64 BLAS product against the INT8 weight
+    (src/m5kernels/engine.py:173-175 -- the reference's own CPU GEMM), the
+    scale epilogue and BF16 rounding.  Every timed step runs all M=4096 rows
+    of the job unless `steps` of them would exceed `budget_s`, in which case
+    each step runs a stated number of rows; the W warm-up steps run 64 rows.
     """
     import numpy as np
 
@@ -156,26 +208,58 @@ def cpu_reference(steps: int, warmup: int, target_s: float = 12.0):
     del w
 
     def one(rows):
-        a = rng.standard_normal((rows, K), dtype=np.float32)
+        a = _bf16_rows(rng, rows)
         t0 = time.perf_counter()
         q, s = ref.quantize_reference(a, "int8")
         y = (q.astype(np.float64) * s.astype(np.float64)[:, None]) @ wd.T
         ref.bf16_round_reference(y)
         return time.perf_counter() - t0
 
-    rows = 64
-    t = one(rows)
-    rows = int(max(16, min(M, rows * (target_s / max(steps, 1)) / max(t, 1e-3))))
-    for _ in range(max(warmup, 0)):
-        one(min(rows, 64))
-    times = [one(rows) for _ in range(max(steps, 1))]
+    for _ in range(max(warmup, 1)):
+        t64 = one(64)
+    est_full = t64 * M / 64
+    steps = max(steps, 1)
+    rows = M if steps * est_full <= budget_s else max(64, int(M * budget_s / (steps * est_full)))
+    times = [one(rows) for _ in range(steps)]
     per = statistics.median(times)
     tops = 2.0 * rows * N * K / per / 1e12
-    cores = os.cpu_count() or 1
-    return {"value": tops, "unit": "TOPS", "cores": cores, "kind": "port",
-            "sample": f"{rows} of {M} activation rows per step (FFN-down K={K}, N={N}); "
-                      f"NumPy float32 quantize_reference + float64 BLAS decoded GEMM",
-            "seconds_per_step": per}
+    return {"value": tops, "unit": "TOPS", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": (f"{rows} of {M} activation rows per timed step, {steps} timed steps "
+                       f"(median), {max(warmup, 1)} warm-up steps of 64 rows; FFN-down K={K}, "
+                       f"N={N}; NumPy float32 quantize_reference + float64 BLAS decoded GEMM"),
+            "rows_per_step": rows, "seconds_per_step": per, "steps_timed": steps,
+            "threads": _thread_env()}
+
+
+def cpu_omp_baseline(target_s: float = 8.0):
+    """The repository's multi-threaded C restatement (OpenMP, INT32 accumulation;
+    oracle/m5_cpu_omp.c) of the same step on the host cores: quantization of
+    bf16 rows and the W8A8 GEMM with the bf16 epilogue."""
+    import torch
+
+    from oracle import c_oracle as co
+
+    g = torch.Generator().manual_seed(0)
+    wq = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g)
+    ws = torch.rand(N, generator=g) * 1e-3
+    lib = co.omp_lib()
+    t0 = time.perf_counter()
+    co.omp_projection(torch.randn(64, K, generator=g).to(torch.bfloat16), wq, ws)
+    t64 = time.perf_counter() - t0
+    rows = int(min(M, max(64, 64 * (target_s / 3) / max(t64, 1e-4))) // 64 * 64)
+    x = torch.randn(rows, K, generator=g).to(torch.bfloat16)
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        co.omp_projection(x, wq, ws)
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times)
+    simd = {2: "AVX-512 VNNI", 1: "AVX2", 0: "plain C"}[int(lib.m5c_simd_level())]
+    return {"value": 2.0 * rows * N * K / per / 1e12, "unit": "TOPS",
+            "cores": int(lib.m5c_threads()), "kind": "port",
+            "sample": (f"{rows} of {M} rows per step, median of 3 steps; C restatement "
+                       f"(OpenMP, {simd} INT8 dot products, INT32 accumulation)"),
+            "threads": _thread_env()}
 
 
 def run_secondary(args, world, rank, local):
@@ -505,16 +589,19 @@ def run_colpar(args, world, rank, local):
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the reference's CPU path on rank 0 (other ranks exit)."""
     if rank != 0:
         return 0
     cb = cpu_reference(args.steps, args.warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "TOPS",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 2.0 * M * N * K / (cb["value"] * 1e12) * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N},
-        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "n_gpus": args.gpus, "steps": cb["steps_timed"], "warmup": args.warmup,
+        "ms_per_step": cb["seconds_per_step"] * 1e3,
+        "rows_per_step": cb["rows_per_step"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic", "config": _config(args.gpus),
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample",
+                                            "threads")},
         "e2e": {"value": cb["value"], "unit": "TOPS", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -523,10 +610,13 @@ def run_reference(args, world, rank):
 
 
 def run_b200(args, world, rank, local):
+    import ctypes
+
     import torch
     import torch.distributed as dist
 
     import m5kernels_b200 as m5
+    from m5kernels_b200 import _lib
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -539,162 +629,223 @@ def run_b200(args, world, rank, local):
         if world > 1:
             dist.barrier()
 
+    def max_over_ranks(v):
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # This rank's rows of the job.  --rank-share S (one GPU) runs rank 0's share
+    # of an S-GPU job: the per-rank step of that run, on this GPU alone.
+    share = world if world > 1 else max(1, args.rank_share)
+    r0, r1 = _rows(share, rank if world > 1 else 0)
+    m = r1 - r0
+    nsets = _operand_sets(m)
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    sets = []
-    for i in range(SETS):
-        a = torch.randn(M, K, device=dev, generator=gen, dtype=torch.float32).to(torch.bfloat16)
+    steps_sets = []
+    for _ in range(nsets):
+        a = torch.randn(m, K, device=dev, generator=gen, dtype=torch.float32).to(torch.bfloat16)
         w = (torch.randn(N, K, device=dev, generator=gen, dtype=torch.float32) * 0.02).to(torch.bfloat16)
         wq, ws = m5.quantize(w, "int8")  # offline weight preparation (untimed)
         del w
-        sets.append((a, wq, ws))
+        y = torch.empty((m, N), dtype=torch.bfloat16, device=dev)
+        steps_sets.append(m5.OnlineProjection(a, wq, ws, y, "int8"))
     torch.cuda.synchronize()
-
-    def step(i):
-        a, wq, ws = sets[i % SETS]
-        q, s = m5.quantize(a, "int8")
-        return m5.gemm(q, wq, "int8", a_scales=s, b_scales=ws, output_dtype=torch.bfloat16)
+    splitk = steps_sets[0].gemm_ws is not None
 
     for i in range(args.warmup):
-        step(i)
+        steps_sets[i % nsets]()
     torch.cuda.synchronize()
     barrier()
 
     stream = torch.cuda.current_stream(dev)
-    # Events around each kernel of every timed step: the per-kernel averages
-    # come from the same timed region as the headline number.
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    K_steps = args.steps
+    # The timed steps as one CUDA graph; external events between the kernels
+    # give each kernel's device time inside the same timed region.
+    kernel_timing = "CUDA events between the kernels inside the timed graph"
+    ev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+          for _ in range(K_steps)]
+    graph = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(graph):
+            for i in range(K_steps):
+                st = steps_sets[i % nsets]
+                ev[i][0].record()
+                st.quantize()
+                ev[i][1].record()
+                st.gemm()
+                ev[i][2].record()
+        in_graph_events = True
+    except Exception:  # no event nodes: per-kernel times from graphs of one kernel each
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(K_steps):
+                steps_sets[i % nsets]()
+        in_graph_events = False
+        kernel_timing = "separate CUDA-graph replays of each kernel (no in-graph events)"
+    graph.replay()  # untimed first replay (graph upload)
+    torch.cuda.synchronize()
+    barrier()
 
-    def timed_step(i):
-        a, wq, ws = sets[i % SETS]
-        ev[i][0].record(stream)
-        q, s = m5.quantize(a, "int8")
-        ev[i][1].record(stream)
-        m5.gemm(q, wq, "int8", a_scales=s, b_scales=ws, output_dtype=torch.bfloat16)
-        ev[i][2].record(stream)
-
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         barrier()
         torch.cuda.synchronize()
-        for i in range(args.steps):
-            timed_step(i)
+        clocks.active.set()
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        clocks.active.clear()
+        barrier()
+        ms_total = e0.elapsed_time(e1)
+        if in_graph_events:
+            prep_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / K_steps
+            gemm_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / K_steps
+        else:
+            def one_kernel_ms(fn):
+                g1 = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g1):
+                    for i in range(K_steps):
+                        fn(steps_sets[i % nsets])
+                g1.replay()
+                torch.cuda.synchronize()
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                g1.replay()
+                a1.record(stream)
+                torch.cuda.synchronize()
+                return a0.elapsed_time(a1) / K_steps
+            prep_ms = one_kernel_ms(lambda st: st.quantize())
+            gemm_ms = one_kernel_ms(lambda st: st.gemm())
+        del graph
+        ms_per_step = max_over_ranks(ms_total / K_steps)
+        prep_ms_max = max_over_ranks(prep_ms)
+        gemm_ms_max = max_over_ranks(gemm_ms)
+        ops_job = 2.0 * M * N * K
+        ops_rank = 2.0 * m * N * K
+        # the whole job over the slowest rank (one GPU: the job, or with
+        # --rank-share only this GPU's share of it)
+        value = (ops_job if world > 1 else ops_rank) / (ms_per_step * 1e-3) / 1e12
+
+        if args.profile:
+            if rank == 0:
+                print(json.dumps({"profile": True, "ms_per_step": ms_per_step, "gemm_ms": gemm_ms,
+                                  "prep_ms": prep_ms, "rows_per_rank": m, "splitk": splitk}),
+                      flush=True)
+            if world > 1:
+                dist.destroy_process_group()
+            return 0
+
+        # End to end through the public C ABI (one m5b_linear_ex call per step:
+        # online quantize -> GEMM) from pinned host memory: every step copies
+        # this rank's activations host -> device and its output device -> host
+        # inside the timed region.  Copies run on their own streams so that step
+        # i's host -> device copy, step i-1's compute and step i-2's
+        # device -> host copy overlap (the link is full duplex); device buffers
+        # are double-buffered and events order every reuse.
+        host_a = [steps_sets[i].x.to("cpu").pin_memory() for i in range(nsets)]
+        host_out = [torch.empty((m, N), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        dev_a = [torch.empty((m, K), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        dev_y = [torch.empty((m, N), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        h2d_stream = torch.cuda.Stream(dev)
+        d2h_stream = torch.cuda.Stream(dev)
+        lib = _lib.lib()
+        ws_bytes = int(lib.m5b_linear_workspace_bytes(m, K))
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        gws_bytes = int(lib.m5b_gemm_workspace_bytes(m, N, K, _lib.MODE["int8"]))
+        gemm_ws = torch.zeros(max(gws_bytes, 1), dtype=torch.uint8, device=dev)
+
+        def linear_into(x, wq, wsc, y):
+            _lib.check(lib.m5b_linear_ex(
+                ctypes.c_void_p(x.data_ptr()), _lib.BF16, m, K, 0, None,
+                ctypes.c_void_p(wq.data_ptr()), ctypes.c_void_p(wsc.data_ptr()), N,
+                _lib.MODE["int8"], ctypes.c_void_p(y.data_ptr()), _lib.BF16,
+                ctypes.c_void_p(workspace.data_ptr()), ws_bytes,
+                ctypes.c_void_p(gemm_ws.data_ptr()) if gws_bytes else None, gws_bytes,
+                ctypes.c_void_p(stream.cuda_stream)))
+
+        def run_e2e(n):
+            h2d_done = [torch.cuda.Event() for _ in range(n)]
+            comp_done = [torch.cuda.Event() for _ in range(n)]
+            d2h_done = [torch.cuda.Event() for _ in range(n)]
+            for i in range(n):
+                b = i % 2
+                with torch.cuda.stream(h2d_stream):
+                    if i >= 2:
+                        h2d_stream.wait_event(comp_done[i - 2])  # dev_a[b] consumed
+                    dev_a[b].copy_(host_a[i % nsets], non_blocking=True)
+                    h2d_done[i].record(h2d_stream)
+                stream.wait_event(h2d_done[i])
+                if i >= 2:
+                    stream.wait_event(d2h_done[i - 2])  # dev_y[b] copied out
+                st = steps_sets[i % nsets]
+                linear_into(dev_a[b], st.wq, st.w_scales, dev_y[b])
+                comp_done[i].record(stream)
+                with torch.cuda.stream(d2h_stream):
+                    d2h_stream.wait_event(comp_done[i])
+                    host_out[b].copy_(dev_y[b], non_blocking=True)
+                    d2h_done[i].record(d2h_stream)
+            stream.wait_event(d2h_done[n - 1])  # the timed region ends after the last copy
+
+        run_e2e(min(args.warmup, 3))
         torch.cuda.synchronize()
         barrier()
-    ms_total = ev[0][0].elapsed_time(ev[-1][2])
-    prep_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
-    gemm_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
-    ms = torch.tensor([ms_total / args.steps], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms_per_step = float(ms.item())
-    ops_per_rank = 2.0 * M * N * K
-    value = world * ops_per_rank / (ms_per_step * 1e-3) / 1e12
-
-    if args.profile:
-        if rank == 0:
-            print(json.dumps({"profile": True, "ms_per_step": ms_per_step, "gemm_ms": gemm_ms,
-                              "prep_ms": prep_ms}), flush=True)
-        if world > 1:
-            dist.destroy_process_group()
-        return 0
-
-    # End to end through the public API (one m5b_linear call per step: online
-    # quantize -> GEMM) from pinned host memory: every step copies its
-    # activations host -> device and its output device -> host inside the
-    # timed region.  Copies run on their own streams so that step i's
-    # host -> device copy, step i-1's compute and step i-2's device -> host copy
-    # overlap (the link is full duplex); device buffers are double-buffered and
-    # events order every reuse.
-    host_a = [sets[i][0].to("cpu").pin_memory() for i in range(SETS)]
-    host_out = [torch.empty((M, N), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    dev_a = [torch.empty((M, K), dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    dev_y = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    h2d_stream = torch.cuda.Stream(dev)
-    d2h_stream = torch.cuda.Stream(dev)
-    lib = m5._lib.lib()
-    ws_bytes = int(lib.m5b_linear_workspace_bytes(M, K))
-    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    import ctypes
-
-    def linear_into(x, wq, wsc, y):
-        m5._lib.check(lib.m5b_linear(
-            ctypes.c_void_p(x.data_ptr()), m5._lib.BF16, M, K, 0, None,
-            ctypes.c_void_p(wq.data_ptr()), ctypes.c_void_p(wsc.data_ptr()), N,
-            m5._lib.MODE["int8"], ctypes.c_void_p(y.data_ptr()), m5._lib.BF16,
-            ctypes.c_void_p(workspace.data_ptr()), ws_bytes, ctypes.c_void_p(stream.cuda_stream)))
-
-    def run_e2e(n):
-        h2d_done = [torch.cuda.Event() for _ in range(n)]
-        comp_done = [torch.cuda.Event() for _ in range(n)]
-        d2h_done = [torch.cuda.Event() for _ in range(n)]
-        for i in range(n):
-            b = i % 2
-            with torch.cuda.stream(h2d_stream):
-                if i >= 2:
-                    h2d_stream.wait_event(comp_done[i - 2])  # dev_a[b] consumed
-                dev_a[b].copy_(host_a[i % SETS], non_blocking=True)
-                h2d_done[i].record(h2d_stream)
-            stream.wait_event(h2d_done[i])
-            if i >= 2:
-                stream.wait_event(d2h_done[i - 2])  # dev_y[b] copied out
-            _, wq, wsc = sets[i % SETS]
-            linear_into(dev_a[b], wq, wsc, dev_y[b])
-            comp_done[i].record(stream)
-            with torch.cuda.stream(d2h_stream):
-                d2h_stream.wait_event(comp_done[i])
-                host_out[b].copy_(dev_y[b], non_blocking=True)
-                d2h_done[i].record(d2h_stream)
-        stream.wait_event(d2h_done[n - 1])  # the timed region ends after the last copy
-
-    run_e2e(min(args.warmup, 3))
-    torch.cuda.synchronize()
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e2e_steps = max(3, min(args.steps, 10))
-    e0.record(stream)
-    h2d_stream.wait_event(e0)
-    run_e2e(e2e_steps)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = world * ops_per_rank / (float(e2e_ms.item()) * 1e-3) / 1e12
+        e2e_steps = max(3, min(args.steps, 10))
+        torch.cuda.synchronize()
+        clocks.active.set()
+        e0.record(stream)
+        h2d_stream.wait_event(e0)
+        run_e2e(e2e_steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        clocks.active.clear()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    e2e_value = (ops_job if world > 1 else ops_rank) / (e2e_ms * 1e-3) / 1e12
 
     peaks = _peaks()
     int8_peak = 2.0 * peaks["bf16"]  # dense INT8 = 2x dense BF16 on B200 (4.5 / 2.25 PF nominal)
-    gemm_tops = ops_per_rank / (gemm_ms * 1e-3) / 1e12
-    prep_bytes = M * (3 * K + 4)
-    prep_gbs = prep_bytes / (prep_ms * 1e-3) / 1e9
-    traffic = _profiled_traffic()
+    gemm_tops = ops_rank / (gemm_ms_max * 1e-3) / 1e12
+    prep_bytes = m * (3 * K + 4)
+    prep_gbs = prep_bytes / (prep_ms_max * 1e-3) / 1e9
     out = None
     if rank == 0:
-        cb = cpu_reference(1, 0, target_s=10.0) if world == 1 else None
+        cb = cpu_reference(1, 1, budget_s=12.0) if world == 1 and share == 1 else None
+        omp = cpu_omp_baseline() if world == 1 and share == 1 else None
         clock = clocks.summary()
+        kernel = "gemm_tc_kernel<i8,256,pair>" + (" split-K" if splitk else "")
         out = {
             "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "M_per_gpu": M, "K": K, "N": N,
-                       "global_M": M * world, "parallelism": f"token-sharded x{world}",
-                       "l2": f"inputs larger than L2; {SETS} rotating operand sets"},
+            "config": _config(share),
             "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
-                         "unit": "TFLOP/s", "frac": gemm_tops / int8_peak, "traffic": traffic,
-                         "kernel": "gemm_tc_kernel<i8,256,pair>",
-                         "peak_source": f"2 x {peaks['source']} dense bf16 ({peaks['bf16']} TF/s)"},
-            "prep": {"kernel": "quant_rows_kernel<bf16,int8,VPT=8,exact>", "ms": prep_ms,
+                         "unit": "TFLOP/s", "frac": gemm_tops / int8_peak,
+                         "traffic": GEMM_TRAFFIC_BYTES.get(m),
+                         "traffic_source": GEMM_TRAFFIC_SOURCE if m in GEMM_TRAFFIC_BYTES else None,
+                         "kernel": kernel,
+                         "peak_source": (f"2 x {peaks['source']} dense bf16 ({peaks['bf16']} TF/s); "
+                                         "nominal dense INT8 4500 TOPS"),
+                         "frac_of_nominal_int8": gemm_tops / 4500.0},
+            "prep": {"kernel": "quant_rows_kernel<bf16,int8,VPT=8,exact>", "ms": prep_ms_max,
                      "achieved_gbs": prep_gbs, "peak_gbs": peaks["hbm_gbs"],
                      "frac": prep_gbs / peaks["hbm_gbs"], "bytes": prep_bytes},
-            "gemm_ms": gemm_ms,
-            "pct_int8_peak_incl_quant": value / world / int8_peak,
-            "cpu_baseline": ({k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
-                             if cb else None),
-            "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": M * K * 2,
-                    "d2h_bytes_per_step": M * N * 2},
+            "gemm_ms": gemm_ms_max, "rows_per_rank": m, "kernel_timing": kernel_timing,
+            "pct_int8_peak_incl_quant": (ops_rank / (ms_per_step * 1e-3) / 1e12) / int8_peak,
+            "cpu_baseline": ({k: cb[k] for k in ("value", "unit", "cores", "kind", "sample",
+                                                 "threads")} if cb else None),
+            "cpu_baseline_omp": omp,
+            "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": m * K * 2,
+                    "d2h_bytes_per_step": m * N * 2, "api": "m5b_linear_ex"},
             "clocks": clock,
             "gpu_launches": 2 * args.steps,
         }
+        if world == 1 and share > 1:
+            out["rank_share"] = {"of_gpus": share, "note": "rank 0's rows of a " + str(share) +
+                                 "-GPU job timed alone on this GPU; value is this GPU's share",
+                                 "projected_job_tops": value * share}
         print(json.dumps(out), flush=True)
     if world > 1:
         barrier()
@@ -713,6 +864,8 @@ def main(argv=None):
                     help="ffn_down is the headline; the others time one other BASELINE config")
     ap.add_argument("--profile", action="store_true",
                     help="profiling run: timed steps and per-kernel timing only (no e2e, no CPU leg)")
+    ap.add_argument("--rank-share", type=int, default=1,
+                    help="(one GPU) time rank 0's rows of an N-GPU job on this GPU alone")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

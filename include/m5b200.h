@@ -68,7 +68,8 @@ M5B_API int m5b_version(void);
 M5B_API const char* m5b_last_error(void);
 
 /* Device status word of the current device: bit 0 producer wait, bit 1 MMA
- * wait, bit 2 epilogue wait, bit 3 drain wait gave up.  Synchronizes the
+ * wait, bit 2 epilogue wait, bit 3 drain wait, bit 4 split-K partial-sum
+ * wait gave up.  Synchronizes the
  * device.  If clear != 0 the word is reset to zero afterwards. */
 M5B_API int m5b_device_status(unsigned int* status_out, int clear);
 
@@ -76,7 +77,7 @@ M5B_API int m5b_device_status(unsigned int* status_out, int clear);
  * mode INT8: q int8, scale = amax/127, q = clip(rint(x/scale), +-127).
  * mode FP8 : q = E4M3 bits (RNE, saturating), scale = amax/448.
  * All-zero rows get scale 1.
- * Replaces src/m5kernels/metal.py:106-123 (quantize) with the arithmetic of
+ * Replaces src/m5kernels/metal.py:27-44 (quantize) with the arithmetic of
  * src/m5kernels/numerics.py:29-46 (quantize_reference). */
 M5B_API int m5b_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int mode, void* q,
                  float* scales, void* stream);
@@ -183,12 +184,37 @@ M5B_API int m5b_qk_norm_rope(const void* projected, int64_t m, int64_t n, const 
  *       gate [n] or [gate_rows, n] with gate_row_map.
  *   out_dtype: M5B_BF16, M5B_F16 or M5B_F32; M5B_I32 (INT8 mode, no scales,
  *       bias or gate) stores the raw INT32 accumulators.
- * Replaces src/m5kernels/metal.py:237-348 (gemm). */
+ * Replaces src/m5kernels/metal.py:158-269 (gemm). */
 M5B_API int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
              const float* a_scales, const float* b_scales, void* out, int out_dtype,
              const float* bias, const int32_t* bias_row_map, int64_t bias_rows,
              const void* residual, const void* gate, const int32_t* gate_row_map,
              int64_t gate_rows, void* stream);
+
+/* Workspace bytes that let m5b_gemm_ex (and m5b_linear_ex,
+ * m5b_projection_qk_rope_ex) run an m x n x k GEMM of `mode` on the current
+ * device with the split-K schedule, or 0 when that shape keeps the
+ * data-parallel schedule.  Split-K is taken by INT8 GEMMs whose 256 x 256
+ * tiles would fill at most a quarter of the GPU's CTA pairs (very few rows
+ * and columns): every tile runs on S >= 2 CTA pairs over equal K ranges, and
+ * the last of them to finish adds the others' INT32 partial sums (exact) --
+ * outputs are bit-identical to the data-parallel schedule.
+ * The size depends only on the device's SM count (about 0.25 MB per CTA
+ * pair). */
+M5B_API int64_t m5b_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int mode);
+
+/* m5b_gemm with a workspace for the split-K schedule (NULL / 0: data-
+ * parallel only, exactly m5b_gemm).  The workspace must be 256-byte aligned
+ * and all zero before its first use (cudaMemset once after allocating it);
+ * every call leaves it zeroed again.  Calls that overlap on the GPU must not
+ * share a workspace.  After a nonzero m5b_device_status (a timed-out wait)
+ * zero it again.  Same replacement as m5b_gemm. */
+M5B_API int m5b_gemm_ex(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
+                        const float* a_scales, const float* b_scales, void* out, int out_dtype,
+                        const float* bias, const int32_t* bias_row_map, int64_t bias_rows,
+                        const void* residual, const void* gate, const int32_t* gate_row_map,
+                        int64_t gate_rows, void* workspace, int64_t workspace_bytes,
+                        void* stream);
 
 /* Column-parallel projection with the all-gather fused into the epilogue.
  * This rank holds n output channels of W (b [n, k], b_scales [n]); its
@@ -202,7 +228,7 @@ M5B_API int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t
  * n % 32 == 0, col_offset % 32 == 0, n_total % 8 == 0, n_peers <= 7.
  * Replaces the optional column-parallel FFN-up variant's GEMM +
  * all_gather_into_tensor (the reference itself is
- * single-GPU: metal.py:237-348 per rank). */
+ * single-GPU: metal.py:158-269 per rank). */
 M5B_API int m5b_gemm_allgather(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
                                int mode, const float* a_scales, const float* b_scales, void* out,
                                int64_t n_total, int64_t col_offset, void* const* peer_outs,
@@ -236,6 +262,16 @@ M5B_API int m5b_linear(const void* x, int x_dtype, int64_t m, int64_t k, int blo
                        int mode, void* out, int out_dtype, void* workspace,
                        int64_t workspace_bytes, void* stream);
 
+/* m5b_linear whose GEMM may take the split-K schedule: gemm_workspace
+ * (m5b_gemm_workspace_bytes(m, n, k, mode) bytes, separate from the codes /
+ * scales workspace) follows the rules of m5b_gemm_ex's workspace.  Same
+ * replacement as m5b_linear. */
+M5B_API int m5b_linear_ex(const void* x, int x_dtype, int64_t m, int64_t k, int block_size,
+                          const int8_t* signs, const void* wq, const float* w_scales, int64_t n,
+                          int mode, void* out, int out_dtype, void* workspace,
+                          int64_t workspace_bytes, void* gemm_workspace,
+                          int64_t gemm_workspace_bytes, void* stream);
+
 /* m5b_linear for callers that cannot allocate device memory (a host whose
  * device memory is already committed to its own pool, a plugin host that
  * forbids extension allocations, a hot path that must not take cudaMalloc's
@@ -245,7 +281,9 @@ M5B_API int m5b_linear(const void* x, int x_dtype, int64_t m, int64_t k, int blo
  * m * k <= 67,108,864 and m <= 16,384 (else M5B_EINVAL).  Calls share that
  * array: calls whose kernels overlap on the GPU race and must be ordered.
  * The first call on a device looks the array's address up (make it before
- * any stream capture).  Allocates nothing.  No counterpart in the reference. */
+ * any stream capture); the address is tied to the device's CUDA context, and
+ * the first call after a cudaDeviceReset looks it up again (also before any
+ * capture).  Allocates nothing.  No counterpart in the reference. */
 M5B_API int m5b_linear_noalloc(const void* x, int x_dtype, int64_t m, int64_t k, int block_size,
                                const int8_t* signs, const void* wq, const float* w_scales,
                                int64_t n, int mode, void* out, int out_dtype, void* stream);
@@ -261,6 +299,17 @@ M5B_API int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int6
                            int mode, const float* a_scales, const float* b_scales,
                            const void* gamma, const void* cos, const void* sin, int rope_half,
                            float epsilon, void* out, void* stream);
+
+/* m5b_projection_qk_rope with a workspace for the split-K schedule of its
+ * INT8 GEMM (m5b_gemm_workspace_bytes(m, n, k, mode) bytes; rules as for
+ * m5b_gemm_ex).  The finishing CTA pair of a split tile adds the INT32
+ * partial sums before the BF16 projection, so RMS and RoPE see the same
+ * values as without the split.  Same replacement as m5b_projection_qk_rope. */
+M5B_API int m5b_projection_qk_rope_ex(const void* a, const void* b, int64_t m, int64_t n,
+                                      int64_t k, int mode, const float* a_scales,
+                                      const float* b_scales, const void* gamma, const void* cos,
+                                      const void* sin, int rope_half, float epsilon, void* out,
+                                      void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Grouped Q/K/V projection: b is [heads, 3, 128, k] (rows in [head, stream,
  * channel] order, streams Q, K, V), b_scales [heads * 384].  One GEMM; per

@@ -534,10 +534,30 @@ static int output_map(CUtensorMap* map, void* out, int out_dtype, int64_t m, int
   return M5B_OK;
 }
 
+// Split-K factor of a CTA-pair GEMM with `tiles` 256 x 256 tiles of nkb
+// k-blocks on `slots` CTA pairs, or 0 for the data-parallel schedule.  An
+// INT8 GEMM whose tiles fill at most a quarter of the pairs (even as N-halves
+// they would leave half of the GPU idle) runs every tile as S >= 2 pairs over
+// equal K ranges, up to S = 4; INT32 partial sums add exactly, so the result
+// is the data-parallel one bit for bit.  Larger GEMMs keep the data-parallel
+// schedule with its N-halves: at 32 tiles on 74 pairs (512 rows of FFN-down)
+// two pairs per full tile measured 39.0 us against 35.7 us for one pair per
+// N-half.  M5B_GEMM_SPLITK=0 turns it off (tuning and tests).
+static int splitk_factor(int tiles, int nkb, int slots) {
+  if (tiles <= 0 || 4 * tiles > slots) return 0;
+  if (const char* force = std::getenv("M5B_GEMM_SPLITK"))
+    if (force[0] == '0') return 0;
+  int s = slots / tiles;
+  if (s > kSplitKMaxSplits) s = kSplitKMaxSplits;
+  while (s >= 2 && nkb / s < kSplitKMinBlocks) --s;
+  return s >= 2 ? s : 0;
+}
+
 static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
                        GemmArgs& g, int bn, bool pair, void* stream,
                        const CUtensorMap* to = nullptr, const CUtensorMap* to_k = nullptr,
-                       const CUtensorMap* to_v = nullptr) {
+                       const CUtensorMap* to_v = nullptr, void* sk_ws = nullptr,
+                       int64_t sk_ws_bytes = 0) {
   unsigned int* status = nullptr;
   int sms = 0;
   int rc = device_state(&status, &sms);
@@ -548,12 +568,30 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   const int slots = pair ? sms / 2 : sms;  // persistent CTAs (pairs)
   g.num_full = tiles;
   g.num_units = tiles;
+  g.sk = 0;
   const int rem = tiles % slots;
   if (pair && tiles > slots && rem > 0 && 2 * rem <= slots) {
     g.num_full = tiles - rem;
     g.num_units = g.num_full + 2 * rem;
+  } else if (pair && 2 * tiles <= slots) {  // under half a wave: every tile as two N-halves
+    g.num_full = 0;
+    g.num_units = 2 * tiles;
   }
-  const int grid = (g.num_units < slots ? g.num_units : slots) * (pair ? 2 : 1);
+  int grid = (g.num_units < slots ? g.num_units : slots) * (pair ? 2 : 1);
+  if (pair && bn == 256 && g.kind == KIND_I8 && sk_ws &&
+      sk_ws_bytes >= splitk_workspace_bytes(slots) && aligned(sk_ws, 256)) {
+    const int splits = splitk_factor(tiles, g.num_k_blocks, slots);
+    if (splits > 0) {
+      g.sk = 1;
+      g.sk_splits = splits;
+      g.sk_tiles = tiles;
+      g.sk_part = static_cast<uint4*>(sk_ws);
+      g.sk_ctr = reinterpret_cast<int*>(static_cast<uint8_t*>(sk_ws) + splitk_part_bytes(slots));
+      g.num_full = tiles;
+      g.num_units = tiles;
+      grid = 2 * tiles * splits;
+    }
+  }
   const CUtensorMap& o = to ? *to : tbh;
   cudaError_t e = launch_gemm(ta, tb, tbh, o, to_k ? *to_k : o, to_v ? *to_v : o, g, bn, grid,
                               pair, static_cast<cudaStream_t>(stream));
@@ -561,11 +599,29 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   return ok();
 }
 
-int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
-             const float* a_scales, const float* b_scales, void* out, int out_dtype,
-             const float* bias, const int32_t* bias_row_map, int64_t bias_rows,
-             const void* residual, const void* gate, const int32_t* gate_row_map,
-             int64_t gate_rows, void* stream) {
+int64_t m5b_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int mode) {
+  if (mode != M5B_MODE_INT8 || m <= 0 || n <= 0 || k <= 0 || !use_pair(EPI_PLAIN, m, n))
+    return 0;
+  if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return 0;
+  int sms = 0;
+  unsigned int* status = nullptr;
+  if (device_state(&status, &sms) != M5B_OK || sms < 4) return 0;
+  const int64_t tiles = ((m + 255) / 256) * ((n + 255) / 256);
+  if (tiles > 0x7fffffffLL) return 0;
+  const int splits =
+      splitk_factor(static_cast<int>(tiles), static_cast<int>((k + 127) / 128), sms / 2);
+  return splits > 0 ? splitk_workspace_bytes(sms / 2) : 0;
+}
+
+static int gemm_impl(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
+                     const float* a_scales, const float* b_scales, void* out, int out_dtype,
+                     const float* bias, const int32_t* bias_row_map, int64_t bias_rows,
+                     const void* residual, const void* gate, const int32_t* gate_row_map,
+                     int64_t gate_rows, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (workspace_bytes < 0 || (workspace_bytes > 0 && !workspace))
+    return fail(M5B_EINVAL, "workspace pointer is NULL");
+  if (workspace && !aligned(workspace, 256))
+    return fail(M5B_EINVAL, "workspace must be 256-byte aligned");
   GemmArgs g{};
   g.epi = EPI_PLAIN;
   g.N = static_cast<int>(n);
@@ -583,7 +639,8 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
     if (!out) return fail(M5B_EINVAL, "output pointer is NULL");
     g.out = out;
     g.out_dtype = DT_I32;
-    return gemm_launch(ta, tb, tbh, g, bn, pair, stream);
+    return gemm_launch(ta, tb, tbh, g, bn, pair, stream, nullptr, nullptr, nullptr, workspace,
+                       workspace_bytes);
   }
   const bool quant = (mode == M5B_MODE_INT8 || mode == M5B_MODE_FP8);
   if (quant && (!a_scales || !b_scales)) return fail(M5B_EINVAL, "scales required");
@@ -630,9 +687,30 @@ int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int 
     if (rc) return rc;
     g.tma_store = 1;
     g.ldo = n;
-    return gemm_launch(ta, tb, tbh, g, bn, pair, stream, &to);
+    return gemm_launch(ta, tb, tbh, g, bn, pair, stream, &to, nullptr, nullptr, workspace,
+                       workspace_bytes);
   }
-  return gemm_launch(ta, tb, tbh, g, bn, pair, stream);
+  return gemm_launch(ta, tb, tbh, g, bn, pair, stream, nullptr, nullptr, nullptr, workspace,
+                     workspace_bytes);
+}
+
+int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
+             const float* a_scales, const float* b_scales, void* out, int out_dtype,
+             const float* bias, const int32_t* bias_row_map, int64_t bias_rows,
+             const void* residual, const void* gate, const int32_t* gate_row_map,
+             int64_t gate_rows, void* stream) {
+  return gemm_impl(a, b, m, n, k, mode, a_scales, b_scales, out, out_dtype, bias, bias_row_map,
+                   bias_rows, residual, gate, gate_row_map, gate_rows, nullptr, 0, stream);
+}
+
+int m5b_gemm_ex(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
+                const float* a_scales, const float* b_scales, void* out, int out_dtype,
+                const float* bias, const int32_t* bias_row_map, int64_t bias_rows,
+                const void* residual, const void* gate, const int32_t* gate_row_map,
+                int64_t gate_rows, void* workspace, int64_t workspace_bytes, void* stream) {
+  return gemm_impl(a, b, m, n, k, mode, a_scales, b_scales, out, out_dtype, bias, bias_row_map,
+                   bias_rows, residual, gate, gate_row_map, gate_rows, workspace, workspace_bytes,
+                   stream);
 }
 
 int m5b_gemm_allgather(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
@@ -747,7 +825,11 @@ static int qk_projection(const void* a, const void* b, int64_t m, int64_t n, int
                          const float* a_scales, const float* b_scales, const void* gamma,
                          const void* gamma_k, const void* cos, const void* sin, int rope_half,
                          float epsilon, void* out, void* out_k, void* out_v, bool grouped,
-                         void* stream) {
+                         void* workspace, int64_t workspace_bytes, void* stream) {
+  if (workspace_bytes < 0 || (workspace_bytes > 0 && !workspace))
+    return fail(M5B_EINVAL, "workspace pointer is NULL");
+  if (workspace && !aligned(workspace, 256))
+    return fail(M5B_EINVAL, "workspace must be 256-byte aligned");
   if (mode != M5B_MODE_INT8 && mode != M5B_MODE_BF16)
     return fail(M5B_EUNSUPPORTED, "Q/K projection fusion supports INT8 or BF16 only");
   if (m <= 0 || n <= 0 || n % 128)
@@ -802,7 +884,7 @@ static int qk_projection(const void* a, const void* b, int64_t m, int64_t n, int
     if (rc) return rc;
   }
   return gemm_launch(ta, tb, tbh, g, bn, pair, stream, &to, grouped ? &to_k : nullptr,
-                     grouped ? &to_v : nullptr);
+                     grouped ? &to_v : nullptr, workspace, workspace_bytes);
 }
 
 int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
@@ -810,7 +892,17 @@ int m5b_projection_qk_rope(const void* a, const void* b, int64_t m, int64_t n, i
                            const void* gamma, const void* cos, const void* sin, int rope_half,
                            float epsilon, void* out, void* stream) {
   return qk_projection(a, b, m, n, k, mode, a_scales, b_scales, gamma, nullptr, cos, sin,
-                       rope_half, epsilon, out, nullptr, nullptr, false, stream);
+                       rope_half, epsilon, out, nullptr, nullptr, false, nullptr, 0, stream);
+}
+
+int m5b_projection_qk_rope_ex(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
+                              int mode, const float* a_scales, const float* b_scales,
+                              const void* gamma, const void* cos, const void* sin, int rope_half,
+                              float epsilon, void* out, void* workspace, int64_t workspace_bytes,
+                              void* stream) {
+  return qk_projection(a, b, m, n, k, mode, a_scales, b_scales, gamma, nullptr, cos, sin,
+                       rope_half, epsilon, out, nullptr, nullptr, false, workspace,
+                       workspace_bytes, stream);
 }
 
 int m5b_projection_qkv_rope(const void* a, const void* b, int64_t m, int64_t heads, int64_t k,
@@ -821,7 +913,7 @@ int m5b_projection_qkv_rope(const void* a, const void* b, int64_t m, int64_t hea
   if (heads <= 0 || heads > (int64_t(1) << 20))
     return fail(M5B_EINVAL, "heads must be a positive count of 128-wide heads");
   return qk_projection(a, b, m, heads * 384, k, mode, a_scales, b_scales, gamma_q, gamma_k, cos,
-                       sin, rope_half, epsilon, q_out, k_out, v_out, true, stream);
+                       sin, rope_half, epsilon, q_out, k_out, v_out, true, nullptr, 0, stream);
 }
 
 int64_t m5b_linear_workspace_bytes(int64_t m, int64_t k) {
@@ -830,9 +922,12 @@ int64_t m5b_linear_workspace_bytes(int64_t m, int64_t k) {
   return codes + m * int64_t(sizeof(float));
 }
 
-int m5b_linear(const void* x, int x_dtype, int64_t m, int64_t k, int block_size,
-               const int8_t* signs, const void* wq, const float* w_scales, int64_t n, int mode,
-               void* out, int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+
+static int linear_impl(const void* x, int x_dtype, int64_t m, int64_t k, int block_size,
+                       const int8_t* signs, const void* wq, const float* w_scales, int64_t n,
+                       int mode, void* out, int out_dtype, void* workspace,
+                       int64_t workspace_bytes, void* gemm_workspace,
+                       int64_t gemm_workspace_bytes, void* stream) {
   if (mode != M5B_MODE_INT8 && mode != M5B_MODE_FP8)
     return fail(M5B_EUNSUPPORTED, "the online projection supports int8 and fp8 (E4M3)");
   if (m <= 0 || k <= 0 || n <= 0) return fail(M5B_EINVAL, "A and B must be nonempty matrices");
@@ -849,8 +944,23 @@ int m5b_linear(const void* x, int x_dtype, int64_t m, int64_t k, int block_size,
                                        stream)
                : m5b_quantize(x, x_dtype, m, k, mode, codes, scales, stream);
   if (rc) return rc;
-  return m5b_gemm(codes, wq, m, n, k, mode, scales, w_scales, out, out_dtype, nullptr, nullptr, 0,
-                  nullptr, nullptr, nullptr, 0, stream);
+  return gemm_impl(codes, wq, m, n, k, mode, scales, w_scales, out, out_dtype, nullptr, nullptr, 0,
+                   nullptr, nullptr, nullptr, 0, gemm_workspace, gemm_workspace_bytes, stream);
+}
+
+int m5b_linear(const void* x, int x_dtype, int64_t m, int64_t k, int block_size,
+               const int8_t* signs, const void* wq, const float* w_scales, int64_t n, int mode,
+               void* out, int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+  return linear_impl(x, x_dtype, m, k, block_size, signs, wq, w_scales, n, mode, out, out_dtype,
+                     workspace, workspace_bytes, nullptr, 0, stream);
+}
+
+int m5b_linear_ex(const void* x, int x_dtype, int64_t m, int64_t k, int block_size,
+                  const int8_t* signs, const void* wq, const float* w_scales, int64_t n, int mode,
+                  void* out, int out_dtype, void* workspace, int64_t workspace_bytes,
+                  void* gemm_workspace, int64_t gemm_workspace_bytes, void* stream) {
+  return linear_impl(x, x_dtype, m, k, block_size, signs, wq, w_scales, n, mode, out, out_dtype,
+                     workspace, workspace_bytes, gemm_workspace, gemm_workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -229,6 +229,7 @@ enum DeviceError : unsigned int {
   DEV_TIMEOUT_MMA = 1u << 1,
   DEV_TIMEOUT_EPILOGUE = 1u << 2,
   DEV_TIMEOUT_DRAIN = 1u << 3,
+  DEV_TIMEOUT_FIXUP = 1u << 4,  // split-K: the other pairs' partial stores did not finish
 };
 
 // Wall-clock limit for a single mbarrier wait (nanoseconds).
@@ -270,6 +271,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking probe of a barrier phase (no suspend window): true when the
+// phase with the given parity has completed.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
@@ -355,6 +370,15 @@ __device__ __forceinline__ void bulk_wait_group0() {
 // Generic-proxy shared-memory writes become visible to the async proxy (TMA).
 __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Bulk prefetch of [src, src + bytes) from global memory into L2 (no
+// destination, no completion to wait for).  src 16-byte aligned, bytes a
+// multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
+               "r"(bytes)
+               : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,

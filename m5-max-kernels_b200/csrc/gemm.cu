@@ -2,8 +2,8 @@
 //
 //   C[m, n] = epilogue( sum_k A[m, k] * B[n, k] )        A: [M, K], B: [N, K], both K-major
 //
-// Reference operator: src/m5kernels/metal.py:237-348 (gemm) with the epilogue
-// strings at metal.py:167-207, and the Q/K projection + RMSNorm + RoPE of
+// Reference operator: src/m5kernels/metal.py:158-269 (gemm) with the epilogue
+// strings at metal.py:89-128, and the Q/K projection + RMSNorm + RoPE of
 // src/m5kernels/qk_rope.py:120-182 (shaders/qk_rope_projection.metal,
 // shaders/qk_rope_body.metal).
 //
@@ -57,7 +57,7 @@ struct GemmCfg {
   // (Q/K pair tiles: 5 stages beside their 64 KB of staging.)
   static constexpr int STAGES = QK ? 5 : (STAGE_BYTES <= 32 * 1024 ? 6 : 4);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 32;
   // Epilogue warps: 4, or 8 for pair tiles (each warp drains one of the tile's
   // two heads (Q/K), or half of its columns, for its 32 rows).
   static constexpr int EPI_WARPS = PAIR ? 8 : 4;
@@ -269,6 +269,62 @@ __device__ __forceinline__ void epilogue_pack16(const GemmArgs& g, const uint32_
   }
 }
 
+// ---------------------------------------------------------------- split-K
+// With g.sk, CTA pair u works on tile u % T over k-blocks
+// [s*nkb/S, (s+1)*nkb/S), s = u / T (T = g.sk_tiles, S = g.sk_splits): the S
+// pairs of a tile share its K range, and pairs with the same s walk their
+// k-blocks in step, so tiles that share operands read them together.
+// Partial accumulators of pair u, CTA `rank` of the pair: 128 rows x BN INT32
+// as [chunk][4 words][row] uint4, so the 32 lanes of a warp (32 rows) store
+// and load 512 contiguous bytes.
+template <int BN>
+__device__ __forceinline__ uint4* sk_slot(const GemmArgs& g, int u, uint32_t rank) {
+  constexpr int kSlotU4 = kBM * BN * 4 / 16;
+  return g.sk_part + static_cast<size_t>(u * 2 + static_cast<int>(rank)) * kSlotU4;
+}
+// r += the partial sums of 32-column chunk `chunk` (row prow of this CTA)
+// stored by the other pairs of tile `tile` (pairs tile + s*T, s != the
+// caller's split).  INT32 addition is exact, so the order does not matter.
+template <int BN>
+__device__ __forceinline__ void sk_add_partials(const GemmArgs& g, uint32_t (&r)[32], int chunk,
+                                                int prow, uint32_t rank, int self, int tile) {
+  for (int s = 0; s < g.sk_splits; ++s) {
+    const int v = tile + s * g.sk_tiles;
+    if (v == self) continue;
+    const uint4* src = sk_slot<BN>(g, v, rank) + chunk * 8 * kBM + prow;
+    uint4 p[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) p[q] = __ldcg(src + q * kBM);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      r[4 * q] += p[q].x;
+      r[4 * q + 1] += p[q].y;
+      r[4 * q + 2] += p[q].z;
+      r[4 * q + 3] += p[q].w;
+    }
+  }
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded spin of one thread until *word >= target (shared memory written by
+// other warps of this CTA); records DEV_TIMEOUT_FIXUP and aborts on timeout.
+__device__ __forceinline__ void spin_shared_at_least(volatile int* word, int target,
+                                                     volatile int* abort, unsigned int* status) {
+  if (*word >= target) return;
+  const unsigned long long start = globaltimer_ns();
+  while (*word < target) {
+    if (*abort) return;
+    if (globaltimer_ns() - start > kWaitLimitNs) {
+      if (status) atomicOr(status, DEV_TIMEOUT_FIXUP);
+      *abort = 1;
+      return;
+    }
+  }
+}
+
 template <int KIND, int BN, bool QK, bool PAIR>
 __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -296,6 +352,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // split-K hand-offs between the epilogue warps of this CTA (see below)
+  volatile int* sk_ticket = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* sk_signal = reinterpret_cast<volatile int*>(tmem_slot + 3);
+  int* sk_stored = reinterpret_cast<int*>(tmem_slot + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -315,6 +375,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    *sk_ticket = 0;
+    *sk_signal = 0;
+    *sk_stored = 0;
     fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -342,21 +405,52 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_units_total = g.num_units;
   const int nkb = g.num_k_blocks;
-  // Unit -> (tile, N offset within the tile, width): whole tiles first, then halves.
-  auto unit_tile = [&](int u, int& m_blk, int& n_col, bool& whole) {
+  // Work items of this CTA (pair), walked identically by the producer, MMA
+  // and epilogue roles:
+  //   data-parallel: units t = unit, unit + units, ... -- whole tiles, then
+  //     the N-halves of a split last wave -- each over all k-blocks;
+  //   split-K (g.sk, PAIR only): one item, tile unit % T over the k-blocks
+  //     of split unit / T.
+  struct Work {
+    int tile, m_blk, n_col, kb0, kb1;
+    bool whole, first;
+  };
+  const bool sk = PAIR && g.sk;
+  const long long work_start = unit;
+  auto next_work = [&](long long& cur, Work& w) -> bool {
     int n_blk;
+    if (sk) {  // one item: a tile and this pair's K range of it
+      if (cur != unit) return false;
+      w.tile = unit % g.sk_tiles;
+      const int split = unit / g.sk_tiles;
+      w.kb0 = split * nkb / g.sk_splits;
+      w.kb1 = (split + 1) * nkb / g.sk_splits;
+      w.first = true;
+      cur = -1;
+      tile_coords(w.tile, g, w.m_blk, n_blk);
+      w.n_col = n_blk * BN;
+      w.whole = true;
+      return true;
+    }
+    if (cur >= g.num_units) return false;
+    const int u = static_cast<int>(cur);
     if (u < g.num_full) {
-      tile_coords(u, g, m_blk, n_blk);
-      n_col = n_blk * BN;
-      whole = true;
+      tile_coords(u, g, w.m_blk, n_blk);
+      w.n_col = n_blk * BN;
+      w.whole = true;
     } else {
       const int h = u - g.num_full;
-      tile_coords(g.num_full + (h >> 1), g, m_blk, n_blk);
-      n_col = n_blk * BN + (h & 1) * (BN / 2);
-      whole = false;
+      tile_coords(g.num_full + (h >> 1), g, w.m_blk, n_blk);
+      w.n_col = n_blk * BN + (h & 1) * (BN / 2);
+      w.whole = false;
     }
+    w.tile = u;
+    w.kb0 = 0;
+    w.kb1 = nkb;
+    w.first = true;
+    cur += units;
+    return true;
   };
 
   if (warp == 0) {
@@ -365,16 +459,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int t = unit; t < num_units_total && !*abort_flag; t += units) {
-        int m_blk, n_col;
-        bool whole;
-        unit_tile(t, m_blk, n_col, whole);
-        const int a_row = m_blk * Cfg::TILE_M + static_cast<int>(rank) * kBM;
-        const int b_rows = whole ? Cfg::B_ROWS : Cfg::B_ROWS / 2;
-        const int b_row = n_col + static_cast<int>(rank) * b_rows;
-        const CUtensorMap* bmap = whole ? &tmap_b : &tmap_b_half;
+      long long cur = work_start;
+      Work w;
+      while (!*abort_flag && next_work(cur, w)) {
+        const int a_row = w.m_blk * Cfg::TILE_M + static_cast<int>(rank) * kBM;
+        const int b_rows = w.whole ? Cfg::B_ROWS : Cfg::B_ROWS / 2;
+        const int b_row = w.n_col + static_cast<int>(rank) * b_rows;
+        const CUtensorMap* bmap = w.whole ? &tmap_b : &tmap_b_half;
         const uint32_t stage_bytes = Cfg::A_BYTES + b_rows * 128;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, g.status,
                                  DEV_TIMEOUT_PRODUCER))
             break;
@@ -423,8 +516,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = unit; t < num_units_total && ok; t += units, ++local) {
-        const uint32_t idesc = t < g.num_full ? IDESC : IDESC_HALF;
+      long long cur = work_start;
+      Work w;
+      for (; ok && next_work(cur, w); ++local) {
+        const uint32_t idesc = w.whole ? IDESC : IDESC_HALF;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, abort_flag, g.status,
@@ -434,7 +529,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, g.status, DEV_TIMEOUT_MMA)) {
             ok = false;
             break;
@@ -444,12 +539,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
           const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
+            const uint32_t accumulate = (kb != w.kb0 || k != 0) ? 1u : 0u;
             if constexpr (PAIR)
               tc_mma_pair<KIND>(d_tmem, smem_desc_k128(a_base + k * 32),
-                                smem_desc_k128(b_base + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+                                smem_desc_k128(b_base + k * 32), idesc, accumulate);
             else
               tc_mma<KIND>(d_tmem, smem_desc_k128(a_base + k * 32),
-                           smem_desc_k128(b_base + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+                           smem_desc_k128(b_base + k * 32), idesc, accumulate);
           }
           if constexpr (PAIR)
             tc_commit_pair(&empty[stage]);
@@ -499,10 +595,20 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     uint8_t* out_stage = qk_stage + (warp - 2) * 4096;
     uint32_t ostage = 0;
     int local = 0;
-    for (int t = unit; t < num_units_total; t += units, ++local) {
-      int m_blk, n_col;
-      bool whole;
-      unit_tile(t, m_blk, n_col, whole);
+    long long cur = work_start;
+    Work w;
+    // Split-K hand-offs between this CTA's epilogue warps, all through
+    // bounded spins on shared words (no hardware barrier a timed-out warp
+    // could leave waiting): sk_signal counts the leader's announcements (the
+    // arrival ticket is readable; the other pairs' partial sums are ready),
+    // sk_stored counts warps whose partial stores are complete.  Every warp
+    // walks the same work items, so all of them expect the same counts.
+    int sig_expect = 0, stored_expect = 0;
+    const bool sk_leader = threadIdx.x == 64;  // lane 0 of the first epilogue warp
+    const int prow = quarter * 32 + lane;      // this thread's row within the CTA's 128
+    for (; next_work(cur, w); ++local) {
+      const int m_blk = w.m_blk, n_col = w.n_col;
+      const bool whole = w.whole;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, g.status,
@@ -514,6 +620,78 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const float sa = (g.quantized && row < g.M) ? __ldg(g.a_scales + row) : 1.0f;
+      // Split-K: the S pairs of a tile each take an arrival ticket per CTA;
+      // all but the last store their INT32 partial sums and count them done;
+      // the last waits (bounded) until the others' stores are done, resets
+      // the counters and adds the partials to its own accumulator chunk by
+      // chunk before the ordinary epilogue.
+      bool fixup = false;
+      if (sk) {
+        const int others = g.sk_splits - 1;
+        {
+          int* ctr = g.sk_ctr + (w.tile * 2 + static_cast<int>(rank)) * 2;
+          ++sig_expect;
+          if (sk_leader) {
+            *sk_ticket = atomicAdd(ctr, 1);
+            __threadfence_block();
+            *sk_signal = sig_expect;
+          }
+          if (lane == 0) spin_shared_at_least(sk_signal, sig_expect, abort_flag, g.status);
+          __syncwarp();
+          const int ticket = *sk_ticket;
+          if (ticket < others) {
+            uint4* dst = sk_slot<BN>(g, unit, rank) + prow;
+            constexpr int kChunks = BN / 32;
+            const int c_first = Cfg::EPI_WARPS == 8 ? ehalf * (kChunks / 2) : 0;
+            const int c_end = Cfg::EPI_WARPS == 8 ? c_first + kChunks / 2 : kChunks;
+#pragma unroll 1
+            for (int c = c_first; c < c_end; ++c) {
+              uint32_t r[32];
+              tmem_ld32(taddr + c * 32, r);
+              tmem_wait_ld();
+              if (c == c_end - 1) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) release_acc(acc);
+              }
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                dst[(c * 8 + q) * kBM] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+            }
+            __threadfence();
+            __syncwarp();
+            stored_expect += Cfg::EPI_WARPS;
+            if (lane == 0) atomicAdd(sk_stored, 1);
+            if (sk_leader) {
+              spin_shared_at_least(sk_stored, stored_expect, abort_flag, g.status);
+              __threadfence();
+              atomicAdd(ctr + 1, 1);
+            }
+            __syncwarp();
+            continue;
+          }
+          ++sig_expect;
+          if (sk_leader) {
+            const unsigned long long start = globaltimer_ns();
+            while (ld_acquire_gpu(ctr + 1) < others) {
+              if (*abort_flag) break;
+              if (globaltimer_ns() - start > kWaitLimitNs) {
+                atomicOr(g.status, DEV_TIMEOUT_FIXUP);
+                *abort_flag = 1;
+                break;
+              }
+            }
+            ctr[0] = 0;  // zero again for the next launch
+            ctr[1] = 0;
+            __threadfence();
+            *sk_signal = sig_expect;
+          }
+          if (lane == 0) spin_shared_at_least(sk_signal, sig_expect, abort_flag, g.status);
+          __syncwarp();
+          __threadfence();
+          fixup = true;
+        }
+      }
       if constexpr (!QK) {
         // This warp's 32-column chunks: all of the tile's, or with 8 warps
         // the half matching ehalf.
@@ -529,6 +707,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             uint32_t r[32];
             tmem_ld32(taddr + c * 32, r);
             tmem_wait_ld();
+            if (fixup) sk_add_partials<BN>(g, r, c, prow, rank, unit, w.tile);
             if (c == c_end - 1) {  // the accumulator is drained: hand it back
               tc_fence_before();
               __syncwarp();
@@ -588,6 +767,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             uint32_t r[32];
             tmem_ld32(taddr + c * 32, r);
             tmem_wait_ld();
+            if (fixup) sk_add_partials<BN>(g, r, c, prow, rank, unit, w.tile);
             epilogue_chunk<KIND>(g, r, row, n_col + c * 32, sa);
           }
           tc_fence_before();
@@ -662,6 +842,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             uint32_t r[32];
             tmem_ld32(taddr + hh * 128 + c * 32, r);
             tmem_wait_ld();
+            if (fixup) sk_add_partials<BN>(g, r, hh * 4 + c, prow, rank, unit, w.tile);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               uint32_t pk[4];

@@ -186,8 +186,31 @@ struct GemmArgs {
   // two N-halves each (units [num_full, num_units)), which evens out the wave.
   int num_full;
   int num_units;
+  // Split-K schedule (INT8 CTA-pair GEMMs whose tiles fill at most half of
+  // the GPU's CTA pairs, see gemm.cu): CTA pair u works on tile u % sk_tiles
+  // over the k-blocks of split u / sk_tiles (sk_splits equal K ranges); the
+  // last pair of a tile to finish adds the others' INT32 partial
+  // accumulators (sk_part) to its own.  sk_ctr holds two counters per (tile,
+  // CTA of the pair): arrival tickets and finished partial stores; they start
+  // at zero and the finishing pair resets them, so they are zero again after
+  // every launch.
+  int sk;                     // 1: split-K schedule
+  int sk_splits;              // S >= 2 pairs per tile
+  int sk_tiles;               // T tiles; the launch has T * S CTA pairs
+  int* sk_ctr;                // [tiles][2 CTAs][ticket, done]
+  uint4* sk_part;             // [T * S pairs][2 CTAs][128 x 256 INT32 partials]
   unsigned int* status;       // device status word (bounded-wait errors)
 };
+
+// Split-K workspace for a GPU with `pairs` CTA pairs: the partial
+// accumulators of every pair (128 x 256 INT32 per CTA) and the counters of up
+// to `pairs` tiles.
+constexpr int kSplitKMaxSplits = 4;
+constexpr int kSplitKMinBlocks = 8;        // k-blocks per split, at least
+inline long long splitk_part_bytes(int pairs) { return (long long)pairs * 2 * 128 * 256 * 4; }
+inline long long splitk_workspace_bytes(int pairs) {
+  return splitk_part_bytes(pairs) + (long long)pairs * 2 * 2 * (long long)sizeof(int);
+}
 
 // `to`: the Q/K output map (3D {128, M, N/128} bf16, boxes {64, 32, 1}, 128-byte
 // swizzle), or with g.tma_store the [M, N] output map of the other epilogues

@@ -1,7 +1,7 @@
 // Per-token symmetric quantization of plain rows (no normalization, no
 // rotation): the online activation quantization of the W8A8 / FP8 GEMM.
 //
-// Reference contract: src/m5kernels/metal.py:106-123 (quantize) with the
+// Reference contract: src/m5kernels/metal.py:27-44 (quantize) with the
 // arithmetic of src/m5kernels/numerics.py:29-46 (quantize_reference):
 //   scale = peak / 127 (int8) or peak / 448 (E4M3), 1 for an all-zero row;
 //   code  = clip(rint(x / scale), +-127) or E4M3_RNE_saturating(x / scale).
@@ -11,9 +11,11 @@
 // instruction) and keeps them packed in registers (a bf16 row of 16384 is 32
 // registers per thread), reduces max |x| on the packed 16-bit pairs, then
 // quantizes the same registers with packed-FP32 arithmetic and stores the
-// codes 8 bytes per lane.  Rows wider than 256 x 16 vectors stream twice
-// (peak pass from HBM, code pass from L2).  HBM traffic per row:
-// K * sizeof(T) read, K written, 4 for the scale.
+// codes 8 bytes per lane.  While a row is processed, the CTA's next row is
+// already streaming into L2 (one bulk prefetch per row).  Rows wider than
+// 256 x 16 vectors stream twice (peak pass from HBM, code pass from L2).  HBM
+// traffic per row: K * sizeof(T) read, K written, 4 for the scale.
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -26,9 +28,9 @@ namespace {
 
 using namespace qv;
 
-constexpr int kThreads = 256;
 constexpr int kTieQueue = 64;  // queued near-tie vectors per warp and row
 
+template <int NT>
 __device__ __forceinline__ float cta_peak(float peak, float* red) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, off));
@@ -36,41 +38,47 @@ __device__ __forceinline__ float cta_peak(float peak, float* red) {
   __syncthreads();
   peak = red[0];
 #pragma unroll
-  for (int w = 1; w < kThreads / 32; ++w) peak = fmaxf(peak, red[w]);
+  for (int w = 1; w < NT / 32; ++w) peak = fmaxf(peak, red[w]);
   __syncthreads();
   return peak;
 }
 
-// VPT > 0: each thread holds VPT vectors of the row in registers (one HBM
-// read).  VPT == 0: two streaming passes for very wide rows.  EXACT: the row
-// is exactly VPT * kThreads vectors (K = 2048 * 2^k for 16-bit inputs), so no
-// vector needs a bounds guard.
-template <typename T, int OUT, int VPT, bool EXACT>
-__global__ void __launch_bounds__(kThreads)
+// NT threads per row.  VPT > 0: each thread holds VPT vectors of the row in
+// registers (one HBM read).  VPT == 0: two streaming passes for very wide
+// rows.  EXACT: the row is exactly VPT * NT vectors, so no vector needs a
+// bounds guard.
+template <typename T, int OUT, int VPT, bool EXACT, int NT>
+__global__ void __launch_bounds__(NT)
     quant_rows_kernel(const T* __restrict__ x, int64_t rows, int64_t K, uint8_t* __restrict__ q,
                       float* __restrict__ s) {
   constexpr int V = kVec<T>;
-  __shared__ float red[kThreads / 32];
-  __shared__ uint4 tie_raw[kThreads / 32][kTieQueue];
-  __shared__ int tie_idx[kThreads / 32][kTieQueue];
-  __shared__ int tie_n[kThreads / 32];
+  __shared__ float red[NT / 32];
+  __shared__ uint4 tie_raw[NT / 32][kTieQueue];
+  __shared__ int tie_idx[NT / 32][kTieQueue];
+  __shared__ int tie_n[NT / 32];
   const int tid = threadIdx.x;
   const int nvec = static_cast<int>(K / V);  // K % V == 0 on this path
   const float qmax = OUT == OUT_E4M3 ? 448.0f : 127.0f;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
     uint8_t* qr = q + row * K;
+    // This CTA's next row starts streaming into L2 now, so its reads overlap
+    // the dependent chain of this row (peak, barrier, codes, stores) instead
+    // of following it.  Rows here are whole 16-byte vectors on 16-byte
+    // aligned bases (quant_rows_applicable).
+    if (VPT > 0 && tid == 0 && row + gridDim.x < rows)
+      prefetch_l2_bulk(x + (row + gridDim.x) * K, static_cast<uint32_t>(K * sizeof(T)));
     if constexpr (VPT > 0) {
       uint4 raw[VPT];
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
-        const int j = tid + i * kThreads;
+        const int j = tid + i * NT;
         raw[i] = (EXACT || j < nvec) ? __ldg(xr + j) : make_uint4(0, 0, 0, 0);
       }
       Peak<T> pk;
 #pragma unroll
       for (int i = 0; i < VPT; ++i) pk.add(raw[i]);
-      const float peak = cta_peak(pk.value(), red);
+      const float peak = cta_peak<NT>(pk.value(), red);
       const float scale = peak == 0.0f ? 1.0f : __fdiv_rn(peak, qmax);
       const float inv = __frcp_rn(scale);
       const bool fast = scale >= 0x1p-100f;
@@ -86,7 +94,7 @@ __global__ void __launch_bounds__(kThreads)
         __syncwarp();
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
-          const int j = tid + i * kThreads;
+          const int j = tid + i * NT;
           if (EXACT || j < nvec) {
             uint32_t words[V / 4];
             const uint32_t acc = pack_i8_vec<T>(raw[i], br, words);
@@ -113,7 +121,7 @@ __global__ void __launch_bounds__(kThreads)
       } else {
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
-          const int j = tid + i * kThreads;
+          const int j = tid + i * NT;
           if (j < nvec) {
             uint32_t words[V / 4];
             vec_codes<T, OUT>(raw[i], scale, inv, fast, words);
@@ -124,22 +132,22 @@ __global__ void __launch_bounds__(kThreads)
     } else {
       Peak<T> p0, p1, p2, p3;
       int j = tid;
-      for (; j + 3 * kThreads < nvec; j += 4 * kThreads) {
-        const uint4 a = __ldg(xr + j), b = __ldg(xr + j + kThreads);
-        const uint4 c = __ldg(xr + j + 2 * kThreads), d = __ldg(xr + j + 3 * kThreads);
+      for (; j + 3 * NT < nvec; j += 4 * NT) {
+        const uint4 a = __ldg(xr + j), b = __ldg(xr + j + NT);
+        const uint4 c = __ldg(xr + j + 2 * NT), d = __ldg(xr + j + 3 * NT);
         p0.add(a);
         p1.add(b);
         p2.add(c);
         p3.add(d);
       }
-      for (; j < nvec; j += kThreads) p0.add(__ldg(xr + j));
+      for (; j < nvec; j += NT) p0.add(__ldg(xr + j));
       const float peak =
-          cta_peak(fmaxf(fmaxf(p0.value(), p1.value()), fmaxf(p2.value(), p3.value())), red);
+          cta_peak<NT>(fmaxf(fmaxf(p0.value(), p1.value()), fmaxf(p2.value(), p3.value())), red);
       const float scale = peak == 0.0f ? 1.0f : __fdiv_rn(peak, qmax);
       const float inv = __frcp_rn(scale);
       const bool fast = scale >= 0x1p-100f;
       if (tid == 0) s[row] = scale;
-      for (j = tid; j < nvec; j += kThreads) {
+      for (j = tid; j < nvec; j += NT) {
         uint32_t words[V / 4];
         vec_codes<T, OUT>(__ldg(xr + j), scale, inv, fast, words);
         store_codes<T>(qr, j, words);
@@ -148,19 +156,19 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-template <typename T, int OUT, int VPT>
+template <typename T, int OUT, int VPT, int NT>
 cudaError_t launch_quant_v(const RowPrepArgs& a, cudaStream_t stream) {
-  const bool exact = VPT > 0 && a.K / kVec<T> == int64_t(VPT) * kThreads;
-  auto kern = exact ? quant_rows_kernel<T, OUT, VPT, VPT != 0>
-                    : quant_rows_kernel<T, OUT, VPT, false>;
+  const bool exact = VPT > 0 && a.K / kVec<T> == int64_t(VPT) * NT;
+  auto kern = exact ? quant_rows_kernel<T, OUT, VPT, VPT != 0, NT>
+                    : quant_rows_kernel<T, OUT, VPT, false, NT>;
   static std::atomic<long long> shape[2][kMaxLaunchDevices];
   int dev = 0, sms = 0, per_sm = 0;
-  cudaError_t e = launch_shape(reinterpret_cast<const void*>(kern), kThreads, 0, shape[exact],
-                               &dev, &sms, &per_sm);
+  cudaError_t e = launch_shape(reinterpret_cast<const void*>(kern), NT, 0, shape[exact], &dev,
+                               &sms, &per_sm);
   if (e != cudaSuccess) return e;
   int64_t grid = int64_t(sms) * per_sm;
   if (grid > a.rows) grid = a.rows;
-  kern<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
+  kern<<<static_cast<unsigned>(grid), NT, 0, stream>>>(
       reinterpret_cast<const T*>(a.x), a.rows, a.K, reinterpret_cast<uint8_t*>(a.q), a.s);
   return cudaGetLastError();
 }
@@ -168,12 +176,13 @@ cudaError_t launch_quant_v(const RowPrepArgs& a, cudaStream_t stream) {
 template <typename T, int OUT>
 cudaError_t launch_quant_t(const RowPrepArgs& a, cudaStream_t stream) {
   const int64_t nvec = a.K / kVec<T>;
-  if (nvec <= 1 * kThreads) return launch_quant_v<T, OUT, 1>(a, stream);
-  if (nvec <= 2 * kThreads) return launch_quant_v<T, OUT, 2>(a, stream);
-  if (nvec <= 4 * kThreads) return launch_quant_v<T, OUT, 4>(a, stream);
-  if (nvec <= 8 * kThreads) return launch_quant_v<T, OUT, 8>(a, stream);
-  if (nvec <= 16 * kThreads) return launch_quant_v<T, OUT, 16>(a, stream);
-  return launch_quant_v<T, OUT, 0>(a, stream);
+  constexpr int kNT = 256;
+  if (nvec <= 1 * kNT) return launch_quant_v<T, OUT, 1, kNT>(a, stream);
+  if (nvec <= 2 * kNT) return launch_quant_v<T, OUT, 2, kNT>(a, stream);
+  if (nvec <= 4 * kNT) return launch_quant_v<T, OUT, 4, kNT>(a, stream);
+  if (nvec <= 8 * kNT) return launch_quant_v<T, OUT, 8, kNT>(a, stream);
+  if (nvec <= 16 * kNT) return launch_quant_v<T, OUT, 16, kNT>(a, stream);
+  return launch_quant_v<T, OUT, 0, kNT>(a, stream);
 }
 
 }  // namespace

@@ -9,14 +9,14 @@ The `cuda-b200` backend of the m5kernels operator contracts:
     projection_qk_rope, qk_norm_rope   (twin of m5kernels.qk_rope)
     projection_qkv_rope                (grouped Q/K/V layout of the H3 integration)
     rms_quantize                       (twin of m5kernels.rms_quant)
-    linear                             (the online quantize -> gemm stage in one call)
+    linear, OnlineProjection           (the online quantize -> gemm stage in one call / bound step)
 All of them run hand-written CUDA kernels from libm5b200.so through its C ABI
 (include/m5b200.h); there is no CPU fallback.
 """
 
 from .cuda import gemm, gemm_allgather, quantize
 from .hadamard import SUPPORTED_BLOCK_SIZES, hadamard_quantize, rotate
-from .linear import linear
+from .linear import OnlineProjection, linear
 from .norm_hadamard import (fused_gated_residual_norm_hadamard_quantize,
                             fused_norm_hadamard_quantize, gated_residual_add, unfused_norm)
 from .qk_rope import (grouped_qkv_weights, projection_qk_rope, projection_qkv_rope, qk_norm_rope,
@@ -28,4 +28,5 @@ __all__ = [
     "fused_norm_hadamard_quantize", "fused_gated_residual_norm_hadamard_quantize",
     "projection_qk_rope", "rope_tables", "linear", "rms_quantize", "gated_residual_add",
     "unfused_norm", "qk_norm_rope", "projection_qkv_rope", "grouped_qkv_weights",
+    "OnlineProjection",
 ]

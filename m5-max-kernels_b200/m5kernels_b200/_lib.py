@@ -44,7 +44,10 @@ _SIGNATURES = {
     "m5b_gated_residual_add": ([P, P, I, I64, I64, P, I, P, I64, P, P], I),
     "m5b_qk_norm_rope": ([P, I64, I64, P, P, P, I, F, P, P], I),
     "m5b_gemm": ([P, P, I64, I64, I64, I, P, P, P, I, P, P, I64, P, P, P, I64, P], I),
+    "m5b_gemm_workspace_bytes": ([I64, I64, I64, I], I64),
+    "m5b_gemm_ex": ([P, P, I64, I64, I64, I, P, P, P, I, P, P, I64, P, P, P, I64, P, I64, P], I),
     "m5b_projection_qk_rope": ([P, P, I64, I64, I64, I, P, P, P, P, P, I, F, P, P], I),
+    "m5b_projection_qk_rope_ex": ([P, P, I64, I64, I64, I, P, P, P, P, P, I, F, P, P, I64, P], I),
     "m5b_projection_qkv_rope": ([P, P, I64, I64, I64, I, P, P, P, P, P, P, I, F, P, P, P, P], I),
     "m5b_gemm_allgather": ([P, P, I64, I64, I64, I, P, P, P, I64, I64, P, I, P], I),
     "m5b_ipc_export": ([P, P, ctypes.POINTER(ctypes.c_int64)], I),
@@ -52,6 +55,7 @@ _SIGNATURES = {
     "m5b_ipc_release": ([P, I64], I),
     "m5b_linear_workspace_bytes": ([I64, I64], I64),
     "m5b_linear": ([P, I, I64, I64, I, P, P, P, I64, I, P, I, P, I64, P], I),
+    "m5b_linear_ex": ([P, I, I64, I64, I, P, P, P, I64, I, P, I, P, I64, P, I64, P], I),
     "m5b_linear_noalloc": ([P, I, I64, I64, I, P, P, P, I64, I, P, I, P], I),
 }
 

@@ -29,7 +29,7 @@ def quantize(x: torch.Tensor, mode: str, tag: str = "packed"):
 
     int8: scale = amax/127, codes = clip(rint(x/scale), +-127) (int8).
     fp8:  scale = amax/448, codes = E4M3 bits (uint8), RNE, saturating.
-    All-zero rows use scale 1.  Mirrors src/m5kernels/metal.py:106-123.
+    All-zero rows use scale 1.  Mirrors src/m5kernels/metal.py:27-44.
     """
     del tag
     if mode == "mxint8":
@@ -50,16 +50,6 @@ def quantize(x: torch.Tensor, mode: str, tag: str = "packed"):
     return q, s
 
 
-def _pad_k(t: torch.Tensor, multiple: int) -> torch.Tensor:
-    k = t.shape[1]
-    pad = (-k) % multiple
-    if pad == 0:
-        return t
-    out = torch.zeros((t.shape[0], k + pad), dtype=t.dtype, device=t.device)
-    out[:, :k] = t
-    return out
-
-
 def gemm(a, b, mode="bf16", tile=(64, 64, 4, 1), a_scales=None, b_scales=None,
          output_dtype=None, bias=None, bias_row_map=None, residual=None, gate=None,
          gate_row_map=None):
@@ -69,7 +59,7 @@ def gemm(a, b, mode="bf16", tile=(64, 64, 4, 1), a_scales=None, b_scales=None,
     INT8 optionally adds an FP32 bias [N] or a bias table [P,N] selected by
     int32 bias_row_map[M].  INT8/BF16 optionally fuse the gated residual
     out = R + bf16(branch) * gate with BF16 residual [M,N] and gate [N] or
-    [P,N] + gate_row_map.  Mirrors src/m5kernels/metal.py:237-348; output
+    [P,N] + gate_row_map.  Mirrors src/m5kernels/metal.py:158-269; output
     dtype defaults to float32 like the reference.  output_dtype=torch.int32
     (INT8, no scales) returns the raw INT32 accumulators.
     """
@@ -89,6 +79,12 @@ def gemm(a, b, mode="bf16", tile=(64, 64, 4, 1), a_scales=None, b_scales=None,
             "FP8 requires K/row stride divisible by 128; padding is not implicit")
     if mode == "int8" and k > 133144:
         raise NotImplementedError("INT32 worst-case overflow bound exceeded")
+    elem = 1 if mode in ("int8", "fp8") else 2
+    if (k * elem) % 16:
+        # TMA reads K-major rows whose stride must be a multiple of 16 bytes;
+        # the reference keeps padding explicit (metal.py:186-190), so does this.
+        raise NotImplementedError(
+            f"K*{elem} bytes per row must be a multiple of 16 for TMA; padding is not implicit")
     expected = {"int8": (torch.int8,), "fp8": (torch.uint8,), "bf16": (torch.bfloat16,),
                 "fp16": (torch.float16,)}[mode]
     if a.dtype not in expected or b.dtype not in expected:
@@ -154,22 +150,25 @@ def gemm(a, b, mode="bf16", tile=(64, 64, 4, 1), a_scales=None, b_scales=None,
                             gate_row_map)
     if m == 0 or n == 0 or k == 0:
         raise ValueError("A and B must be nonempty matrices")
-    # TMA needs 16-byte row strides; zero K-padding leaves every sum unchanged.
-    elem = 1 if mode in ("int8", "fp8") else 2
-    a = _pad_k(a.contiguous(), 16 // elem)
-    b = _pad_k(b.contiguous(), 16 // elem)
-    kp = a.shape[1]
+    a = a.contiguous()
+    b = b.contiguous()
     args = [t.contiguous() if t is not None else None
             for t in (a_scales, b_scales, bias, bias_row_map, residual, gate, gate_row_map)]
     a_scales, b_scales, bias, bias_row_map, residual, gate, gate_row_map = args
     out = torch.empty((m, n), dtype=out_dtype, device=dev)
-    check(_lib.lib().m5b_gemm(
-        ptr(a), ptr(b), m, n, kp, _lib.MODE[mode], ptr(a_scales), ptr(b_scales), ptr(out),
+    lib = _lib.lib()
+    # split-K workspace (zero-filled once, left zeroed by every call) for the
+    # shapes that take the split schedule; None keeps the data-parallel one
+    from .linear import gemm_workspace
+
+    ws = gemm_workspace(dev, int(lib.m5b_gemm_workspace_bytes(m, n, k, _lib.MODE[mode])))
+    check(lib.m5b_gemm_ex(
+        ptr(a), ptr(b), m, n, k, _lib.MODE[mode], ptr(a_scales), ptr(b_scales), ptr(out),
         _lib.DTYPE_CODE[out_dtype], ptr(bias), ptr(bias_row_map),
         bias.shape[0] if (bias is not None and bias.dim() == 2) else 0,
         ptr(residual), ptr(gate), ptr(gate_row_map),
         gate.shape[0] if (gate is not None and gate.dim() == 2) else 0,
-        _lib.stream_handle(dev)))
+        ptr(ws), 0 if ws is None else ws.numel(), _lib.stream_handle(dev)))
     return out
 
 

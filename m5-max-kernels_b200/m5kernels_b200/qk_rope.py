@@ -91,9 +91,14 @@ def projection_qk_rope(a, b, gamma, cos, sin, mode="int8", tile=(32, 128, 4, 1),
     a_scales = a_scales.contiguous() if a_scales is not None else None
     b_scales = b_scales.contiguous() if b_scales is not None else None
     out = torch.empty((n // HEAD_DIM, m, HEAD_DIM), dtype=torch.bfloat16, device=dev)
-    check(_lib.lib().m5b_projection_qk_rope(
+    lib = _lib.lib()
+    from .linear import gemm_workspace  # split-K workspace for the shapes that split
+
+    ws = gemm_workspace(dev, int(lib.m5b_gemm_workspace_bytes(m, n, a.shape[1], _lib.MODE[mode])))
+    check(lib.m5b_projection_qk_rope_ex(
         ptr(a), ptr(b), m, n, a.shape[1], _lib.MODE[mode], ptr(a_scales), ptr(b_scales),
-        ptr(gamma), ptr(cos), ptr(sin), rope_half, eps, ptr(out), _lib.stream_handle(dev)))
+        ptr(gamma), ptr(cos), ptr(sin), rope_half, eps, ptr(out), ptr(ws),
+        0 if ws is None else ws.numel(), _lib.stream_handle(dev)))
     return out
 
 

@@ -40,6 +40,52 @@ def build(force: bool = False) -> Path:
     return LIB
 
 
+OMP_SRC = HERE / "m5_cpu_omp.c"
+OMP_LIB = BUILD / "libm5cpu_omp.so"
+_omp = None
+
+
+def build_omp(force: bool = False) -> Path:
+    """Compile the multi-threaded CPU baseline (OpenMP; SIMD kernels chosen at run time)."""
+    BUILD.mkdir(exist_ok=True)
+    if OMP_LIB.exists() and not force and OMP_LIB.stat().st_mtime >= OMP_SRC.stat().st_mtime:
+        return OMP_LIB
+    cmd = ["gcc", "-O3", "-std=c11", "-fPIC", "-shared", "-fopenmp", "-ffp-contract=off",
+           "-fno-fast-math", str(OMP_SRC), "-o", str(OMP_LIB), "-lm"]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    return OMP_LIB
+
+
+def omp_lib() -> ctypes.CDLL:
+    global _omp
+    if _omp is None:
+        _omp = ctypes.CDLL(str(build_omp()))
+        P, I64 = ctypes.c_void_p, ctypes.c_int64
+        _omp.m5c_quantize_bf16.argtypes = [P, I64, I64, P, P]
+        _omp.m5c_quantize_bf16.restype = None
+        _omp.m5c_gemm_i8_bf16.argtypes = [P, P, I64, I64, I64, P, P, P]
+        _omp.m5c_gemm_i8_bf16.restype = None
+        _omp.m5c_threads.restype = ctypes.c_int
+        _omp.m5c_simd_level.restype = ctypes.c_int
+    return _omp
+
+
+def omp_projection(x_bf16, wq, w_scales):
+    """Multi-threaded CPU online projection: INT8 quantize of bf16 rows, then
+    bf16((float(acc) * s_x) * w_scales).  Returns (out bf16, codes, scales)."""
+    x = _cpu(x_bf16)
+    wq, w_scales = _cpu(wq), _cpu(w_scales)
+    m, k = x.shape
+    n = wq.shape[0]
+    q = torch.empty((m, k), dtype=torch.int8)
+    s = torch.empty((m,), dtype=torch.float32)
+    out = torch.empty((m, n), dtype=torch.bfloat16)
+    o = omp_lib()
+    o.m5c_quantize_bf16(_ptr(x), m, k, _ptr(q), _ptr(s))
+    o.m5c_gemm_i8_bf16(_ptr(q), _ptr(wq), m, n, k, _ptr(s), _ptr(w_scales), _ptr(out))
+    return out, q, s
+
+
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
@@ -189,6 +235,6 @@ def row_prep_warps(k: int, block: int) -> int:
 
 
 __all__ = [
-    "build", "row_prep", "quantize", "rotate", "gemm_i8_acc", "gemm_i8_acc_fast",
+    "build", "build_omp", "omp_projection", "row_prep", "quantize", "rotate", "gemm_i8_acc", "gemm_i8_acc_fast",
     "gemm_epilogue", "qk_rope_from_acc", "e4m3_encode_scalar", "row_prep_warps", "np",
 ]

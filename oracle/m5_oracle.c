@@ -14,7 +14,7 @@
  *                                          shaders/norm_hadamard.metal:1-121
  *   gated residual update                src/m5kernels/gated_residual_reference.py:21-60,
  *                                          norm_hadamard.py:62-70
- *   W8A8 GEMM + scale/bias/gate epilogue src/m5kernels/metal.py:167-207
+ *   W8A8 GEMM + scale/bias/gate epilogue src/m5kernels/metal.py:89-128
  *   Q/K RMSNorm + split-half RoPE        src/m5kernels/qk_rope_reference.py:45-134,
  *                                          shaders/qk_rope_body.metal:1-20
  *   RMS scale-folding INT8 preparation   src/m5kernels/rms_quant_reference.py:24-89,

@@ -4,8 +4,7 @@
 
 The reference (9Tempest/m5-max-kernels) is a Python package whose CPU
 references depend only on NumPy.  This script imports them from
-$M5_REFERENCE_SRC (default: the read-only checkout this build was made next
-to), runs them on small seeded inputs and writes the inputs and outputs to
+$M5_REFERENCE_SRC (required: the reference checkout's src/ directory), runs them on small seeded inputs and writes the inputs and outputs to
 tests/golden/*.npz.  The fixtures are committed; the tests never need the
 reference at run time.
 
@@ -28,11 +27,12 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-DEFAULT_SRC = "/root/reference/src"
 
 
 def _import_reference():
-    src = os.environ.get("M5_REFERENCE_SRC", DEFAULT_SRC)
+    src = os.environ.get("M5_REFERENCE_SRC")
+    if not src:
+        raise SystemExit("set M5_REFERENCE_SRC to the reference checkout's src/ directory")
     if not Path(src, "m5kernels").is_dir():
         raise SystemExit(f"reference sources not found under {src}")
     sys.path.insert(0, src)

@@ -23,7 +23,6 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-DEFAULT_ROOT = "/root/reference"
 
 DRIVER = r"""
 #include <stdint.h>
@@ -46,7 +45,10 @@ def _bf16_bits(x: np.ndarray) -> np.ndarray:
 
 
 def main() -> int:
-    root = Path(os.environ.get("M5_REFERENCE_ROOT", DEFAULT_ROOT))
+    env = os.environ.get("M5_REFERENCE_ROOT")
+    if not env:
+        raise SystemExit("set M5_REFERENCE_ROOT to the reference checkout")
+    root = Path(env)
     header_dir = root / "integrations" / "h3"
     if not (header_dir / "qkv_reference.h").is_file():
         raise SystemExit(f"qkv_reference.h not found under {header_dir}")

@@ -36,10 +36,17 @@ def test_reference_arm_prints_one_contract_line():
     assert d["impl"] == "reference"
     assert d["metric"] == base["metric"]
     assert d["unit"] == "TOPS" and d["value"] > 0 and d["higher_is_better"] is True
-    assert d["scaling"] == "weak" and d["n_gpus"] == 1 and d["steps"] == 1
+    assert d["scaling"] == "strong" and d["n_gpus"] == 1 and d["steps"] == 1
     assert d["config"]["workload"].startswith("ffn_down")
+    # the same config dict as the CUDA arm's line at this GPU count
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    assert d["config"] == bench._config(1)
+    assert d["config"]["global_M"] == 4096 and d["rows_per_step"] == 4096  # the full job per step
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["kind"] == "port" and cb["cores"] >= 1 and cb["sample"]
+    assert "OMP_NUM_THREADS" in cb["threads"] and "OPENBLAS_NUM_THREADS" in cb["threads"]
     assert d["e2e"] == {"value": d["value"], "unit": "TOPS", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
 

@@ -105,3 +105,29 @@ def test_qk_rejections(ops):
         ops.projection_qk_rope(aq, bq, gamma, cs, cs, a_scales=s, b_scales=torch.ones(100, device=DEV))
     with pytest.raises(NotImplementedError):
         ops.projection_qk_rope(aq, bq, gamma, cs, cs, "fp8")
+
+
+@pytest.mark.parametrize("shape", [(256, 4096, 4096), (300, 512, 8192), (700, 1408, 4096)])
+def test_qk_rope_splitk_bit_exact(ops, shape, monkeypatch):
+    """Q/K projections with few rows take the split-K schedule (2 to 4 CTA
+    pairs per tile; an odd head count and an M tail): the finishing pair adds
+    the INT32 partial sums before the BF16 projection, so the output is
+    bit-identical to the C epilogue and to the data-parallel schedule."""
+    from m5kernels_b200 import _lib
+
+    m, n, k = shape
+    half = 64
+    assert int(_lib.lib().m5b_gemm_workspace_bytes(m, n, k, _lib.MODE["int8"])) > 0
+    x, w, gamma, cos, sin = _inputs(m, n, k, half, seed=61)
+    aq, sa = ops.quantize(x.to(DEV), "int8")
+    bq, sb = ops.quantize(w.to(DEV), "int8")
+    args = (aq, bq, gamma.to(DEV), cos.to(DEV), sin.to(DEV), "int8")
+    y = ops.projection_qk_rope(*args, a_scales=sa, b_scales=sb, epsilon=1e-5)
+    y2 = ops.projection_qk_rope(*args, a_scales=sa, b_scales=sb, epsilon=1e-5)
+    acc = co.gemm_i8_acc_fast(aq.cpu(), bq.cpu()).float()
+    expect = co.qk_rope_from_acc(acc, sa.cpu(), sb.cpu(), gamma, cos, sin, half, 1e-5)
+    assert torch.equal(y.cpu(), expect) and torch.equal(y2, y)
+    monkeypatch.setenv("M5B_GEMM_SPLITK", "0")
+    dp = ops.projection_qk_rope(*args, a_scales=sa, b_scales=sb, epsilon=1e-5)
+    assert torch.equal(dp, y)
+    assert _lib.device_status() == 0

@@ -82,3 +82,4 @@ def test_hadamard_prep_ties_match_oracle(block):
         o = co.row_prep(x, block=64, norm="rms", eps=1e-5, round_output=True, gamma=gamma,
                         scale=sc, shift=sh, signs=signs)
     assert torch.equal(q.cpu(), o["q"]) and torch.equal(s.cpu(), o["s"])
+

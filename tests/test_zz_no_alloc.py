@@ -85,3 +85,9 @@ def test_noalloc_refuses_sizes_beyond_its_scratch():
                                 _lib.MODE["int8"], ctypes.c_void_p(out.data_ptr()), _lib.BF16,
                                 None)
     assert rc == _lib.EINVAL and b"16384 rows" in lib.m5b_last_error()
+    # a k so large that m * k would overflow int64: refused, not wrapped around
+    rc = lib.m5b_linear_noalloc(ctypes.c_void_p(x.data_ptr()), _lib.BF16, 8, 1 << 61, 0, None,
+                                ctypes.c_void_p(wq.data_ptr()), ctypes.c_void_p(ws.data_ptr()), 8,
+                                _lib.MODE["int8"], ctypes.c_void_p(out.data_ptr()), _lib.BF16,
+                                None)
+    assert rc == _lib.EINVAL and b"67108864" in lib.m5b_last_error()
