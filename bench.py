@@ -660,33 +660,33 @@ def run_b200(args, world, rank, local):
 
     stream = torch.cuda.current_stream(dev)
     K_steps = args.steps
-    # The timed steps as one CUDA graph; external events between the kernels
-    # give each kernel's device time inside the same timed region.
-    kernel_timing = "CUDA events between the kernels inside the timed graph"
-    ev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
-          for _ in range(K_steps)]
-    graph = torch.cuda.CUDAGraph()
-    try:
-        with torch.cuda.graph(graph):
-            for i in range(K_steps):
-                st = steps_sets[i % nsets]
-                ev[i][0].record()
-                st.quantize()
-                ev[i][1].record()
-                st.gemm()
-                ev[i][2].record()
-        in_graph_events = True
-    except Exception:  # no event nodes: per-kernel times from graphs of one kernel each
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            for i in range(K_steps):
-                steps_sets[i % nsets]()
-        in_graph_events = False
-        kernel_timing = "separate CUDA-graph replays of each kernel (no in-graph events)"
-    graph.replay()  # untimed first replay (graph upload)
-    torch.cuda.synchronize()
-    barrier()
 
+    def graph_of(fn):
+        """The K timed launches as one CUDA graph (no events inside: event nodes
+        between kernels add their own latency to every step)."""
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(K_steps):
+                fn(steps_sets[i % nsets])
+        g.replay()  # untimed first replay (graph upload)
+        torch.cuda.synchronize()
+        return g
+
+    def replay_ms(g):
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        g.replay()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        return a0.elapsed_time(a1)
+
+    graph = graph_of(lambda st: st())
+    barrier()
+    # Kernel durations for the roofline: the same K launches of each kernel
+    # alone, replayed as a graph right after the timed region.
+    kernel_timing = ("each kernel's K launches alone as a CUDA graph, CUDA events around the "
+                     "replay, right after the timed region")
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -700,26 +700,13 @@ def run_b200(args, world, rank, local):
         clocks.active.clear()
         barrier()
         ms_total = e0.elapsed_time(e1)
-        if in_graph_events:
-            prep_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / K_steps
-            gemm_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / K_steps
-        else:
-            def one_kernel_ms(fn):
-                g1 = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g1):
-                    for i in range(K_steps):
-                        fn(steps_sets[i % nsets])
-                g1.replay()
-                torch.cuda.synchronize()
-                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a0.record(stream)
-                g1.replay()
-                a1.record(stream)
-                torch.cuda.synchronize()
-                return a0.elapsed_time(a1) / K_steps
-            prep_ms = one_kernel_ms(lambda st: st.quantize())
-            gemm_ms = one_kernel_ms(lambda st: st.gemm())
         del graph
+        g_prep = graph_of(lambda st: st.quantize())
+        prep_ms = replay_ms(g_prep) / K_steps
+        del g_prep
+        g_gemm = graph_of(lambda st: st.gemm())
+        gemm_ms = replay_ms(g_gemm) / K_steps
+        del g_gemm
         ms_per_step = max_over_ranks(ms_total / K_steps)
         prep_ms_max = max_over_ranks(prep_ms)
         gemm_ms_max = max_over_ranks(gemm_ms)

@@ -82,6 +82,19 @@ M5B_API int m5b_device_status(unsigned int* status_out, int clear);
 M5B_API int m5b_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int mode, void* q,
                  float* scales, void* stream);
 
+/* MXINT8 quantization of x[rows, k] (bf16 / fp16 / fp32), k % 32 == 0: per
+ * 32-element block along a row, peak = max|x|,
+ *   e = clip(floor(log2(peak)) - 6, -127, 127)   (0 for an all-zero block),
+ *   q = clip(rint(x / 2^e), +-127)  int8 [rows, k],
+ *   scale_bytes[rows, k / 32] = e + 127           (E8M0),
+ * so x ~= q * 2^e (the S1.6 /64 of OCP MXINT8 folded into the scale plane).
+ * floor(log2(peak)) is the exact binary exponent of the peak.  x 16-byte
+ * aligned, q 8-byte aligned.
+ * Replaces src/m5kernels/metal.py:27-44 (quantize, mode "mxint8") with the
+ * arithmetic of src/m5kernels/numerics.py:32-40 (quantize_reference). */
+M5B_API int m5b_quantize_mxint8(const void* x, int x_dtype, int64_t rows, int64_t k, int8_t* q,
+                                uint8_t* scale_bytes, void* stream);
+
 /* FP32 signed block Hadamard rotation y = x D H (H normalized Sylvester,
  * blocks of block_size along k, block_size in {32..1024}, k % block_size == 0).
  * signs: int8[k] of +-1, or NULL for D = I.

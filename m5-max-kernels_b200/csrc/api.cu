@@ -266,6 +266,22 @@ int m5b_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int mode, 
   return run_row_prep(a, x_dtype, 0, out, stream);
 }
 
+int m5b_quantize_mxint8(const void* x, int x_dtype, int64_t rows, int64_t k, int8_t* q,
+                        uint8_t* scale_bytes, void* stream) {
+  int rc = check_rows(rows, k);
+  if (rc) return rc;
+  if (k % 32) return fail(M5B_EINVAL, "MXINT8 requires K divisible by 32");
+  if (!float_dtype(x_dtype)) return fail(M5B_EINVAL, "input dtype must be float16, bfloat16 or float32");
+  if (!x || !q || !scale_bytes) return fail(M5B_EINVAL, "input or output pointer is NULL");
+  if (!aligned(x, 16) || !aligned(q, 8))
+    return fail(M5B_EINVAL, "input must be 16-byte and codes 8-byte aligned");
+  if (rows > (int64_t(1) << 40) / k) return fail(M5B_EUNSUPPORTED, "tensor too large");
+  cudaError_t e = launch_mxint8(x, x_dtype, rows * k, q, scale_bytes,
+                                static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "MXINT8 quantization launch");
+  return ok();
+}
+
 int m5b_rotate(const void* x, int x_dtype, int64_t rows, int64_t k, int block_size,
                const int8_t* signs, float* y, void* stream) {
   RowPrepArgs a;
@@ -578,6 +594,14 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     g.num_units = 2 * tiles;
   }
   int grid = (g.num_units < slots ? g.num_units : slots) * (pair ? 2 : 1);
+  // Programmatic dependent launch: the GEMM's set-up (barriers, TMEM,
+  // descriptor prefetch) overlaps the end of the previous kernel in the
+  // stream; every read of operands, scales and epilogue inputs, and every
+  // write, waits for that kernel to complete (grid_dependency_wait).  Measured
+  // after the quantization: 512 rows x K16384 -> N4096 step 50.2 -> 47.8 us,
+  // 4096 rows unchanged.  M5B_GEMM_PDL=0 turns it off (tuning).
+  g.pdl = 1;
+  if (const char* env = std::getenv("M5B_GEMM_PDL")) g.pdl = env[0] == '0' ? 0 : 1;
   if (pair && bn == 256 && g.kind == KIND_I8 && sk_ws &&
       sk_ws_bytes >= splitk_workspace_bytes(slots) && aligned(sk_ws, 256)) {
     const int splits = splitk_factor(tiles, g.num_k_blocks, slots);

@@ -242,6 +242,20 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start before the previous kernel in the stream ends; it
+// must execute grid_dependency_wait() before it reads anything that kernel
+// wrote (or writes anything it reads).  grid_dependents_launch() lets the
+// next such kernel start launching.  Both are no-ops without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Shared-memory address helpers and mbarriers
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -349,6 +363,23 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
       "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
           reinterpret_cast<uint64_t>(map)),
       "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+      : "memory");
+}
+// An L2 cache policy that makes the lines it touches the first to be evicted
+// (streaming data: written once and not read again soon).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+// tma_store_2d with an L2 cache policy (e.g. evict-first for outputs that
+// the next kernel does not read, so they leave L2 while DRAM has headroom).
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, const void* smem_src,
+                                                  int32_t x, int32_t y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint"
+      " [%0, {%2, %3}], [%1], %4;" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() {

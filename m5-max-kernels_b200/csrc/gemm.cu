@@ -456,6 +456,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one()) {
+      // With programmatic dependent launch the set-up above overlapped the
+      // previous kernel; the operands it may have written are read only now.
+      grid_dependency_wait();
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
@@ -593,6 +596,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     };
     // plain epilogues: this warp's two staging buffers and their use count
     uint8_t* out_stage = qk_stage + (warp - 2) * 4096;
+    const uint64_t out_policy = l2_policy_evict_first();
     uint32_t ostage = 0;
     int local = 0;
     long long cur = work_start;
@@ -605,6 +609,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     // walks the same work items, so all of them expect the same counts.
     int sig_expect = 0, stored_expect = 0;
     const bool sk_leader = threadIdx.x == 64;  // lane 0 of the first epilogue warp
+    // scales, bias, gate, residual and the outputs are touched only after the
+    // previous kernel in the stream has completed (programmatic launch)
+    grid_dependency_wait();
     const int prow = quarter * 32 + lane;      // this thread's row within the CTA's 128
     for (; next_work(cur, w); ++local) {
       const int m_blk = w.m_blk, n_col = w.n_col;
@@ -728,7 +735,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             fence_proxy_async_shared();
             __syncwarp();
             if (lane == 0 && row0 < g.M && n_col + c * 32 < g.N) {
-              tma_store_2d(&tmap_out, buf, g.col_off + n_col + c * 32, static_cast<int32_t>(row0));
+              // evict-first: the output is not read by this kernel, and its
+              // write-back then overlaps the MMAs instead of the next kernel
+              tma_store_2d_hint(&tmap_out, buf, g.col_off + n_col + c * 32,
+                                static_cast<int32_t>(row0), out_policy);
               bulk_commit_group();
             }
             if (g.n_peers > 0 && ((c - c_first) & 1)) {
@@ -977,15 +987,22 @@ static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const 
   cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  unsigned n_attr = 0;
   if (PAIR) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[n_attr].id = cudaLaunchAttributeClusterDimension;
+    attr[n_attr].val.clusterDim.x = 2;
+    attr[n_attr].val.clusterDim.y = 1;
+    attr[n_attr].val.clusterDim.z = 1;
+    ++n_attr;
   }
+  if (g.pdl) {  // programmatic dependent launch (see grid_dependency_wait)
+    attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
+    ++n_attr;
+  }
+  cfg.attrs = n_attr ? attr : nullptr;
+  cfg.numAttrs = n_attr;
   e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tbh, to, tok, tov, g);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

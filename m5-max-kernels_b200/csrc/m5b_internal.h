@@ -108,6 +108,10 @@ bool rows16_applicable(const RowPrepArgs& a, int x_dtype, int block, int out);
 cudaError_t launch_rows16(const RowPrepArgs& a, int x_dtype, int block, int out,
                           cudaStream_t stream);
 
+// MXINT8 block quantization of n = rows * K values (K % 32 == 0; mxint8.cu).
+cudaError_t launch_mxint8(const void* x, int x_dtype, int64_t n, void* q, uint8_t* e,
+                          cudaStream_t stream);
+
 // Staged comparators (staged.cu).
 struct GatedAddArgs {
   const void* residual;        // [rows, K]
@@ -186,6 +190,7 @@ struct GemmArgs {
   // two N-halves each (units [num_full, num_units)), which evens out the wave.
   int num_full;
   int num_units;
+  int pdl;                    // launch with programmatic stream serialization
   // Split-K schedule (INT8 CTA-pair GEMMs whose tiles fill at most half of
   // the GPU's CTA pairs, see gemm.cu): CTA pair u works on tile u % sk_tiles
   // over the k-blocks of split u / sk_tiles (sk_splits equal K ranges); the

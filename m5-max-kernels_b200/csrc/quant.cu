@@ -59,6 +59,10 @@ __global__ void __launch_bounds__(NT)
   const int tid = threadIdx.x;
   const int nvec = static_cast<int>(K / V);  // K % V == 0 on this path
   const float qmax = OUT == OUT_E4M3 ? 448.0f : 127.0f;
+  // A GEMM launched after this kernel with programmatic serialization may
+  // begin its set-up now; it waits for this grid's completion before it
+  // reads the codes and scales.
+  grid_dependents_launch();
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
     uint8_t* qr = q + row * K;
@@ -73,7 +77,9 @@ __global__ void __launch_bounds__(NT)
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int j = tid + i * NT;
-        raw[i] = (EXACT || j < nvec) ? __ldg(xr + j) : make_uint4(0, 0, 0, 0);
+        // streaming loads: the activations are read once, and the codes
+        // written here (read next by the GEMM) should keep their L2 lines
+        raw[i] = (EXACT || j < nvec) ? __ldcs(xr + j) : make_uint4(0, 0, 0, 0);
       }
       Peak<T> pk;
 #pragma unroll

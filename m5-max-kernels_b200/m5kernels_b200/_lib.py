@@ -32,6 +32,7 @@ _SIGNATURES = {
     "m5b_last_error": ([], ctypes.c_char_p),
     "m5b_device_status": ([ctypes.POINTER(ctypes.c_uint), I], I),
     "m5b_quantize": ([P, I, I64, I64, I, P, P, P], I),
+    "m5b_quantize_mxint8": ([P, I, I64, I64, P, P, P], I),
     "m5b_rotate": ([P, I, I64, I64, I, P, P, P], I),
     "m5b_hadamard_quantize": ([P, I, I64, I64, I, P, I, P, P, P], I),
     "m5b_fused_norm_hadamard_quantize": (

@@ -29,11 +29,28 @@ def quantize(x: torch.Tensor, mode: str, tag: str = "packed"):
 
     int8: scale = amax/127, codes = clip(rint(x/scale), +-127) (int8).
     fp8:  scale = amax/448, codes = E4M3 bits (uint8), RNE, saturating.
-    All-zero rows use scale 1.  Mirrors src/m5kernels/metal.py:27-44.
+    All-zero rows use scale 1.
+    mxint8: 32-element blocks along each row; returns int8 codes [rows, K] and
+    uint8 E8M0 exponent bytes [rows, K/32]: e = floor(log2(block peak)) - 6
+    (clipped to +-127, 0 for a zero block), codes = clip(rint(x / 2^e), +-127),
+    byte = e + 127.  Mirrors src/m5kernels/metal.py:27-44.
     """
     del tag
     if mode == "mxint8":
-        raise NotImplementedError("MXINT8 packing is not part of the cuda-b200 backend")
+        if x.dim() != 2 or 0 in x.shape:
+            raise ValueError("input must have nonempty shape [rows, K]")
+        if x.shape[1] % 32:
+            raise ValueError("MXINT8 requires K divisible by 32")
+        if x.dtype not in FLOAT_DTYPES:
+            raise ValueError("input dtype must be float16, bfloat16 or float32")
+        dev = _lib.require_cuda(x)
+        x = x.contiguous()
+        rows, k = x.shape
+        q = torch.empty((rows, k), dtype=torch.int8, device=dev)
+        e = torch.empty((rows, k // 32), dtype=torch.uint8, device=dev)
+        check(_lib.lib().m5b_quantize_mxint8(ptr(x), _lib.DTYPE_CODE[x.dtype], rows, k, ptr(q),
+                                             ptr(e), _lib.stream_handle(dev)))
+        return q, e
     if mode not in ("int8", "fp8"):
         raise ValueError(f"unknown quantization mode {mode!r}")
     if x.dim() != 2 or 0 in x.shape:

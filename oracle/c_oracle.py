@@ -106,6 +106,8 @@ def lib() -> ctypes.CDLL:
         _lib.m5o_qk_rope_from_acc.restype = None
         _lib.m5o_rms_quantize.argtypes = [P, I32, P, P, I64, I64, I32, I32, F, P, P]
         _lib.m5o_rms_quantize.restype = None
+        _lib.m5o_quantize_mxint8.argtypes = [P, I32, I64, I64, P, P]
+        _lib.m5o_quantize_mxint8.restype = None
     return _lib
 
 
@@ -159,6 +161,16 @@ def row_prep(x, *, block=0, norm=None, eps=1e-5, round_output=False, out="int8",
 def quantize(x, mode="int8"):
     r = row_prep(x, out=mode)
     return r["q"], r["s"]
+
+
+def quantize_mxint8(x):
+    """MXINT8 restatement: (int8 codes [rows, K], uint8 E8M0 bytes [rows, K/32])."""
+    x = _cpu(x)
+    rows, k = x.shape
+    q = torch.empty((rows, k), dtype=torch.int8)
+    e = torch.empty((rows, k // 32), dtype=torch.uint8)
+    lib().m5o_quantize_mxint8(_ptr(x), _code(x), rows, k, _ptr(q), _ptr(e))
+    return q, e
 
 
 def rotate(x, block, signs=None):
@@ -235,6 +247,6 @@ def row_prep_warps(k: int, block: int) -> int:
 
 
 __all__ = [
-    "build", "build_omp", "omp_projection", "row_prep", "quantize", "rotate", "gemm_i8_acc", "gemm_i8_acc_fast",
+    "build", "build_omp", "omp_projection", "quantize_mxint8", "row_prep", "quantize", "rotate", "gemm_i8_acc", "gemm_i8_acc_fast",
     "gemm_epilogue", "qk_rope_from_acc", "e4m3_encode_scalar", "row_prep_warps", "np",
 ]

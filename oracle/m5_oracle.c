@@ -319,6 +319,41 @@ void m5o_rms_quantize(const void* x, int x_dtype, const float* gamma, const int8
   free(v);
 }
 
+/* ------------------------------------------------------------------ MXINT8 */
+/* 32-element blocks of each row (k % 32 == 0): e = clip(floor(log2(peak)) - 6,
+ * -127, 127) (0 for an all-zero block), q = clip(rint(x / 2^e), +-127),
+ * byte = e + 127 (numerics.py:32-40).  floor(log2(peak)) is the exact binary
+ * exponent of the fp32 peak (frexpf), and x / 2^e an exact power-of-two
+ * scaling (ldexpf). */
+void m5o_quantize_mxint8(const void* x, int x_dtype, int64_t rows, int64_t k, int8_t* q,
+                         uint8_t* ebytes) {
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t b = 0; b < k / 32; ++b) {
+      const int64_t base = r * k + b * 32;
+      float peak = 0.0f;
+      for (int i = 0; i < 32; ++i) {
+        const float v = fabsf(load_elem(x, x_dtype, base + i));
+        if (v > peak) peak = v;
+      }
+      int e = 0;
+      if (peak > 0.0f) {
+        int ex = 0;
+        (void)frexpf(peak, &ex); /* peak = m * 2^ex, m in [0.5, 1) */
+        e = (ex - 1) - 6;
+        if (e < -127) e = -127;
+        if (e > 127) e = 127;
+      }
+      ebytes[r * (k / 32) + b] = (uint8_t)(e + 127);
+      for (int i = 0; i < 32; ++i) {
+        float z = rintf(ldexpf(load_elem(x, x_dtype, base + i), -e));
+        if (z > 127.0f) z = 127.0f;
+        if (z < -127.0f) z = -127.0f;
+        q[base + i] = (int8_t)(int)z;
+      }
+    }
+  }
+}
+
 /* ------------------------------------------------------------------ GEMM */
 /* Exact INT32 accumulators acc[m, n] = sum_k a[m, k] * b[n, k]. */
 void m5o_gemm_i8_acc(const int8_t* a, const int8_t* b, int64_t M, int64_t N, int64_t K,

@@ -115,8 +115,8 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
 def test_python_contract_validation_matches_reference_messages():
     import m5kernels_b200 as m
 
-    with pytest.raises(NotImplementedError):
-        m.quantize(torch.ones(2, 64), "mxint8")
+    with pytest.raises(ValueError, match="divisible by 32"):
+        m.quantize(torch.ones(2, 48), "mxint8")
     with pytest.raises(ValueError, match="nonempty"):
         m.quantize(torch.ones(0, 64), "int8")
     with pytest.raises(ValueError, match="power of two"):
