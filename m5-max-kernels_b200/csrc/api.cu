@@ -557,12 +557,19 @@ static int output_map(CUtensorMap* map, void* out, int out_dtype, int64_t m, int
 // equal K ranges, up to S = 4; INT32 partial sums add exactly, so the result
 // is the data-parallel one bit for bit.  Larger GEMMs keep the data-parallel
 // schedule with its N-halves: at 32 tiles on 74 pairs (512 rows of FFN-down)
-// two pairs per full tile measured 39.0 us against 35.7 us for one pair per
-// N-half.  M5B_GEMM_SPLITK=0 turns it off (tuning and tests).
+// two pairs per full tile finish their MMAs at 22 us against 29 us for one
+// pair per N-half, but moving a 128 KB partial through global memory and
+// adding it costs ~14 us of tail (37.7 against 35.3 us per GEMM); at 16
+// tiles (256 rows) four pairs per tile measured 33.8 against 35.4 us.
+// M5B_GEMM_SPLITK=0 turns it off, =2 extends it to half-filling tile counts
+// (tuning and tests).
 static int splitk_factor(int tiles, int nkb, int slots) {
-  if (tiles <= 0 || 4 * tiles > slots) return 0;
-  if (const char* force = std::getenv("M5B_GEMM_SPLITK"))
+  int fill = 4;  // tiles fill at most 1/fill of the pairs
+  if (const char* force = std::getenv("M5B_GEMM_SPLITK")) {
     if (force[0] == '0') return 0;
+    if (force[0] == '2') fill = 2;  // also up to half of the pairs (tuning)
+  }
+  if (tiles <= 0 || fill * tiles > slots) return 0;
   int s = slots / tiles;
   if (s > kSplitKMaxSplits) s = kSplitKMaxSplits;
   while (s >= 2 && nkb / s < kSplitKMinBlocks) --s;

@@ -57,7 +57,7 @@ struct GemmCfg {
   // (Q/K pair tiles: 5 stages beside their 64 KB of staging.)
   static constexpr int STAGES = QK ? 5 : (STAGE_BYTES <= 32 * 1024 ? 6 : 4);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 32;
+  static constexpr int BAR_BYTES = (2 * STAGES + 6) * 8 + 32;
   // Epilogue warps: 4, or 8 for pair tiles (each warp drains one of the tile's
   // two heads (Q/K), or half of its columns, for its 32 rows).
   static constexpr int EPI_WARPS = PAIR ? 8 : 4;
@@ -282,28 +282,6 @@ __device__ __forceinline__ uint4* sk_slot(const GemmArgs& g, int u, uint32_t ran
   constexpr int kSlotU4 = kBM * BN * 4 / 16;
   return g.sk_part + static_cast<size_t>(u * 2 + static_cast<int>(rank)) * kSlotU4;
 }
-// r += the partial sums of 32-column chunk `chunk` (row prow of this CTA)
-// stored by the other pairs of tile `tile` (pairs tile + s*T, s != the
-// caller's split).  INT32 addition is exact, so the order does not matter.
-template <int BN>
-__device__ __forceinline__ void sk_add_partials(const GemmArgs& g, uint32_t (&r)[32], int chunk,
-                                                int prow, uint32_t rank, int self, int tile) {
-  for (int s = 0; s < g.sk_splits; ++s) {
-    const int v = tile + s * g.sk_tiles;
-    if (v == self) continue;
-    const uint4* src = sk_slot<BN>(g, v, rank) + chunk * 8 * kBM + prow;
-    uint4 p[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) p[q] = __ldcg(src + q * kBM);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      r[4 * q] += p[q].x;
-      r[4 * q + 1] += p[q].y;
-      r[4 * q + 2] += p[q].z;
-      r[4 * q + 3] += p[q].w;
-    }
-  }
-}
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -350,7 +328,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* fix_bar = drain + 1;  // split-K: partner partial sums landed in shared memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fix_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // split-K hand-offs between the epilogue warps of this CTA (see below)
   volatile int* sk_ticket = reinterpret_cast<volatile int*>(tmem_slot + 2);
@@ -374,6 +353,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
       mbar_init(&acc_empty[a], (PAIR ? 2 : 1) * Cfg::EPI_WARPS);
     }
     mbar_init(drain, 1);
+    mbar_init(fix_bar, 1);
     *abort_flag = 0;
     *sk_ticket = 0;
     *sk_signal = 0;
@@ -608,6 +588,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     // sk_stored counts warps whose partial stores are complete.  Every warp
     // walks the same work items, so all of them expect the same counts.
     int sig_expect = 0, stored_expect = 0;
+    uint32_t fix_phase = 0;
     const bool sk_leader = threadIdx.x == 64;  // lane 0 of the first epilogue warp
     // scales, bias, gate, residual and the outputs are touched only after the
     // previous kernel in the stream has completed (programmatic launch)
@@ -627,77 +608,120 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const float sa = (g.quantized && row < g.M) ? __ldg(g.a_scales + row) : 1.0f;
-      // Split-K: the S pairs of a tile each take an arrival ticket per CTA;
-      // all but the last store their INT32 partial sums and count them done;
-      // the last waits (bounded) until the others' stores are done, resets
-      // the counters and adds the partials to its own accumulator chunk by
-      // chunk before the ordinary epilogue.
-      bool fixup = false;
+      // Split-K: the S pairs of a tile each take an arrival ticket per CTA.
+      // All but the last stage their INT32 partial sums in the (now idle)
+      // operand ring, store them to their workspace slot with one bulk copy
+      // and count them done.  The last waits (bounded) until the others are
+      // done, resets the counters, and for each partner bulk-loads its slot
+      // into the ring and adds it into its own TMEM accumulator; the ordinary
+      // epilogue then reads complete sums.  (All of this CTA's MMAs have
+      // retired once acc_full completed, so the ring's 192 KB are free.)
       if (sk) {
         const int others = g.sk_splits - 1;
-        {
-          int* ctr = g.sk_ctr + (w.tile * 2 + static_cast<int>(rank)) * 2;
-          ++sig_expect;
-          if (sk_leader) {
-            *sk_ticket = atomicAdd(ctr, 1);
-            __threadfence_block();
-            *sk_signal = sig_expect;
-          }
-          if (lane == 0) spin_shared_at_least(sk_signal, sig_expect, abort_flag, g.status);
-          __syncwarp();
-          const int ticket = *sk_ticket;
-          if (ticket < others) {
-            uint4* dst = sk_slot<BN>(g, unit, rank) + prow;
-            constexpr int kChunks = BN / 32;
-            const int c_first = Cfg::EPI_WARPS == 8 ? ehalf * (kChunks / 2) : 0;
-            const int c_end = Cfg::EPI_WARPS == 8 ? c_first + kChunks / 2 : kChunks;
-#pragma unroll 1
-            for (int c = c_first; c < c_end; ++c) {
-              uint32_t r[32];
-              tmem_ld32(taddr + c * 32, r);
-              tmem_wait_ld();
-              if (c == c_end - 1) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) release_acc(acc);
-              }
-#pragma unroll
-              for (int q = 0; q < 8; ++q)
-                dst[(c * 8 + q) * kBM] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
-            }
-            __threadfence();
-            __syncwarp();
-            stored_expect += Cfg::EPI_WARPS;
-            if (lane == 0) atomicAdd(sk_stored, 1);
-            if (sk_leader) {
-              spin_shared_at_least(sk_stored, stored_expect, abort_flag, g.status);
-              __threadfence();
-              atomicAdd(ctr + 1, 1);
-            }
-            __syncwarp();
-            continue;
-          }
-          ++sig_expect;
-          if (sk_leader) {
-            const unsigned long long start = globaltimer_ns();
-            while (ld_acquire_gpu(ctr + 1) < others) {
-              if (*abort_flag) break;
-              if (globaltimer_ns() - start > kWaitLimitNs) {
-                atomicOr(g.status, DEV_TIMEOUT_FIXUP);
-                *abort_flag = 1;
-                break;
-              }
-            }
-            ctr[0] = 0;  // zero again for the next launch
-            ctr[1] = 0;
-            __threadfence();
-            *sk_signal = sig_expect;
-          }
-          if (lane == 0) spin_shared_at_least(sk_signal, sig_expect, abort_flag, g.status);
-          __syncwarp();
-          __threadfence();
-          fixup = true;
+        int* ctr = g.sk_ctr + (w.tile * 2 + static_cast<int>(rank)) * 2;
+        uint4* ring = reinterpret_cast<uint4*>(smem);  // [chunk][4 words][row] uint4
+        constexpr int kChunks = BN / 32;
+        const int c_first = Cfg::EPI_WARPS == 8 ? ehalf * (kChunks / 2) : 0;
+        const int c_end = Cfg::EPI_WARPS == 8 ? c_first + kChunks / 2 : kChunks;
+        constexpr uint32_t kSlotBytes = kBM * BN * 4;
+        ++sig_expect;
+        if (sk_leader) {
+          *sk_ticket = atomicAdd(ctr, 1);
+          __threadfence_block();
+          *sk_signal = sig_expect;
         }
+        if (lane == 0) spin_shared_at_least(sk_signal, sig_expect, abort_flag, g.status);
+        __syncwarp();
+        const int ticket = *sk_ticket;
+        if (ticket < others) {
+#pragma unroll 1
+          for (int c = c_first; c < c_end; ++c) {
+            uint32_t r[32];
+            tmem_ld32(taddr + c * 32, r);
+            tmem_wait_ld();
+            if (c == c_end - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) release_acc(acc);
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              ring[(c * 8 + q) * kBM + prow] =
+                  make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          }
+          fence_proxy_async_shared();  // the bulk copy (async proxy) reads these writes
+          __syncwarp();
+          stored_expect += Cfg::EPI_WARPS;
+          if (lane == 0) atomicAdd(sk_stored, 1);
+          if (sk_leader) {
+            spin_shared_at_least(sk_stored, stored_expect, abort_flag, g.status);
+            bulk_store_s2g(sk_slot<BN>(g, unit, rank), ring, kSlotBytes);
+            bulk_commit_group();
+            bulk_wait_group0();        // the partial sums are in global memory
+            fence_proxy_async_global();
+            __threadfence();
+            atomicAdd(ctr + 1, 1);
+          }
+          __syncwarp();
+          continue;
+        }
+        ++sig_expect;
+        if (sk_leader) {
+          const unsigned long long start = globaltimer_ns();
+          while (ld_acquire_gpu(ctr + 1) < others) {
+            if (*abort_flag) break;
+            if (globaltimer_ns() - start > kWaitLimitNs) {
+              atomicOr(g.status, DEV_TIMEOUT_FIXUP);
+              *abort_flag = 1;
+              break;
+            }
+          }
+          ctr[0] = 0;  // zero again for the next launch
+          ctr[1] = 0;
+          __threadfence();
+          fence_proxy_async_global();  // the partners' slots are read by bulk copies
+          *sk_signal = sig_expect;
+        }
+        if (lane == 0) spin_shared_at_least(sk_signal, sig_expect, abort_flag, g.status);
+        __syncwarp();
+        for (int s = 0; s < g.sk_splits; ++s) {
+          const int v = w.tile + s * g.sk_tiles;
+          if (v == unit) continue;
+          if (sk_leader) {
+            mbar_arrive_expect_tx(fix_bar, kSlotBytes);
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(sk_slot<BN>(g, v, rank));
+            for (uint32_t off = 0; off < kSlotBytes; off += 16384)
+              bulk_load_g2s(reinterpret_cast<uint8_t*>(ring) + off, src + off, 16384, fix_bar);
+          }
+          if (!mbar_wait_bounded(fix_bar, fix_phase, abort_flag, g.status, DEV_TIMEOUT_FIXUP))
+            break;
+          fix_phase ^= 1u;
+#pragma unroll 1
+          for (int c = c_first; c < c_end; ++c) {
+            uint32_t r[32];
+            tmem_ld32(taddr + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint4 pv = ring[(c * 8 + q) * kBM + prow];
+              r[4 * q] += pv.x;
+              r[4 * q + 1] += pv.y;
+              r[4 * q + 2] += pv.z;
+              r[4 * q + 3] += pv.w;
+            }
+            tmem_st32(taddr + c * 32, r);
+            tmem_wait_st();
+          }
+          // every warp has read the ring before the next partner's copy lands
+          __syncwarp();
+          stored_expect += Cfg::EPI_WARPS;
+          if (lane == 0) atomicAdd(sk_stored, 1);
+          if (lane == 0) spin_shared_at_least(sk_stored, stored_expect, abort_flag, g.status);
+          __syncwarp();
+        }
+        tc_fence_before();
+        __syncwarp();
+        tc_fence_after();
       }
       if constexpr (!QK) {
         // This warp's 32-column chunks: all of the tile's, or with 8 warps
@@ -714,7 +738,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             uint32_t r[32];
             tmem_ld32(taddr + c * 32, r);
             tmem_wait_ld();
-            if (fixup) sk_add_partials<BN>(g, r, c, prow, rank, unit, w.tile);
             if (c == c_end - 1) {  // the accumulator is drained: hand it back
               tc_fence_before();
               __syncwarp();
@@ -777,7 +800,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             uint32_t r[32];
             tmem_ld32(taddr + c * 32, r);
             tmem_wait_ld();
-            if (fixup) sk_add_partials<BN>(g, r, c, prow, rank, unit, w.tile);
             epilogue_chunk<KIND>(g, r, row, n_col + c * 32, sa);
           }
           tc_fence_before();
@@ -852,7 +874,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
             uint32_t r[32];
             tmem_ld32(taddr + hh * 128 + c * 32, r);
             tmem_wait_ld();
-            if (fixup) sk_add_partials<BN>(g, r, hh * 4 + c, prow, rank, unit, w.tile);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               uint32_t pk[4];
