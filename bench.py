@@ -46,9 +46,9 @@ WORKLOAD = "ffn_down_w8a8_online_quant_M4096_K16384_N4096"
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
 # the GEMM kernel, from ncu captures of this workload's per-rank shapes
 # (rows per rank -> bytes).  Recorded constants, not measured by this script.
-GEMM_TRAFFIC_BYTES = {4096: 342205184}
-GEMM_TRAFFIC_SOURCE = ("ncu capture (--set full, 1 launch) of gemm_tc_kernel<i8,256,pair> on the "
-                       "per-rank shape; recorded constant")
+GEMM_TRAFFIC_BYTES = {4096: 315609088 + 24830976, 512: 75607552 + 3584512}
+GEMM_TRAFFIC_SOURCE = ("ncu capture (1 launch, dram__bytes_read.sum + dram__bytes_write.sum) of "
+                       "gemm_tc_kernel<i8,256,pair> on the per-rank shape; recorded constant")
 
 
 def _peaks():
@@ -682,11 +682,32 @@ def run_b200(args, world, rank, local):
         return a0.elapsed_time(a1)
 
     graph = graph_of(lambda st: st())
+    # Kernel durations for the roofline: the same K steps replayed once more
+    # right after the timed region, now with CUDA events recorded between the
+    # kernels (event nodes inside the graph; they lengthen each kernel's
+    # interval by their own latency, which is why the headline replay has
+    # none).  Without event nodes in graphs, each kernel's K launches alone.
+    kernel_timing = ("CUDA events between the kernels in a second replay of the same K steps "
+                     "right after the timed region")
+    ev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+          for _ in range(K_steps)]
+    graph_ev = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(graph_ev):
+            for i in range(K_steps):
+                st = steps_sets[i % nsets]
+                ev[i][0].record()
+                st.quantize()
+                ev[i][1].record()
+                st.gemm()
+                ev[i][2].record()
+        graph_ev.replay()
+        torch.cuda.synchronize()
+    except Exception:
+        graph_ev = None
+        kernel_timing = ("each kernel's K launches alone as a CUDA graph, CUDA events around the "
+                         "replay, right after the timed region")
     barrier()
-    # Kernel durations for the roofline: the same K launches of each kernel
-    # alone, replayed as a graph right after the timed region.
-    kernel_timing = ("each kernel's K launches alone as a CUDA graph, CUDA events around the "
-                     "replay, right after the timed region")
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -701,12 +722,19 @@ def run_b200(args, world, rank, local):
         barrier()
         ms_total = e0.elapsed_time(e1)
         del graph
-        g_prep = graph_of(lambda st: st.quantize())
-        prep_ms = replay_ms(g_prep) / K_steps
-        del g_prep
-        g_gemm = graph_of(lambda st: st.gemm())
-        gemm_ms = replay_ms(g_gemm) / K_steps
-        del g_gemm
+        if graph_ev is not None:
+            graph_ev.replay()
+            torch.cuda.synchronize()
+            prep_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / K_steps
+            gemm_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / K_steps
+            del graph_ev
+        else:
+            g_prep = graph_of(lambda st: st.quantize())
+            prep_ms = replay_ms(g_prep) / K_steps
+            del g_prep
+            g_gemm = graph_of(lambda st: st.gemm())
+            gemm_ms = replay_ms(g_gemm) / K_steps
+            del g_gemm
         ms_per_step = max_over_ranks(ms_total / K_steps)
         prep_ms_max = max_over_ranks(prep_ms)
         gemm_ms_max = max_over_ranks(gemm_ms)
