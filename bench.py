@@ -215,20 +215,34 @@ def cpu_reference(steps: int, warmup: int, budget_s: float = 150.0):
         ref.bf16_round_reference(y)
         return time.perf_counter() - t0
 
-    for _ in range(max(warmup, 1)):
-        t64 = one(64)
-    est_full = t64 * M / 64
-    steps = max(steps, 1)
-    rows = M if steps * est_full <= budget_s else max(64, int(M * budget_s / (steps * est_full)))
-    times = [one(rows) for _ in range(steps)]
+    # every host thread this process may run on, whatever OMP_NUM_THREADS the
+    # launcher set (torchrun sets 1 for multi-rank jobs)
+    ncores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    try:
+        from threadpoolctl import threadpool_limits
+
+        pool = threadpool_limits(limits=ncores, user_api="blas")
+    except Exception:
+        pool = None
+    try:
+        for _ in range(max(warmup, 1)):
+            t64 = one(64)
+        est_full = t64 * M / 64
+        steps = max(steps, 1)
+        rows = M if steps * est_full <= budget_s else max(64, int(M * budget_s / (steps * est_full)))
+        times = [one(rows) for _ in range(steps)]
+        threads = _thread_env()
+    finally:
+        if pool is not None:
+            pool.unregister()
     per = statistics.median(times)
     tops = 2.0 * rows * N * K / per / 1e12
-    return {"value": tops, "unit": "TOPS", "cores": os.cpu_count() or 1, "kind": "port",
+    return {"value": tops, "unit": "TOPS", "cores": ncores, "kind": "port",
             "sample": (f"{rows} of {M} activation rows per timed step, {steps} timed steps "
                        f"(median), {max(warmup, 1)} warm-up steps of 64 rows; FFN-down K={K}, "
                        f"N={N}; NumPy float32 quantize_reference + float64 BLAS decoded GEMM"),
             "rows_per_step": rows, "seconds_per_step": per, "steps_timed": steps,
-            "threads": _thread_env()}
+            "threads": threads}
 
 
 def cpu_omp_baseline(target_s: float = 8.0):

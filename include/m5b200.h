@@ -216,6 +216,20 @@ M5B_API int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t
  * pair). */
 M5B_API int64_t m5b_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int mode);
 
+/* GEMM schedule for the calling host thread, the B200 counterpart of the
+ * reference's per-call Metal tile (src/m5kernels/metal.py:158-166 `tile`,
+ * swept by `m5bench tune`, src/m5kernels/cli.py:66-151).  It changes how
+ * the work is scheduled, never the result (outputs are bit-identical under
+ * every schedule).  split_k: -1 the library's rule, 0 data-parallel,
+ * 2..4 that many CTA pairs per 256 x 256 tile over equal K ranges -- taken
+ * by INT8 CTA-pair GEMMs given a workspace when all tiles x splits fit on the
+ * GPU at once and each split keeps >= 8 k-blocks, else data-parallel.
+ * group_m: 0 the library's raster, else M-blocks walked per N-block group.
+ * Every GEMM entry point called later from this thread uses it (also
+ * m5b_gemm_workspace_bytes) until (-1, 0) restores the defaults.  No
+ * counterpart in the reference's C-level API: its tile is a call argument. */
+M5B_API int m5b_gemm_set_schedule(int split_k, int group_m);
+
 /* m5b_gemm with a workspace for the split-K schedule (NULL / 0: data-
  * parallel only, exactly m5b_gemm).  The workspace must be 256-byte aligned
  * and all zero before its first use (cudaMemset once after allocating it);

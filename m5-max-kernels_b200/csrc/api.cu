@@ -477,6 +477,16 @@ static bool use_pair(int epi, int64_t m, int64_t n) {
   return m >= 256 && (epi == EPI_QK ? n >= 256 : n > 128);
 }
 
+// GEMM schedule of the calling host thread (m5b_gemm_set_schedule): split_k
+// -1 = the library's rule, 0 = data-parallel, 2..kSplitKMaxSplits = that
+// split-K factor where it applies; group_m 0 = the library's raster group,
+// else M-blocks per group.
+struct ScheduleOverride {
+  int split_k = -1;
+  int group_m = 0;
+};
+static thread_local ScheduleOverride tl_schedule;
+
 static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMap& tbh,
                        const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
                        int bn, bool pair) {
@@ -529,6 +539,7 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMa
   const int64_t a_block_bytes = int64_t(tile_m) * k * eb;
   int64_t group = (48ll << 20) / (a_block_bytes > 0 ? a_block_bytes : 1);
   if (const char* env = std::getenv("M5B_GEMM_GROUP_M")) group = std::atoi(env);
+  if (tl_schedule.group_m > 0) group = tl_schedule.group_m;
   if (group < 1) group = 1;
   if (group > g.num_m_blocks) group = g.num_m_blocks;
   g.group_m = static_cast<int>(group);
@@ -563,7 +574,16 @@ static int output_map(CUtensorMap* map, void* out, int out_dtype, int64_t m, int
 // tiles (256 rows) four pairs per tile measured 33.8 against 35.4 us.
 // M5B_GEMM_SPLITK=0 turns it off, =2 extends it to half-filling tile counts
 // (tuning and tests).
+// A factor set by m5b_gemm_set_schedule applies when all T x S units are
+// resident at once (T x S <= slots) and every split keeps kSplitKMinBlocks
+// k-blocks; otherwise the GEMM runs data-parallel.
 static int splitk_factor(int tiles, int nkb, int slots) {
+  if (tl_schedule.split_k == 0) return 0;
+  if (tl_schedule.split_k >= 2) {
+    const int s = tl_schedule.split_k;
+    if (tiles <= 0 || int64_t(tiles) * s > slots || nkb / s < kSplitKMinBlocks) return 0;
+    return s;
+  }
   int fill = 4;  // tiles fill at most 1/fill of the pairs
   if (const char* force = std::getenv("M5B_GEMM_SPLITK")) {
     if (force[0] == '0') return 0;
@@ -627,6 +647,15 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   cudaError_t e = launch_gemm(ta, tb, tbh, o, to_k ? *to_k : o, to_v ? *to_v : o, g, bn, grid,
                               pair, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
+  return ok();
+}
+
+int m5b_gemm_set_schedule(int split_k, int group_m) {
+  if (split_k < -1 || split_k == 1 || split_k > kSplitKMaxSplits)
+    return fail(M5B_EINVAL, "split_k must be -1 (library rule), 0 or 2..%d", kSplitKMaxSplits);
+  if (group_m < 0) return fail(M5B_EINVAL, "group_m must be >= 0");
+  tl_schedule.split_k = split_k;
+  tl_schedule.group_m = group_m;
   return ok();
 }
 

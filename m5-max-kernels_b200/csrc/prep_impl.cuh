@@ -30,12 +30,12 @@
 // elements [64 t, 64 t + 64) of the row, held in registers.  Hence Hadamard
 // strides 1..32 are register butterflies and strides 64..B/2 are warp
 // shuffles (lane xor 1 .. B/128).  Row reductions have one canonical order,
-// mirrored by the C oracle: within a chunk, eight accumulators a[e] collect
-// elements e, e+8, ..., e+56 in order and combine pairwise
-// ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)); lanes combine with a xor butterfly of
-// increasing offset (1, 2, 4, 8, 16 — a pairwise tree over chunk index);
-// warps combine pairwise in index order (w0+w1, w2+w3, ... then pairs of
-// pairs).
+// mirrored by the C oracle and independent of the schedule: the row is cut
+// into 16-element chunks, each summed by chunk16_sum (eight pairs, combined
+// pairwise), and the chunk sums combine as a pairwise tree over chunk index
+// (zero chunks pad the tree), the total finally added to +0.  Here a thread
+// sums its four chunks pairwise, lanes continue the tree with a xor butterfly
+// of increasing offset (1, 2, 4, 8, 16) and warps pairwise in index order.
 #pragma once
 #include "common.cuh"
 #include "m5b_internal.h"
@@ -214,31 +214,47 @@ __device__ __forceinline__ void param8(const void* base, int dtype, int64_t j, b
 }
 
 // ---------------------------------------------------------------- reductions
-// Canonical chunk sum: eight interleaved accumulators, combined pairwise.
+// Canonical sum of one 16-element chunk given as eight pairs p_k = (u_2k,
+// u_2k+1): SQUARE false sums u, true sums u*u.  Pairs combine as
+// p_2j + p_2j+1 (squares: fma(p_2j, p_2j, p_2j+1 * p_2j+1)), then
+// (l_0 + l_1) + (l_2 + l_3), on both halves at once; the chunk is the even
+// half plus the odd half.
+template <bool SQUARE>
+__device__ __forceinline__ float chunk16_sum(const float2* p) {
+  float2 l[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if constexpr (SQUARE)
+      l[j] = __ffma2_rn(p[2 * j], p[2 * j], __fmul2_rn(p[2 * j + 1], p[2 * j + 1]));
+    else
+      l[j] = __fadd2_rn(p[2 * j], p[2 * j + 1]);
+  }
+  const float2 t = __fadd2_rn(__fadd2_rn(l[0], l[1]), __fadd2_rn(l[2], l[3]));
+  return __fadd_rn(t.x, t.y);
+}
+
+// Canonical sum over a thread's 64-element chunk: its four 16-element chunks
+// (elements past cnt count as zero) combined pairwise.  KIND 0: sum v,
+// 1: sum v*v, 2: sum (v-mean)^2.
 template <int KIND>  // 0: sum v, 1: sum v*v, 2: sum (v-mean)^2
 __device__ __forceinline__ float chunk_sum(const float* v, int cnt, float mean) {
-  float a[8];
+  float c[4];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) a[e] = 0.0f;
+  for (int i = 0; i < 4; ++i) {
+    float2 p[8];
 #pragma unroll
-  for (int i = 0; i < 64; i += 8) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (i + e < cnt) {
-        const float x = v[i + e];
-        if constexpr (KIND == 0) {
-          a[e] = __fadd_rn(a[e], x);
-        } else if constexpr (KIND == 1) {
-          a[e] = __fmaf_rn(x, x, a[e]);
-        } else {
-          const float d = __fsub_rn(x, mean);
-          a[e] = __fmaf_rn(d, d, a[e]);
-        }
+    for (int k = 0; k < 8; ++k) {
+      const int e = 16 * i + 2 * k;
+      float x0 = e < cnt ? v[e] : 0.0f, x1 = e + 1 < cnt ? v[e + 1] : 0.0f;
+      if constexpr (KIND == 2) {
+        x0 = e < cnt ? __fsub_rn(x0, mean) : 0.0f;
+        x1 = e + 1 < cnt ? __fsub_rn(x1, mean) : 0.0f;
       }
+      p[k] = make_float2(x0, x1);
     }
+    c[i] = chunk16_sum<KIND != 0>(p);
   }
-  return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
-                   __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
+  return __fadd_rn(__fadd_rn(c[0], c[1]), __fadd_rn(c[2], c[3]));
 }
 
 // max |v| over a chunk as a balanced tree (exact in any order)
@@ -273,7 +289,7 @@ __device__ __forceinline__ float cta_sum(float v, float* red, int W) {
 #pragma unroll
     for (int w = 0; w + step < 16; w += 2 * step) part[w] = __fadd_rn(part[w], part[w + step]);
   __syncthreads();
-  return part[0];
+  return __fadd_rn(part[0], 0.0f);
 }
 
 __device__ __forceinline__ float cta_max(float v, float* red, int W) {
@@ -310,7 +326,7 @@ __device__ __forceinline__ float2 cta_sum_max(float v, float m, float* red, floa
   float t = red_max[0];
   for (int w = 1; w < W; ++w) t = fmaxf(t, red_max[w]);
   __syncthreads();
-  return make_float2(part[0], t);
+  return make_float2(__fadd_rn(part[0], 0.0f), t);
 }
 
 // ---------------------------------------------------------------- TMA row tiles

@@ -216,32 +216,25 @@ __device__ __forceinline__ void store8(T* dst, const float2* v) {
   }
 }
 
-// Canonical chunk sum on pairs: accumulators a[e] (element e mod 8) held as
-// four packed pairs, elements added in index order, combined
-// ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)).  KIND 0: v, 1: v*v, 2: (v-mean)^2.
+// Canonical sum over a 64-element chunk held as 32 pairs: its four
+// 16-element chunks (chunk16_sum) combined pairwise.  KIND 0: v, 1: v*v,
+// 2: (v-mean)^2.
 template <int KIND>
 __device__ __forceinline__ float chunk_sum2(const float2* v, float mean) {
-  float2 A[4];
-#pragma unroll
-  for (int p = 0; p < 4; ++p) A[p] = f2(0.0f);
+  float c[4];
   const float2 nm = f2(-mean);
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (KIND == 2) {
+      float2 d[8];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const float2 x = v[4 * q + p];
-      if constexpr (KIND == 0) {
-        A[p] = __fadd2_rn(A[p], x);
-      } else if constexpr (KIND == 1) {
-        A[p] = __ffma2_rn(x, x, A[p]);
-      } else {
-        const float2 d = __fadd2_rn(x, nm);
-        A[p] = __ffma2_rn(d, d, A[p]);
-      }
+      for (int k = 0; k < 8; ++k) d[k] = __fadd2_rn(v[8 * i + k], nm);
+      c[i] = chunk16_sum<true>(d);
+    } else {
+      c[i] = chunk16_sum<KIND == 1>(v + 8 * i);
     }
   }
-  return __fadd_rn(__fadd_rn(__fadd_rn(A[0].x, A[0].y), __fadd_rn(A[1].x, A[1].y)),
-                   __fadd_rn(__fadd_rn(A[2].x, A[2].y), __fadd_rn(A[3].x, A[3].y)));
+  return __fadd_rn(__fadd_rn(c[0], c[1]), __fadd_rn(c[2], c[3]));
 }
 
 // Pipeline units: a unit is max(K/64, 32) threads working on RPU = unit / (K/64)
@@ -298,8 +291,9 @@ __global__ void __launch_bounds__(kThreads, MODE == kPlain ? 2 : 1)
     else
       named_sync(1 + u, PW);
   };
-  // Canonical row sum: lanes as a pairwise tree over chunk index, then the
-  // unit's warps pairwise in index order.  Also a unit barrier.
+  // Canonical row sum: lanes continue the pairwise tree over chunk index,
+  // then the unit's warps pairwise in index order, the total added to +0.
+  // Also a unit barrier.
   auto unit_sum = [&](float v, float* buf) -> float {
     const int span = tpr < 32 ? tpr : 32;
 #pragma unroll
@@ -319,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, MODE == kPlain ? 2 : 1)
           part[w] = __fadd_rn(part[w], part[w + step]);
       v = part[0];
     }
-    return v;
+    return __fadd_rn(v, 0.0f);
   };
 
   if (tid == 0) {

@@ -9,20 +9,19 @@
 //     the next row's loads are issued before the current row is computed;
 //     one row per CTA (K / 16 threads), at most 64 registers per thread
 //     (four 256-thread CTAs per SM for K = 4096).
-//   * the canonical chunk of 64 elements ([64 t, 64 t + 64), eight
-//     accumulators a[e] taking elements e, e + 8, ..., e + 56 in order) spans
-//     the four threads of a quad: the accumulators pass down the quad with
-//     shuffles, each thread adding its elements in order, so every chunk sum
-//     is the one a thread holding the whole chunk computes.  Lanes then
-//     combine chunks with a xor tree (chunk index bits 0-2 are lane bits
-//     2-4), warps in fours (a 2048-element "old warp" of the canonical tree)
-//     and those pairwise, padded to 16 with zeros.
+//   * a thread's 16 elements are one chunk of the canonical reduction tree
+//     (chunk16_sum); lanes continue the pairwise tree over chunk index with a
+//     xor butterfly, and the warps' partials combine pairwise (padded to 16).
+//     LayerNorm keeps the centered values x - mean of its second pass for the
+//     normalization, and divides by K as a multiply when K is a power of two
+//     (the same correctly rounded quotient).
 //   * Hadamard strides 1-8 are register butterflies on packed pairs, strides
 //     16-512 shuffles (lane xor 1, 2, 4, 8, 16), so B <= 512.
 //   * modulation / gate / gamma slices are per-thread data (a thread always
 //     handles the same 16 columns); they are kept in shared memory in a
-//     conflict-free per-thread layout and reloaded only when the row's table
-//     index changes.
+//     conflict-free per-thread layout (the modulation's 1 + scale and shift
+//     as fp32, ready to use) and reloaded only when the row's table index
+//     changes.
 // Modes: plain rotation (+ quantization), norm + AdaLN (+ gated residual),
 // RMS scale folding (folded / direct); 16-bit inputs.
 #pragma once
@@ -59,16 +58,38 @@ __device__ __forceinline__ Raw16 ld_raw_stream(const void* p) {
   return r;
 }
 
+// The two 16-bit values of a word of T, as floats.
+template <typename T>
+__device__ __forceinline__ float2 word_pair(uint32_t x) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    return make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xFFFF0000u));
+  else
+    return __half22float2(*reinterpret_cast<const __half2*>(&x));
+}
+
+// a * b + c for the two 16-bit values of the words a and b (lane-wise), with
+// fp32 c: sm_100's mixed-precision FMA, one rounding -- the same value as
+// fmaf(float(a), float(b), c) -- without unpacking a and b first.
+template <typename T>
+__device__ __forceinline__ float2 fma_words16(uint32_t a, uint32_t b, float2 c) {
+  float2 d;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    asm("{\n.reg .b16 al, ah, bl, bh;\nmov.b32 {al, ah}, %2;\nmov.b32 {bl, bh}, %3;\n"
+        "fma.rn.f32.bf16 %0, al, bl, %4;\nfma.rn.f32.bf16 %1, ah, bh, %5;\n}"
+        : "=f"(d.x), "=f"(d.y) : "r"(a), "r"(b), "f"(c.x), "f"(c.y));
+  else
+    asm("{\n.reg .b16 al, ah, bl, bh;\nmov.b32 {al, ah}, %2;\nmov.b32 {bl, bh}, %3;\n"
+        "fma.rn.f32.f16 %0, al, bl, %4;\nfma.rn.f32.f16 %1, ah, bh, %5;\n}"
+        : "=f"(d.x), "=f"(d.y) : "r"(a), "r"(b), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 // Pair k (elements 2k, 2k+1) of a Raw16 of T, as floats.
 template <typename T>
 __device__ __forceinline__ float2 pair_of(const Raw16& r, int k) {
   const uint4& w = k < 4 ? r.lo : r.hi;
   const int i = k & 3;
-  const uint32_t x = i == 0 ? w.x : i == 1 ? w.y : i == 2 ? w.z : w.w;
-  if constexpr (std::is_same<T, __nv_bfloat16>::value)
-    return make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xFFFF0000u));
-  else
-    return __half22float2(*reinterpret_cast<const __half2*>(&x));
+  return word_pair<T>(i == 0 ? w.x : i == 1 ? w.y : i == 2 ? w.z : w.w);
 }
 
 template <typename T>
@@ -111,126 +132,76 @@ __device__ __forceinline__ uint4* tslot(uint8_t* base, int nthreads, int t, int 
 }
 
 // ---------------------------------------------------------------- reductions
-// Canonical chunk sum of the quad's 64 elements (see the header comment):
-// KIND 0 sum v, 1 sum v*v, 2 sum (v - mean)^2.  Every lane of the quad gets
-// the chunk's sum; lanes past the row get 0.
-template <int KIND>
-__device__ __forceinline__ float quad_chunk_sum(const float2* v, float mean, int q, int lane,
-                                                bool have) {
-  float2 A[4];
-#pragma unroll
-  for (int p = 0; p < 4; ++p) A[p] = f2(0.0f);
-  const float2 nm = f2(-mean);
-  // Branch-free: every lane adds its elements at every stage, but only lane
-  // q == s holds the chain's accumulators at stage s (the others' results are
-  // replaced by the shuffle that follows), so the chain is unchanged.
-#pragma unroll
-  for (int s = 0; s < 4; ++s) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const float2 x = v[4 * h + p];
-        if constexpr (KIND == 0) {
-          A[p] = __fadd2_rn(A[p], x);
-        } else if constexpr (KIND == 1) {
-          A[p] = __ffma2_rn(x, x, A[p]);
-        } else {
-          const float2 d = __fadd2_rn(x, nm);
-          A[p] = __ffma2_rn(d, d, A[p]);
-        }
-      }
-    }
-    if (s < 3) {  // hand the accumulators to the next thread of the quad
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        A[p].x = __shfl_up_sync(kFull, A[p].x, 1);
-        A[p].y = __shfl_up_sync(kFull, A[p].y, 1);
-      }
-    }
-  }
-  float c = __fadd_rn(__fadd_rn(__fadd_rn(A[0].x, A[0].y), __fadd_rn(A[1].x, A[1].y)),
-                      __fadd_rn(__fadd_rn(A[2].x, A[2].y), __fadd_rn(A[3].x, A[3].y)));
-  c = __shfl_sync(kFull, c, lane | 3);
-  return have ? c : 0.0f;
-}
-
-// Row total of per-quad chunk sums in the canonical tree.  `part` holds one
-// float per warp (this reduction's own buffer); one CTA barrier.  After the
-// barrier lane l forms old warp l's sum (four new warps, pairwise) and the
-// sixteen old-warp sums (zero-padded) are combined pairwise by a xor
-// butterfly over lanes 0-15 -- the same pairing as a sequential pairwise
-// tree -- and broadcast from lane 0.
-__device__ __forceinline__ float old_warp_sum(const float* part, int l, int nwarps, int old_warps) {
-  if (l >= old_warps) return 0.0f;
-  const float p0 = 4 * l < nwarps ? part[4 * l] : 0.0f;
-  const float p1 = 4 * l + 1 < nwarps ? part[4 * l + 1] : 0.0f;
-  const float p2 = 4 * l + 2 < nwarps ? part[4 * l + 2] : 0.0f;
-  const float p3 = 4 * l + 3 < nwarps ? part[4 * l + 3] : 0.0f;
-  return __fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3));
-}
-__device__ __forceinline__ float pairwise16(float o) {
+// Row total of the threads' chunk sums in the canonical tree: lanes xor 1..16
+// (a pairwise tree over chunk index), one float per warp in `part` (this
+// reduction's own buffer), one CTA barrier, then the warps pairwise (zero
+// padded to 16) by a xor butterfly over lanes 0-15; the total is added to +0.
+__device__ __forceinline__ float warps_pairwise16(const float* part, int lane, int nwarps) {
+  float o = (lane & 15) < nwarps ? part[lane & 15] : 0.0f;
 #pragma unroll
   for (int off = 1; off < 16; off <<= 1) o = __fadd_rn(o, __shfl_xor_sync(kFull, o, off));
-  return __shfl_sync(kFull, o, 0);
+  return __fadd_rn(o, 0.0f);
 }
 
-__device__ __forceinline__ float row_total(float c, float* part, int warp, int lane, int nwarps,
-                                           int old_warps) {
-  c = __fadd_rn(c, __shfl_xor_sync(kFull, c, 4));
-  c = __fadd_rn(c, __shfl_xor_sync(kFull, c, 8));
-  c = __fadd_rn(c, __shfl_xor_sync(kFull, c, 16));
+__device__ __forceinline__ float row_total(float c, float* part, int warp, int lane, int nwarps) {
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) c = __fadd_rn(c, __shfl_xor_sync(kFull, c, off));
   if (lane == 0) part[warp] = c;
   __syncthreads();
-  return pairwise16(old_warp_sum(part, lane & 15, nwarps, old_warps));
+  return warps_pairwise16(part, lane, nwarps);
+}
+
+// x / K, correctly rounded: a multiply by the exact reciprocal when K is a
+// power of two.
+__device__ __forceinline__ float div_k(float x, float kf, float rk, bool pow2) {
+  return pow2 ? __fmul_rn(x, rk) : __fdiv_rn(x, kf);
+}
+
+// Maximum of a non-negative float over the warp (one redux instruction).
+__device__ __forceinline__ float warp_max(float m) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(m));
+  return r;
 }
 
 __device__ __forceinline__ float row_max(float m, float* part, int warp, int lane, int nwarps) {
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
+  m = warp_max(m);
   if (lane == 0) part[warp] = m;
   __syncthreads();
-  // both half-warps reduce the same 16 partials (nwarps <= 16: rows of <= 8192)
-  float t = (lane & 15) < nwarps ? part[lane & 15] : 0.0f;
-#pragma unroll
-  for (int off = 8; off > 0; off >>= 1) t = fmaxf(t, __shfl_xor_sync(kFull, t, off));
-  return t;
+  // every warp reduces the same partials (nwarps <= 16: rows of <= 8192)
+  return warp_max((lane & 15) < nwarps ? part[lane & 15] : 0.0f);
 }
 
 // Sum (canonical) and max with one barrier (RMS scale folding).
 __device__ __forceinline__ float2 row_total_max(float c, float m, float* part, float* part_max,
-                                                int warp, int lane, int nwarps, int old_warps) {
-  c = __fadd_rn(c, __shfl_xor_sync(kFull, c, 4));
-  c = __fadd_rn(c, __shfl_xor_sync(kFull, c, 8));
-  c = __fadd_rn(c, __shfl_xor_sync(kFull, c, 16));
+                                                int warp, int lane, int nwarps) {
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
+  for (int off = 1; off < 32; off <<= 1) c = __fadd_rn(c, __shfl_xor_sync(kFull, c, off));
+  m = warp_max(m);
   if (lane == 0) {
     part[warp] = c;
     part_max[warp] = m;
   }
   __syncthreads();
-  const float total = pairwise16(old_warp_sum(part, lane & 15, nwarps, old_warps));
-  float t = (lane & 15) < nwarps ? part_max[lane & 15] : 0.0f;
-#pragma unroll
-  for (int off = 8; off > 0; off >>= 1) t = fmaxf(t, __shfl_xor_sync(kFull, t, off));
-  return make_float2(total, t);
+  const float total = warps_pairwise16(part, lane, nwarps);
+  return make_float2(total, warp_max((lane & 15) < nwarps ? part_max[lane & 15] : 0.0f));
 }
 
 // ---------------------------------------------------------------- transforms
-// Signs of the thread's 16 columns (16 bytes of +-1) applied to its values.
-__device__ __forceinline__ void apply_signs(float2* v, const int8_t* sg) {
-  const uint4 sv = __ldg(reinterpret_cast<const uint4*>(sg));
-  const uint32_t w[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-  for (int qd = 0; qd < 4; ++qd) {
-    float2& p0 = v[2 * qd];
-    float2& p1 = v[2 * qd + 1];
-    p0.x = __uint_as_float(__float_as_uint(p0.x) ^ ((w[qd] << 24) & 0x80000000u));
-    p0.y = __uint_as_float(__float_as_uint(p0.y) ^ ((w[qd] << 16) & 0x80000000u));
-    p1.x = __uint_as_float(__float_as_uint(p1.x) ^ ((w[qd] << 8) & 0x80000000u));
-    p1.y = __uint_as_float(__float_as_uint(p1.y) ^ (w[qd] & 0x80000000u));
-  }
+// Sign bit (0x80000000 or 0) of element e of the thread's 16 columns, from
+// their 16 sign bytes (+-1) read as four words.
+__device__ __forceinline__ uint32_t sign_bit(const uint32_t* sw, int e) {
+  return (sw[e >> 2] << (24 - 8 * (e & 3))) & 0x80000000u;
+}
+__device__ __forceinline__ void sign_words(const int8_t* sg, uint32_t* sw) {
+  const uint4 s4 = __ldg(reinterpret_cast<const uint4*>(sg));
+  sw[0] = s4.x;
+  sw[1] = s4.y;
+  sw[2] = s4.z;
+  sw[3] = s4.w;
+}
+__device__ __forceinline__ float flip(float x, uint32_t bit) {
+  return __uint_as_float(__float_as_uint(x) ^ bit);
 }
 
 // Walsh-Hadamard butterflies of each B block (natural Sylvester order,
@@ -283,20 +254,21 @@ __global__ void __launch_bounds__(MAXT, 65536 / (MAXT * 64))
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int q = lane & 3;
   const int nthreads = blockDim.x;
   const int nwarps = nthreads >> 5;
   const int64_t K = a.K;
   const int tpr = static_cast<int>(K >> 4);
   const bool have = tid < tpr;
-  const int64_t j0 = int64_t(have ? tid : 0) * 16;
-  const int old_warps = static_cast<int>((K + 2047) / 2048);
+  const int j0 = (have ? tid : 0) * 16;  // first column of this thread
   const float kf = static_cast<float>(K);
+  const bool k_pow2 = (K & (K - 1)) == 0;
+  const float rk = k_pow2 ? 1.0f / kf : 0.0f;  // exact when K is a power of two
 
-  // Table slots: gated: gate [0,2), norm: gamma [2,4), scale [4,6), shift [6,8);
-  // RMS: gamma (fp32) [0,4).
+  // Table slots: gated: gate [0,2), norm: gamma [2,4), s * (1 + scale) (fp32)
+  // [4,8), s * shift (fp32) [8,12); RMS: s * gamma (fp32) [0,4); plain: the
+  // packed sign masks [0,2) (s: the Hadamard signs of the thread's columns).
   uint8_t* tb = tbl;
-  int64_t cur_gmap = -1, cur_map = -1;
+  int cur_gmap = -1, cur_map = -1;  // table rows now in shared memory (maps are int32)
   (void)tbl_bytes;
   if constexpr (MODE == kNorm || MODE == kNormGated) {
     if (have) {  // gamma once (shared by all rows)
@@ -305,10 +277,27 @@ __global__ void __launch_bounds__(MAXT, 65536 / (MAXT * 64))
       *tslot(tb, nthreads, tid, 3) = g.hi;
     }
   } else if constexpr (MODE == kRms) {
-    if (have) {
+    if (have) {  // gamma (fp32) with the Hadamard signs folded in: s * (t * g) = t * (s * g)
+      uint32_t sw[4] = {0u, 0u, 0u, 0u};
+      if (a.signs != nullptr) sign_words(a.signs + j0, sw);
       const uint4* gp = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(a.gamma) + j0);
 #pragma unroll
-      for (int h = 0; h < 4; ++h) *tslot(tb, nthreads, tid, h) = __ldg(gp + h);
+      for (int h = 0; h < 4; ++h) {
+        const uint4 w = __ldg(gp + h);
+        *tslot(tb, nthreads, tid, h) =
+            make_uint4(w.x ^ sign_bit(sw, 4 * h), w.y ^ sign_bit(sw, 4 * h + 1),
+                       w.z ^ sign_bit(sw, 4 * h + 2), w.w ^ sign_bit(sw, 4 * h + 3));
+      }
+    }
+  } else {
+    if (have && a.signs != nullptr) {  // sign masks of the packed 16-bit pairs
+      uint32_t sw[4];
+      sign_words(a.signs + j0, sw);
+      uint32_t mk[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mk[k] = (sign_bit(sw, 2 * k) >> 16) | sign_bit(sw, 2 * k + 1);
+      *tslot(tb, nthreads, tid, 0) = make_uint4(mk[0], mk[1], mk[2], mk[3]);
+      *tslot(tb, nthreads, tid, 1) = make_uint4(mk[4], mk[5], mk[6], mk[7]);
     }
   }
 
@@ -332,76 +321,137 @@ __global__ void __launch_bounds__(MAXT, 65536 / (MAXT * 64))
     float* rv = red[parity][1];
     float* rm = red[parity][2];
     float2 v[8];
-    unpack16<T>(cx, v);  // zeros past the row (cx is zero there)
+    if constexpr (MODE == kPlain) {
+      if (have && a.signs != nullptr) {  // X D: sign flips on the packed input
+        const uint4 m0 = *tslot(tb, nthreads, tid, 0), m1 = *tslot(tb, nthreads, tid, 1);
+        Raw16 sx;
+        sx.lo = make_uint4(cx.lo.x ^ m0.x, cx.lo.y ^ m0.y, cx.lo.z ^ m0.z, cx.lo.w ^ m0.w);
+        sx.hi = make_uint4(cx.hi.x ^ m1.x, cx.hi.y ^ m1.y, cx.hi.z ^ m1.z, cx.hi.w ^ m1.w);
+        unpack16<T>(sx, v);
+      } else {
+        unpack16<T>(cx, v);  // zeros past the row (cx is zero there)
+      }
+    } else {
+      unpack16<T>(cx, v);  // zeros past the row (cx is zero there)
+    }
 
     if constexpr (MODE == kNormGated) {
       // R' = cast_T(R + branch * gate), written once.
       if (have) {
-        const int64_t gm = a.gate_row_map ? int64_t(__ldg(a.gate_row_map + row)) : 0;
+        const int gm = a.gate_row_map ? __ldg(a.gate_row_map + row) : 0;
         if (gm != cur_gmap) {
-          const Raw16 g = ld_raw(reinterpret_cast<const T*>(a.gate) + gm * K + j0);
+          const Raw16 g = ld_raw(reinterpret_cast<const T*>(a.gate) + int64_t(gm) * K + j0);
           *tslot(tb, nthreads, tid, 0) = g.lo;
           *tslot(tb, nthreads, tid, 1) = g.hi;
           cur_gmap = gm;
         }
-        Raw16 g;
-        g.lo = *tslot(tb, nthreads, tid, 0);
-        g.hi = *tslot(tb, nthreads, tid, 1);
-        float2 br[8];
-        unpack16<T>(cb, br);
+        // one 16-byte half at a time; each R' word is converted once, stored
+        // and unpacked again for the normalization
+        uint4* rdst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.r_out) + row * K + j0);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = round2<T>(__ffma2_rn(br[k], pair_of<T>(g, k), v[k]));
-        st16<T>(reinterpret_cast<T*>(a.r_out) + row * K + j0, v);
+        for (int half = 0; half < 2; ++half) {
+          const uint4 gw = *tslot(tb, nthreads, tid, half);
+          const uint4 bw = half ? cb.hi : cb.lo;
+          const uint32_t gv[4] = {gw.x, gw.y, gw.z, gw.w};
+          const uint32_t bv[4] = {bw.x, bw.y, bw.z, bw.w};
+          uint32_t rw[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int k = 4 * half + i;
+            rw[i] = pack2<T>(fma_words16<T>(bv[i], gv[i], v[k]));
+            v[k] = word_pair<T>(rw[i]);
+          }
+          rdst[half] = make_uint4(rw[0], rw[1], rw[2], rw[3]);
+        }
       }
     }
 
     float inv = 1.0f;      // RMS folding: the row's inverse RMS
     float sq_chunk = 0.0f;
     if constexpr (MODE == kNorm || MODE == kNormGated) {
-      const float c0 = (a.norm == NORM_LAYER) ? quad_chunk_sum<0>(v, 0.0f, q, lane, have)
-                                              : quad_chunk_sum<1>(v, 0.0f, q, lane, have);
-      const float first = __fdiv_rn(row_total(c0, rs, warp, lane, nwarps, old_warps), kf);
-      float mean = 0.0f, moment = first;
-      if (a.norm == NORM_LAYER) {
-        mean = first;
-        moment = __fdiv_rn(
-            row_total(quad_chunk_sum<2>(v, mean, q, lane, have), rv, warp, lane, nwarps, old_warps),
-            kf);
+      const bool layer = a.norm == NORM_LAYER;
+      const float c0 = !have ? 0.0f : layer ? chunk16_sum<false>(v) : chunk16_sum<true>(v);
+      const float first = div_k(row_total(c0, rs, warp, lane, nwarps), kf, rk, k_pow2);
+      float moment = first;
+      if (layer) {
+        // centered values, kept for the normalization: (x - mean) is the
+        // same rounded difference in both places
+        const float2 nm = f2(-first);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __fadd2_rn(v[k], nm);
+        moment = div_k(row_total(have ? chunk16_sum<true>(v) : 0.0f, rv, warp, lane, nwarps), kf,
+                       rk, k_pow2);
       }
       inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(moment, a.eps)));
       if (have) {
-        const int64_t mm = a.row_map ? int64_t(__ldg(a.row_map + row)) : 0;
+        const int mm = a.row_map ? __ldg(a.row_map + row) : 0;
         if (mm != cur_map) {
-          const Raw16 sc = ld_raw(reinterpret_cast<const T*>(a.scale) + mm * K + j0);
-          const Raw16 sh = ld_raw(reinterpret_cast<const T*>(a.shift) + mm * K + j0);
-          *tslot(tb, nthreads, tid, 4) = sc.lo;
-          *tslot(tb, nthreads, tid, 5) = sc.hi;
-          *tslot(tb, nthreads, tid, 6) = sh.lo;
-          *tslot(tb, nthreads, tid, 7) = sh.hi;
+          // the modulation's 1 + scale (rounded once, as where it is used)
+          // and shift, kept as fp32
+          // The Hadamard signs are folded in as well: with s = +-1,
+          // fma(t, s * o, s * sh) = s * fma(t, o, sh) and rounding to the
+          // input dtype commutes with the sign, so the modulated, rounded,
+          // sign-flipped value is the one computed in that order.
+          // (one 16-byte half of the thread's columns at a time: few live
+          // registers in this rarely taken branch)
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const uint4 scw =
+                __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.scale) + int64_t(mm) * K + j0) + half);
+            const uint4 shw =
+                __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.shift) + int64_t(mm) * K + j0) + half);
+            const uint2 sgw = a.signs != nullptr
+                                  ? __ldg(reinterpret_cast<const uint2*>(a.signs + j0) + half)
+                                  : make_uint2(0u, 0u);
+            const uint32_t scv[4] = {scw.x, scw.y, scw.z, scw.w};
+            const uint32_t shv[4] = {shw.x, shw.y, shw.z, shw.w};
+            const uint32_t sgv[2] = {sgw.x, sgw.y};
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const float2 o0 = __fadd2_rn(f2(1.0f), word_pair<T>(scv[2 * hh]));
+              const float2 o1 = __fadd2_rn(f2(1.0f), word_pair<T>(scv[2 * hh + 1]));
+              const float2 s0 = word_pair<T>(shv[2 * hh]), s1 = word_pair<T>(shv[2 * hh + 1]);
+              const uint32_t b0 = sign_bit(sgv + hh, 0), b1 = sign_bit(sgv + hh, 1);
+              const uint32_t b2 = sign_bit(sgv + hh, 2), b3 = sign_bit(sgv + hh, 3);
+              const int h = 2 * half + hh;
+              *tslot(tb, nthreads, tid, 4 + h) =
+                  make_uint4(__float_as_uint(o0.x) ^ b0, __float_as_uint(o0.y) ^ b1,
+                             __float_as_uint(o1.x) ^ b2, __float_as_uint(o1.y) ^ b3);
+              *tslot(tb, nthreads, tid, 8 + h) =
+                  make_uint4(__float_as_uint(s0.x) ^ b0, __float_as_uint(s0.y) ^ b1,
+                             __float_as_uint(s1.x) ^ b2, __float_as_uint(s1.y) ^ b3);
+            }
+          }
           cur_map = mm;
         }
-        Raw16 g, sc, sh;
+        Raw16 g;
         g.lo = *tslot(tb, nthreads, tid, 2);
         g.hi = *tslot(tb, nthreads, tid, 3);
-        sc.lo = *tslot(tb, nthreads, tid, 4);
-        sc.hi = *tslot(tb, nthreads, tid, 5);
-        sh.lo = *tslot(tb, nthreads, tid, 6);
-        sh.hi = *tslot(tb, nthreads, tid, 7);
-        const float2 nm = f2(-mean), inv2 = f2(inv);
+        const float2 inv2 = f2(inv);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float2 t = __fmul2_rn(__fmul2_rn(__fadd2_rn(v[k], nm), inv2), pair_of<T>(g, k));
-          float2 y = __ffma2_rn(t, __fadd2_rn(f2(1.0f), pair_of<T>(sc, k)), pair_of<T>(sh, k));
-          if (a.round_output) y = round2<T>(y);
-          v[k] = y;
+        for (int h = 0; h < 4; ++h) {  // v holds x - mean (LayerNorm) or x (RMS)
+          const uint4 ow = *tslot(tb, nthreads, tid, 4 + h);
+          const uint4 sw = *tslot(tb, nthreads, tid, 8 + h);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int k = 2 * h + e;
+            const float2 ops = e == 0 ? make_float2(__uint_as_float(ow.x), __uint_as_float(ow.y))
+                                      : make_float2(__uint_as_float(ow.z), __uint_as_float(ow.w));
+            const float2 shf = e == 0 ? make_float2(__uint_as_float(sw.x), __uint_as_float(sw.y))
+                                      : make_float2(__uint_as_float(sw.z), __uint_as_float(sw.w));
+            const float2 t = __fmul2_rn(__fmul2_rn(v[k], inv2), pair_of<T>(g, k));
+            float2 y = __ffma2_rn(t, ops, shf);
+            if (a.round_output) y = round2<T>(y);
+            v[k] = y;
+          }
         }
       }
     } else if constexpr (MODE == kRms) {
       // statistics of the ORIGINAL row; direct form normalizes now, folded
       // form keeps the inverse RMS for the row scale
-      sq_chunk = quad_chunk_sum<1>(v, 0.0f, q, lane, have);
+      sq_chunk = have ? chunk16_sum<true>(v) : 0.0f;
       if (a.rms_quant == RMSQ_DIRECT) {
-        const float moment = __fdiv_rn(row_total(sq_chunk, rs, warp, lane, nwarps, old_warps), kf);
+        const float moment = div_k(row_total(sq_chunk, rs, warp, lane, nwarps), kf, rk, k_pow2);
         inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(moment, a.eps)));
       }
       if (have) {
@@ -422,7 +472,7 @@ __global__ void __launch_bounds__(MAXT, 65536 / (MAXT * 64))
         }
       }
     }
-    if (a.signs != nullptr && have) apply_signs(v, a.signs + j0);
+    // (the signs D are already in: packed input flips, or folded into the tables)
     fwht<B>(v, lane, a.inv_sqrt_block);
 
     if constexpr (OUT == OUT_F32) {
@@ -439,8 +489,8 @@ __global__ void __launch_bounds__(MAXT, 65536 / (MAXT * 64))
       float peak;
       if constexpr (MODE == kRms) {
         if (a.rms_quant == RMSQ_FOLD) {
-          const float2 sm = row_total_max(sq_chunk, m, rs, rm, warp, lane, nwarps, old_warps);
-          const float moment = __fdiv_rn(sm.x, kf);
+          const float2 sm = row_total_max(sq_chunk, m, rs, rm, warp, lane, nwarps);
+          const float moment = div_k(sm.x, kf, rk, k_pow2);
           inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(moment, a.eps)));
           peak = sm.y;
         } else {
@@ -528,8 +578,9 @@ cudaError_t launch_k(const RowPrepArgs& a, cudaStream_t stream) {
   const int tpr = static_cast<int>(a.K / 16);
   const int threads = (tpr + 31) & ~31;
   int slots = 0;
-  if (MODE == kNorm || MODE == kNormGated) slots = 8;
+  if (MODE == kNorm || MODE == kNormGated) slots = 12;
   if (MODE == kRms) slots = 4;
+  if (MODE == kPlain) slots = 2;  // packed sign masks
   const int smem = slots * threads * 16;
   static std::atomic<long long> shape[kMaxLaunchDevices];
   int dev = 0, sms = 0, per_sm = 0;

@@ -2,6 +2,7 @@
 
 The `cuda-b200` backend of the m5kernels operator contracts:
     quantize, gemm                     (twin of m5kernels.metal)
+    gemm_schedule                      (the schedule `m5bench tune` sweeps, in place of Metal tiles)
     rotate, hadamard_quantize          (twin of m5kernels.hadamard)
     fused_norm_hadamard_quantize,
     fused_gated_residual_norm_hadamard_quantize,
@@ -14,7 +15,7 @@ All of them run hand-written CUDA kernels from libm5b200.so through its C ABI
 (include/m5b200.h); there is no CPU fallback.
 """
 
-from .cuda import gemm, gemm_allgather, quantize
+from .cuda import gemm, gemm_allgather, gemm_schedule, quantize
 from .hadamard import SUPPORTED_BLOCK_SIZES, hadamard_quantize, rotate
 from .linear import OnlineProjection, linear
 from .norm_hadamard import (fused_gated_residual_norm_hadamard_quantize,
@@ -24,7 +25,7 @@ from .qk_rope import (grouped_qkv_weights, projection_qk_rope, projection_qkv_ro
 from .rms_quant import rms_quantize
 
 __all__ = [
-    "gemm", "gemm_allgather", "quantize", "rotate", "hadamard_quantize", "SUPPORTED_BLOCK_SIZES",
+    "gemm", "gemm_allgather", "gemm_schedule", "quantize", "rotate", "hadamard_quantize", "SUPPORTED_BLOCK_SIZES",
     "fused_norm_hadamard_quantize", "fused_gated_residual_norm_hadamard_quantize",
     "projection_qk_rope", "rope_tables", "linear", "rms_quantize", "gated_residual_add",
     "unfused_norm", "qk_norm_rope", "projection_qkv_rope", "grouped_qkv_weights",

@@ -58,6 +58,7 @@ _SIGNATURES = {
     "m5b_linear": ([P, I, I64, I64, I, P, P, P, I64, I, P, I, P, I64, P], I),
     "m5b_linear_ex": ([P, I, I64, I64, I, P, P, P, I64, I, P, I, P, I64, P, I64, P], I),
     "m5b_linear_noalloc": ([P, I, I64, I64, I, P, P, P, I64, I, P, I, P], I),
+    "m5b_gemm_set_schedule": ([I, I], I),
 }
 
 

@@ -5,11 +5,17 @@
     python -m m5kernels_b200.cli bench --suite baseline --backends cuda-b200 \\
         --precisions int8 [--cases id,...] [--seed 17] [--distribution normal] \\
         [--warmup 3] [--repeat 10] [--out results/run.json]
+    python -m m5kernels_b200.cli tune --suite baseline --filter ffn --precisions int8 \
+        [--tune-backend cuda-b200] --out results/tune.json
     python -m m5kernels_b200.cli report results/run.json
 
 Mirrors the reference CLI (src/m5kernels/cli.py:188-245): suites are
 workload manifests (schema v1), every (case, precision, backend) goes
 through engine.run_case, and results are written with exclusive create.
+`tune` is the twin of the reference's tile sweep (cli.py:66-151): it sweeps
+the B200 GEMM schedules (SCHEDULES) instead of Metal tiles, keeps the fastest
+correct one by the online (quantization + GEMM) time, and re-runs it on a
+fresh seed (seed + 1) as the holdout that decides the exit status.
 """
 
 from __future__ import annotations
@@ -17,6 +23,7 @@ from __future__ import annotations
 import argparse
 import json
 import sys
+from pathlib import Path
 
 from . import engine, workloads
 
@@ -79,6 +86,57 @@ def _bench(args) -> int:
     return 1 if bad else 0
 
 
+# (split_k, group_m): the library's rule, data-parallel, split-K factors,
+# raster groups of 1, 4 and 16 M-blocks -- eight candidates, as the reference
+# sweeps eight tiles.
+SCHEDULES = [(-1, 0), (0, 0), (2, 0), (3, 0), (4, 0), (-1, 1), (-1, 4), (-1, 16)]
+
+
+def _online_ms(r) -> float:
+    return r.get("stages", {}).get("online_activation_plus_gemm", r["timing"])["median_ms"]
+
+
+def _tune(args) -> int:
+    cases = [c for c in workloads.load(args.suite)["cases"]
+             if args.filter in c["id"] and c["op"] == "gemm"]
+    if not cases:
+        raise ValueError("no GEMM cases matched")
+    if args.out and Path(args.out).exists():
+        raise FileExistsError(args.out)
+    doc = {"schema_version": 1, "environment": engine.environment(), "suite": args.suite,
+           "results": [], "selections": []}
+    backend = args.tune_backend
+    for c in cases:
+        for precision in args.precisions.split(","):
+            runs = []
+            for sched in SCHEDULES:
+                r = engine.run_case(c, backend, precision, seed=args.seed,
+                                    distribution=args.distribution, warmup=args.warmup,
+                                    repeat=args.repeat, schedule=sched)
+                doc["results"].append(r)
+                runs.append(r)
+                t = r.get("timing", {}).get("median_ms")
+                print(c["id"], precision, sched, r["status"], t, flush=True)
+            valid = [r for r in runs if r["status"] == "ok" and r["quality_pass"]]
+            if not valid:
+                continue
+            best = min(valid, key=_online_ms)
+            sched = (best["schedule"]["split_k"], best["schedule"]["group_m"])
+            # fresh seed, fresh timing; the selected schedule stays fixed
+            holdout = engine.run_case(c, backend, precision, seed=args.seed + 1,
+                                      distribution=args.distribution, warmup=args.warmup,
+                                      repeat=args.repeat, schedule=sched)
+            doc["selections"].append({"case_id": c["id"], "backend": backend,
+                                      "precision": precision, "schedule": best["schedule"],
+                                      "online_ms": _online_ms(best), "holdout": holdout})
+            print(c["id"], precision, "selected", sched, "holdout", holdout["status"], flush=True)
+    if args.out:
+        engine.write_result(args.out, doc)
+    ok = doc["selections"] and all(
+        s["holdout"]["status"] == "ok" and s["holdout"]["quality_pass"] for s in doc["selections"])
+    return 0 if ok else 1
+
+
 def _report(args) -> int:
     doc = json.loads(open(args.path).read())
     for r in doc["results"]:
@@ -104,12 +162,23 @@ def main(argv=None) -> int:
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--repeat", type=int, default=10)
     p.add_argument("--out", default="")
+    p = sub.add_parser("tune")
+    p.add_argument("--suite", default="baseline")
+    p.add_argument("--filter", default="")
+    p.add_argument("--tune-backend", choices=list(engine.BACKENDS["gemm"]), default="cuda-b200")
+    p.add_argument("--precisions", default="int8")
+    p.add_argument("--seed", type=int, default=17)
+    p.add_argument("--distribution", default="normal", choices=["normal", "outliers", "zeros"])
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--repeat", type=int, default=10)
+    p.add_argument("--out", default="")
     p = sub.add_parser("report")
     p.add_argument("path")
     args = ap.parse_args(argv)
     if getattr(args, "warmup", 1) < 0 or getattr(args, "repeat", 1) < 1:
         ap.error("warmup must be >= 0 and repeat >= 1")
-    return {"doctor": _doctor, "shapes": _shapes, "bench": _bench, "report": _report}[args.cmd](args)
+    return {"doctor": _doctor, "shapes": _shapes, "bench": _bench, "tune": _tune,
+            "report": _report}[args.cmd](args)
 
 
 if __name__ == "__main__":

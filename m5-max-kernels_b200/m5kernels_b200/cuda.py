@@ -11,6 +11,8 @@ narrow outputs).
 
 from __future__ import annotations
 
+import contextlib
+
 import torch
 
 from . import _lib
@@ -22,6 +24,25 @@ FLOAT_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
 def _validate_tile(tile):
     if not isinstance(tile, (tuple, list)) or len(tile) != 4:
         raise ValueError("tile must contain TM, TN, SIMD groups and M swizzle")
+
+
+@contextlib.contextmanager
+def gemm_schedule(split_k: int = -1, group_m: int = 0):
+    """GEMM schedule for the calls made inside the block from this thread.
+
+    The B200 counterpart of the reference's Metal `tile` (what `m5bench tune`
+    sweeps, src/m5kernels/cli.py:66-151): split_k -1 = the library's rule,
+    0 = data-parallel, 2..4 = CTA pairs per 256 x 256 tile over equal K ranges
+    (INT8 GEMMs with a workspace, where every unit fits on the GPU at once);
+    group_m 0 = the library's raster, else M-blocks per raster group.  Results
+    are identical under every schedule; only the time changes.
+    """
+    lib = _lib.lib()
+    check(lib.m5b_gemm_set_schedule(int(split_k), int(group_m)))
+    try:
+        yield
+    finally:
+        check(lib.m5b_gemm_set_schedule(-1, 0))
 
 
 def quantize(x: torch.Tensor, mode: str, tag: str = "packed"):

@@ -22,6 +22,7 @@ Backends (the `backend` string of run_case):
 
 from __future__ import annotations
 
+import contextlib
 import hashlib
 import json
 import platform
@@ -34,7 +35,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .cuda import gemm, quantize
+from .cuda import gemm, gemm_schedule, quantize
 from .hadamard import hadamard_quantize, rotate
 from .norm_hadamard import (fused_gated_residual_norm_hadamard_quantize,
                             fused_norm_hadamard_quantize, gated_residual_add, unfused_norm)
@@ -582,71 +583,87 @@ QUALITY_LIMIT = {"int8": 0.05, "fp8": 0.10}
 
 
 def run_case(c, backend, precision, seed=17, distribution="normal", warmup=3, repeat=10,
-             tile=(64, 64, 4, 1)):
-    """Prepare, check and (only if correct) time one case; never raises."""
+             tile=(64, 64, 4, 1), schedule=None):
+    """Prepare, check and (only if correct) time one case; never raises.
+
+    `schedule` = (split_k, group_m) runs every GEMM of the case under that
+    schedule (cuda.gemm_schedule); None keeps the library's choice.
+    """
     result = dict(case=c, backend=backend, precision=precision, seed=seed,
                   distribution=distribution, tile=list(tile))
+    if schedule is not None:
+        result["schedule"] = {"split_k": int(schedule[0]), "group_m": int(schedule[1])}
     meta = {}
-    try:
-        if c["op"] not in PREPARE:
-            raise NotImplementedError(f"op {c['op']} is not part of the cuda-b200 backend")
-        if backend not in BACKENDS[c["op"]]:
-            raise NotImplementedError(
-                f"backend {backend} does not implement {c['op']}; choose one of {BACKENDS[c['op']]}")
-        if not torch.cuda.is_available():
-            raise _lib.ExtensionMissing("no CUDA device is visible; the cuda-b200 backend has no CPU path")
-        est = (c["m"] * c["k"] + c["n"] * c["k"] + c["m"] * c["n"]) * 8
-        free = torch.cuda.mem_get_info()[0]
-        if est > free:
-            raise NotImplementedError("estimated working set exceeds free device memory; split workload")
-        fn, check, expected, original, stages, meta = PREPARE[c["op"]](
-            c, backend, precision, seed, distribution, tile)
-        y = fn()
-        torch.cuda.synchronize()
-        output_finite = all_finite(y)
-        actual = check(y)
-        impl = metrics(actual, expected)
-        quality = metrics(actual, original)
-        tolerance = 0.008
-        passed = bool(output_finite and impl["finite"] and impl["relative_l2"] <= tolerance
-                      and meta.get("transform_pass", True))
-        quality_passed = bool(quality["finite"] and quality["relative_l2"] <= QUALITY_LIMIT[precision])
-        result.update(meta, status="ok" if passed else "incorrect", output_finite=output_finite,
-                      implementation_error=impl, quality_error=quality,
-                      implementation_relative_l2_limit=tolerance,
-                      quality_relative_l2_limit=QUALITY_LIMIT[precision],
-                      quality_pass=quality_passed)
-        online_y = stages["online_activation_plus_gemm"]()
-        torch.cuda.synchronize()
-        online_error = metrics(check(online_y), expected)
-        online_finite = all_finite(online_y)
-        result["online_implementation_error"] = online_error
-        result["online_output_finite"] = online_finite
-        passed = bool(passed and online_finite and online_error["finite"]
-                      and online_error["relative_l2"] <= tolerance)
-        status_word = _lib.device_status(clear=True)
-        if status_word:
-            passed = False
-            result["device_status"] = status_word
-        result["status"] = "ok" if passed else "incorrect"
-        del online_y
-        if passed:  # never time an incorrect implementation
-            result["timing"] = timed(fn, warmup, repeat)
-            result["stages"] = {name: timed(f, warmup, repeat) for name, f in stages.items()}
-            result["effective_tops"] = meta["mac_operations"] / (result["timing"]["median_ms"] * 1e9)
-            result["online_effective_tops"] = meta["mac_operations"] / (
-                result["stages"]["online_activation_plus_gemm"]["median_ms"] * 1e9)
-        del y, fn, stages
-    except NumericalMismatch as e:
-        result.update(meta)
-        result.update(status="incorrect", reason=str(e), **e.diagnostics)
-    except NotImplementedError as e:
-        result.update(status="unsupported", reason=str(e))
-    except Exception as e:  # noqa: BLE001  (the harness records every failure)
-        result.update(status="error", reason=f"{type(e).__name__}: {e}"[:5000])
+    with contextlib.ExitStack() as scope:
+        try:
+            if schedule is not None:
+                scope.enter_context(gemm_schedule(*schedule))
+            _run_checked(c, backend, precision, seed, distribution, warmup, repeat, tile, result,
+                         meta)
+        except NumericalMismatch as e:
+            result.update(meta)
+            result.update(status="incorrect", reason=str(e), **e.diagnostics)
+        except NotImplementedError as e:
+            result.update(status="unsupported", reason=str(e))
+        except Exception as e:  # noqa: BLE001  (the harness records every failure)
+            result.update(status="error", reason=f"{type(e).__name__}: {e}"[:5000])
     if torch.cuda.is_available():
         torch.cuda.empty_cache()
     return result
+
+
+def _run_checked(c, backend, precision, seed, distribution, warmup, repeat, tile, result, meta):
+    """run_case's body: prepare, check, and time only what passed."""
+    if c["op"] not in PREPARE:
+        raise NotImplementedError(f"op {c['op']} is not part of the cuda-b200 backend")
+    if backend not in BACKENDS[c["op"]]:
+        raise NotImplementedError(
+            f"backend {backend} does not implement {c['op']}; choose one of {BACKENDS[c['op']]}")
+    if not torch.cuda.is_available():
+        raise _lib.ExtensionMissing("no CUDA device is visible; the cuda-b200 backend has no CPU path")
+    est = (c["m"] * c["k"] + c["n"] * c["k"] + c["m"] * c["n"]) * 8
+    free = torch.cuda.mem_get_info()[0]
+    if est > free:
+        raise NotImplementedError("estimated working set exceeds free device memory; split workload")
+    fn, check, expected, original, stages, prepared = PREPARE[c["op"]](
+        c, backend, precision, seed, distribution, tile)
+    meta.update(prepared)
+    y = fn()
+    torch.cuda.synchronize()
+    output_finite = all_finite(y)
+    actual = check(y)
+    impl = metrics(actual, expected)
+    quality = metrics(actual, original)
+    tolerance = 0.008
+    passed = bool(output_finite and impl["finite"] and impl["relative_l2"] <= tolerance
+                  and meta.get("transform_pass", True))
+    quality_passed = bool(quality["finite"] and quality["relative_l2"] <= QUALITY_LIMIT[precision])
+    result.update(meta, status="ok" if passed else "incorrect", output_finite=output_finite,
+                  implementation_error=impl, quality_error=quality,
+                  implementation_relative_l2_limit=tolerance,
+                  quality_relative_l2_limit=QUALITY_LIMIT[precision],
+                  quality_pass=quality_passed)
+    online_y = stages["online_activation_plus_gemm"]()
+    torch.cuda.synchronize()
+    online_error = metrics(check(online_y), expected)
+    online_finite = all_finite(online_y)
+    result["online_implementation_error"] = online_error
+    result["online_output_finite"] = online_finite
+    passed = bool(passed and online_finite and online_error["finite"]
+                  and online_error["relative_l2"] <= tolerance)
+    status_word = _lib.device_status(clear=True)
+    if status_word:
+        passed = False
+        result["device_status"] = status_word
+    result["status"] = "ok" if passed else "incorrect"
+    del online_y
+    if passed:  # never time an incorrect implementation
+        result["timing"] = timed(fn, warmup, repeat)
+        result["stages"] = {name: timed(f, warmup, repeat) for name, f in stages.items()}
+        result["effective_tops"] = meta["mac_operations"] / (result["timing"]["median_ms"] * 1e9)
+        result["online_effective_tops"] = meta["mac_operations"] / (
+            result["stages"]["online_activation_plus_gemm"]["median_ms"] * 1e9)
+    del y, fn, stages
 
 
 def write_result(path, document) -> None:

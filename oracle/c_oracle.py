@@ -94,8 +94,6 @@ def lib() -> ctypes.CDLL:
         _lib.m5o_row_prep.argtypes = [P, I32, P, P, I32, P, P, I32, P, I32, P, I32, P, P, I64, I64,
                                       I32, F, I32, I32, I32, P, P, P, P]
         _lib.m5o_row_prep.restype = None
-        _lib.m5o_row_prep_warps.argtypes = [I64, I32]
-        _lib.m5o_row_prep_warps.restype = I32
         _lib.m5o_e4m3_encode.argtypes = [F]
         _lib.m5o_e4m3_encode.restype = ctypes.c_uint8
         _lib.m5o_gemm_i8_acc.argtypes = [P, P, I64, I64, I64, P]
@@ -242,11 +240,7 @@ def qk_rope_from_acc(accf, sa, sb, gamma, cos, sin, rope_half, eps):
     return out
 
 
-def row_prep_warps(k: int, block: int) -> int:
-    return int(lib().m5o_row_prep_warps(int(k), int(block)))
-
-
 __all__ = [
     "build", "build_omp", "omp_projection", "quantize_mxint8", "row_prep", "quantize", "rotate", "gemm_i8_acc", "gemm_i8_acc_fast",
-    "gemm_epilogue", "qk_rope_from_acc", "e4m3_encode_scalar", "row_prep_warps", "np",
+    "gemm_epilogue", "qk_rope_from_acc", "e4m3_encode_scalar", "np",
 ]

@@ -24,14 +24,18 @@
  * with an unspecified reduction order, which is why the reference accepts a
  * one-code difference.  This restatement instead fixes the FP32 order so it is
  * bit-comparable with the CUDA kernels:
- *   - row reductions: thread t of the row owns the contiguous 64-element chunk
- *     [64 t, 64 t + 64); eight accumulators a[e] take elements e, e+8, ...,
- *     e+56 in order and combine ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)); the 32 lanes of a warp
- *     combine with a xor butterfly of increasing offset (1, 2, 4, 8, 16), i.e.
- *     a pairwise tree over chunk index; the W = ceil(K / 2048) warp partials
- *     (padded with zeros to 16) combine pairwise (w0+w1, w2+w3, ...);
- *   - sum of squares uses fmaf(x, x, acc), the centered LayerNorm pass
- *     fmaf(d, d, acc) with d = x - mean;
+ *   - row reductions: the row is cut into 16-element chunks [16 c, 16 c + 16)
+ *     (elements past K count as zero).  A chunk is eight pairs
+ *     p_k = (x_2k, x_2k+1); pairs combine as L1_j = p_2j (+) p_2j+1 -- for
+ *     squares fmaf(u_2j, u_2j, u_2j+1 * u_2j+1) with u = x or x - mean --
+ *     then (L1_0 + L1_1) + (L1_2 + L1_3), each step on both halves of the
+ *     pair, and the chunk is the pair's even half + odd half.  The chunk sums
+ *     of a row combine as a pairwise tree over chunk index (c0 + c1, c2 + c3,
+ *     ..., then pairs of pairs), padded with zero chunks to a power of two,
+ *     and the total is added to +0 (kernels may pad the tree further);
+ *     The tree does not depend on how a kernel splits the row among threads
+ *     and warps, so every schedule (16 or 64 elements per thread) forms it;
+ *     the centered LayerNorm pass uses u = x - mean, rounded once;
  *   - Hadamard butterflies in natural Sylvester order with increasing stride,
  *     then one multiply by fp32(1/sqrt(B));
  *   - every other operation is a single IEEE-754 binary32 operation in the
@@ -140,52 +144,45 @@ uint8_t m5o_e4m3_encode(float z) {
 static uint8_t e4m3_code(float v, float scale) { return m5o_e4m3_encode(v / scale); }
 
 /* ------------------------------------------------------------------ layout */
-#define CHUNK 64
-
-int m5o_row_prep_warps(int64_t K, int block) {
-  (void)block;
-  const int64_t w = (K + 2047) / 2048;
-  return w < 1 ? 1 : (w > 1024 ? 1024 : (int)w);
+/* Sum of f(v[j]) over one row in the canonical order.  kind 0: sum of v,
+ * kind 1: sum of v*v, kind 2: sum of (v-mean)^2; squares of a pair of
+ * elements as fmaf(u0, u0, u1 * u1). */
+#define RCHUNK 16
+static float chunk16(const float* v, int64_t j0, int64_t K, int kind, float mean) {
+  float u[RCHUNK];
+  for (int i = 0; i < RCHUNK; ++i) {
+    const int64_t j = j0 + i;
+    float x = j < K ? v[j] : 0.0f;
+    if (kind == 2) x = j < K ? x - mean : 0.0f;
+    u[i] = x;
+  }
+  float l1[4][2];
+  for (int jj = 0; jj < 4; ++jj)
+    for (int h = 0; h < 2; ++h) {
+      const float a = u[4 * jj + h], b = u[4 * jj + 2 + h];
+      if (kind == 0) {
+        l1[jj][h] = a + b;
+      } else {
+        const float bb = b * b;
+        l1[jj][h] = fmaf(a, a, bb);
+      }
+    }
+  float pe = (l1[0][0] + l1[1][0]) + (l1[2][0] + l1[3][0]);
+  float po = (l1[0][1] + l1[1][1]) + (l1[2][1] + l1[3][1]);
+  return pe + po;
 }
 
-/* Sum of f(v[j]) over one row in the kernel's canonical order.  kind 0: sum
- * of v, kind 1: sum of v*v (fma), kind 2: sum of (v-mean)^2 (fma). */
-static float row_reduce(const float* v, int64_t K, int W, int kind, float mean) {
-  float part[16];
-  for (int w = 0; w < 16; ++w) part[w] = 0.0f;
-  for (int w = 0; w < W; ++w) {
-    float lane_acc[32];
-    for (int l = 0; l < 32; ++l) {
-      const int64_t j0 = ((int64_t)w * 32 + l) * CHUNK;
-      float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int i = 0; i < CHUNK; i += 8) {
-        for (int e = 0; e < 8; ++e) {
-          const int64_t j = j0 + i + e;
-          if (j >= K) continue;
-          const float x = v[j];
-          if (kind == 0) {
-            a[e] = a[e] + x;
-          } else if (kind == 1) {
-            a[e] = fmaf(x, x, a[e]);
-          } else {
-            const float d = x - mean;
-            a[e] = fmaf(d, d, a[e]);
-          }
-        }
-      }
-      const float acc = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
-      lane_acc[l] = acc;
-    }
-    for (int off = 1; off < 32; off <<= 1) {
-      float nxt[32];
-      for (int l = 0; l < 32; ++l) nxt[l] = lane_acc[l] + lane_acc[l ^ off];
-      memcpy(lane_acc, nxt, sizeof(nxt));
-    }
-    part[w] = lane_acc[0];
-  }
-  for (int step = 1; step < 16; step <<= 1)
-    for (int w = 0; w + step < 16; w += 2 * step) part[w] = part[w] + part[w + step];
-  return part[0];
+static float row_reduce(const float* v, int64_t K, int kind, float mean) {
+  const int64_t n = (K + RCHUNK - 1) / RCHUNK;
+  int64_t np2 = 1;
+  while (np2 < n) np2 <<= 1;
+  float* s = (float*)malloc((size_t)np2 * sizeof(float));
+  for (int64_t c = 0; c < np2; ++c) s[c] = c < n ? chunk16(v, c * RCHUNK, K, kind, mean) : 0.0f;
+  for (int64_t len = np2; len > 1; len >>= 1)
+    for (int64_t c = 0; c < len / 2; ++c) s[c] = s[2 * c] + s[2 * c + 1];
+  const float total = s[0] + 0.0f; /* -0 -> +0: kernels may pad the tree further */
+  free(s);
+  return total;
 }
 
 static void fwht_block(float* v, int B) {
@@ -210,7 +207,6 @@ void m5o_row_prep(const void* x, int x_dtype, const void* branch, const void* ga
                   int64_t K, int norm, float eps, int round_output, int block, int out, void* q,
                   float* s, float* y, void* r_out) {
   float* v = (float*)malloc(sizeof(float) * (size_t)K);
-  const int W = m5o_row_prep_warps(K, block);
   const float inv_sqrt_block = block > 0 ? (float)(1.0 / sqrt((double)block)) : 1.0f;
   for (int64_t r = 0; r < rows; ++r) {
     /* load, gated residual update */
@@ -230,11 +226,11 @@ void m5o_row_prep(const void* x, int x_dtype, const void* branch, const void* ga
     if (norm != NORM_NONE) {
       const float kf = (float)K;
       const float first =
-          row_reduce(v, K, W, norm == NORM_LAYER ? 0 : 1, 0.0f) / kf;
+          row_reduce(v, K, norm == NORM_LAYER ? 0 : 1, 0.0f) / kf;
       float moment = first;
       if (norm == NORM_LAYER) {
         mean = first;
-        moment = row_reduce(v, K, W, 2, mean) / kf;
+        moment = row_reduce(v, K, 2, mean) / kf;
       }
       inv = 1.0f / sqrtf(moment + eps);
     }
@@ -289,11 +285,10 @@ void m5o_rms_quantize(const void* x, int x_dtype, const float* gamma, const int8
                       int64_t rows, int64_t K, int block, int fold, float eps, int8_t* q,
                       float* s) {
   float* v = (float*)malloc(sizeof(float) * (size_t)K);
-  const int W = m5o_row_prep_warps(K, block);
   const float inv_sqrt_block = block > 0 ? (float)(1.0 / sqrt((double)block)) : 1.0f;
   for (int64_t r = 0; r < rows; ++r) {
     for (int64_t j = 0; j < K; ++j) v[j] = load_elem(x, x_dtype, r * K + j);
-    const float moment = row_reduce(v, K, W, 1, 0.0f) / (float)K;
+    const float moment = row_reduce(v, K, 1, 0.0f) / (float)K;
     const float inv = 1.0f / sqrtf(moment + eps);
     for (int64_t j = 0; j < K; ++j) {
       float t = fold ? v[j] : v[j] * inv;

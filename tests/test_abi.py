@@ -85,6 +85,16 @@ def test_contract_errors_come_back_through_the_abi_without_a_gpu():
     assert rc == _lib.EINVAL and b"heads" in lib.m5b_last_error()
 
 
+def test_gemm_schedule_is_validated_on_the_host():
+    from m5kernels_b200 import _lib
+
+    lib = _lib.lib()
+    for bad in ((1, 0), (-2, 0), (5, 0), (-1, -1)):
+        assert lib.m5b_gemm_set_schedule(*bad) == _lib.EINVAL
+    assert lib.m5b_gemm_set_schedule(2, 4) == _lib.OK
+    assert lib.m5b_gemm_set_schedule(-1, 0) == _lib.OK
+
+
 def test_operators_refuse_cpu_tensors():
     import m5kernels_b200 as m
     from m5kernels_b200._lib import ExtensionMissing

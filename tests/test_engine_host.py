@@ -105,6 +105,24 @@ def test_cli_shapes_and_doctor_without_gpu(capsys):
     assert rc == (0 if torch.cuda.is_available() else 1)
 
 
+def test_cli_tune_records_every_schedule(tmp_path, capsys):
+    """Without a device every schedule's run is recorded as an error and no
+    selection is made (exit 1); with no matching GEMM case tune refuses."""
+    from m5kernels_b200 import cli
+
+    if torch.cuda.is_available():
+        pytest.skip("host-only behaviour")
+    out = tmp_path / "tune.json"
+    assert cli.main(["tune", "--suite", "baseline", "--filter", "c1.", "--out", str(out)]) == 1
+    doc = json.loads(out.read_text())
+    assert [tuple(r["schedule"].values()) for r in doc["results"]] == cli.SCHEDULES
+    assert all(r["status"] == "error" for r in doc["results"]) and doc["selections"] == []
+    with pytest.raises(FileExistsError):
+        cli.main(["tune", "--suite", "baseline", "--filter", "c1.", "--out", str(out)])
+    with pytest.raises(ValueError, match="no GEMM cases"):
+        cli.main(["tune", "--suite", "baseline", "--filter", "c4."])
+
+
 def test_rms_case_semantics_are_validated_before_any_device_work():
     from m5kernels_b200 import engine
 

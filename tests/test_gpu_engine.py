@@ -69,3 +69,22 @@ def test_staged_and_fused_backends_agree_exactly(engine, op, backends):
         assert r["status"] == "ok", (r["backend"], r.get("reason"))
         assert r["paired_path_exact"] is True
     assert results[0]["compute_path"] != results[1]["compute_path"]
+
+
+def test_tune_selects_a_schedule_and_passes_the_holdout(tmp_path):
+    """The tune twin: eight schedules of the C1 GEMM, the fastest correct one
+    re-run on a fresh seed (reference: src/m5kernels/cli.py:66-151)."""
+    import json
+
+    from m5kernels_b200 import cli
+
+    out = tmp_path / "tune.json"
+    rc = cli.main(["tune", "--suite", "baseline", "--filter", "c1.", "--warmup", "1",
+                   "--repeat", "3", "--out", str(out)])
+    doc = json.loads(out.read_text())
+    assert rc == 0
+    assert len(doc["results"]) == len(cli.SCHEDULES)
+    assert all(r["status"] == "ok" for r in doc["results"])
+    (sel,) = doc["selections"]
+    assert sel["holdout"]["seed"] == 18 and sel["holdout"]["status"] == "ok"
+    assert sel["holdout"]["schedule"] == sel["schedule"]

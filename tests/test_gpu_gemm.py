@@ -154,6 +154,33 @@ def test_small_m_gemm(ops, shape, mode, monkeypatch):
     assert _lib.device_status() == 0
 
 
+@pytest.mark.parametrize("shape", [(512, 2048, 2048), (256, 512, 4096), (1000, 1000, 3000),
+                                   (4096, 4096, 4096)])
+def test_every_schedule_gives_the_same_output(ops, shape):
+    """The tune twin's schedules (split-K factors, raster groups) change only
+    the time: outputs are bit-identical to the C epilogue under each of them,
+    and the workspace size follows the schedule."""
+    from m5kernels_b200 import _lib, cli
+
+    m, n, k = shape
+    a, b = _operands(m, n, k, seed=47)
+    aq, sa = _q(ops, a)
+    bq, sb = _q(ops, b)
+    expect = co.gemm_epilogue(co.gemm_i8_acc_fast(aq.cpu(), bq.cpu()), sa.cpu(), sb.cpu())
+    lib = _lib.lib()
+    ws_default = lib.m5b_gemm_workspace_bytes(m, n, k, _lib.MODE["int8"])
+    for split_k, group_m in cli.SCHEDULES:
+        with ops.gemm_schedule(split_k, group_m):
+            ws = lib.m5b_gemm_workspace_bytes(m, n, k, _lib.MODE["int8"])
+            if split_k == 0:
+                assert ws == 0
+            y = ops.gemm(aq, bq, "int8", a_scales=sa, b_scales=sb, output_dtype=torch.bfloat16)
+        assert torch.equal(y.cpu(), expect), (split_k, group_m)
+    # leaving the block restores the library's rule
+    assert lib.m5b_gemm_workspace_bytes(m, n, k, _lib.MODE["int8"]) == ws_default
+    assert _lib.device_status() == 0
+
+
 def test_c1_config_w8a8(ops):
     """A [512,2048] ~N(0,1), W [2048,2048] ~N(0,0.02), seed 0."""
     g = torch.Generator().manual_seed(0)
