@@ -56,6 +56,8 @@ extern "C" {
 #define M5B_MODE_FP8 1  /* OCP E4M3 codes (uint8 bits), scale = amax/448 (FP32 accumulation) */
 #define M5B_MODE_BF16 2 /* bf16 operands, FP32 accumulation (GEMM only) */
 #define M5B_MODE_FP16 3 /* fp16 operands, FP32 accumulation (GEMM only) */
+#define M5B_MODE_FP32 4 /* fp32 operands, FP32 accuracy from three TF32 tensor-core products
+                           (GEMM only; needs the m5b_gemm_ex workspace) */
 
 /* normalizations */
 #define M5B_NORM_RMS 1
@@ -213,7 +215,10 @@ M5B_API int m5b_gemm(const void* a, const void* b, int64_t m, int64_t n, int64_t
  * the last of them to finish adds the others' INT32 partial sums (exact) --
  * outputs are bit-identical to the data-parallel schedule.
  * The size depends only on the device's SM count (about 0.25 MB per CTA
- * pair). */
+ * pair).  M5B_MODE_FP32 always needs a workspace: the split operands
+ * [m, 3 K4] and [n, 3 K4] fp32 (K4 = K rounded up to 4), 12 (m + n) K4 bytes
+ * rounded to 256-byte parts.  It is scratch, left overwritten: never share it
+ * with the split-K calls, whose workspace must stay zeroed. */
 M5B_API int64_t m5b_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int mode);
 
 /* GEMM schedule for the calling host thread, the B200 counterpart of the

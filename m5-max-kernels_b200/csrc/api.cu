@@ -88,11 +88,12 @@ int get_encode() {
 
 // K-major [rows, k] operand, boxes of 128 bytes x box_rows, 128-byte swizzle.
 int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int elem_bytes,
-                    int box_rows) {
-  const CUtensorMapDataType dt =
-      elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+                    int box_rows, int64_t ld) {
+  const CUtensorMapDataType dt = elem_bytes == 1   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k * elem_bytes)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>((ld > 0 ? ld : k) * elem_bytes)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem_bytes), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
@@ -487,9 +488,10 @@ struct ScheduleOverride {
 };
 static thread_local ScheduleOverride tl_schedule;
 
+// ld: row stride of A and B in elements (0: k).
 static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMap& tbh,
                        const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
-                       int bn, bool pair) {
+                       int bn, bool pair, int64_t ld = 0) {
   if (m <= 0 || n <= 0 || k <= 0) return fail(M5B_EINVAL, "A and B must be nonempty matrices");
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL)
     return fail(M5B_EUNSUPPORTED, "matrix dimensions exceed 2^31-1");
@@ -500,9 +502,10 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMa
     case M5B_MODE_FP8: kind = KIND_F8; break;
     case M5B_MODE_BF16: kind = KIND_BF16; break;
     case M5B_MODE_FP16: kind = KIND_F16; break;
-    default: return fail(M5B_EUNSUPPORTED, "GEMM modes are int8, fp8, bf16 and fp16");
+    case kModeTf32Parts: kind = KIND_TF32; break;  // the FP32 mode's split [., 3 K4] parts
+    default: return fail(M5B_EUNSUPPORTED, "GEMM modes are int8, fp8, bf16, fp16 and fp32");
   }
-  const int eb = (kind == KIND_BF16 || kind == KIND_F16) ? 2 : 1;
+  const int eb = kind == KIND_TF32 ? 4 : (kind == KIND_BF16 || kind == KIND_F16) ? 2 : 1;
   if (mode == M5B_MODE_FP8 && k % 128)
     return fail(M5B_EUNSUPPORTED,
                 "FP8 requires K/row stride divisible by 128; padding is not implicit");
@@ -514,13 +517,14 @@ static int gemm_common(GemmArgs& g, CUtensorMap& ta, CUtensorMap& tb, CUtensorMa
     return fail(M5B_EINVAL, "operand base addresses must be 16-byte aligned");
   int rc = get_encode();
   if (rc) return rc;
-  rc = make_kmajor_map(&ta, a, m, k, eb, 128);
+  if (ld > 0 && (ld < k || (ld * eb) % 16)) return fail(M5B_EINVAL, "bad operand row stride");
+  rc = make_kmajor_map(&ta, a, m, k, eb, 128, ld);
   if (rc) return rc;
-  rc = make_kmajor_map(&tb, b, n, k, eb, pair ? bn / 2 : bn);
+  rc = make_kmajor_map(&tb, b, n, k, eb, pair ? bn / 2 : bn, ld);
   if (rc) return rc;
   tbh = tb;
   if (pair) {  // half-height B boxes for split tail tiles
-    rc = make_kmajor_map(&tbh, b, n, k, eb, bn / 4);
+    rc = make_kmajor_map(&tbh, b, n, k, eb, bn / 4, ld);
     if (rc) return rc;
   }
   g.M = static_cast<int>(m);
@@ -660,6 +664,12 @@ int m5b_gemm_set_schedule(int split_k, int group_m) {
 }
 
 int64_t m5b_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int mode) {
+  if (mode == M5B_MODE_FP32) {  // the split parts, and the chunks' running sum
+    if (m <= 0 || n <= 0 || k <= 0 || m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL)
+      return 0;
+    return fp32_split_bytes(m, k) + fp32_split_bytes(n, k) +
+           (fp32_chunks(k) > 1 ? (m * n * 4 + 255) / 256 * 256 : 0);
+  }
   if (mode != M5B_MODE_INT8 || m <= 0 || n <= 0 || k <= 0 || !use_pair(EPI_PLAIN, m, n))
     return 0;
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return 0;
@@ -677,11 +687,98 @@ static int gemm_impl(const void* a, const void* b, int64_t m, int64_t n, int64_t
                      const float* a_scales, const float* b_scales, void* out, int out_dtype,
                      const float* bias, const int32_t* bias_row_map, int64_t bias_rows,
                      const void* residual, const void* gate, const int32_t* gate_row_map,
+                     int64_t gate_rows, void* workspace, int64_t workspace_bytes, void* stream);
+
+// FP32 operands (src/m5kernels/metal.py:158-269, mode "fp32"): both operands
+// are split into TF32 parts in the workspace (tf32split.cu), then one TF32
+// GEMM per K chunk of <= kFp32ChunkK columns forms A_hi B_hi + A_hi B_lo +
+// A_lo B_hi over the chunk with FP32 accumulation, each chunk after the first
+// adding the running fp32 result (EPI_ADD_ROWS) -- the accuracy of an FP32
+// GEMM, relative error ~1e-5 at any K.
+static int gemm_fp32(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
+                     const float* a_scales, const float* b_scales, void* out, int out_dtype,
+                     const float* bias, const int32_t* bias_row_map, const void* residual,
+                     const void* gate, const int32_t* gate_row_map, void* workspace,
+                     int64_t workspace_bytes, void* stream) {
+  if (m <= 0 || n <= 0 || k <= 0) return fail(M5B_EINVAL, "A and B must be nonempty matrices");
+  if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL / 3)
+    return fail(M5B_EUNSUPPORTED, "matrix dimensions exceed 2^31-1");
+  if (!a || !b) return fail(M5B_EINVAL, "operand pointer is NULL");
+  if (a_scales || b_scales)
+    return fail(M5B_EINVAL, "float GEMM modes do not accept quantization scales");
+  if (residual || gate || gate_row_map)
+    return fail(M5B_EUNSUPPORTED, "gated GEMM supports INT8 and BF16 only");
+  if (bias || bias_row_map)
+    return fail(M5B_EUNSUPPORTED, "optional GEMM bias currently supports INT8 only");
+  if (out_dtype == M5B_I32)
+    return fail(M5B_EUNSUPPORTED, "int32 accumulator output requires INT8 operands");
+  if (out_dtype != M5B_BF16 && out_dtype != M5B_F16 && out_dtype != M5B_F32)
+    return fail(M5B_EUNSUPPORTED, "output dtype must be bfloat16, float16 or float32");
+  if (!out) return fail(M5B_EINVAL, "output pointer is NULL");
+  if (!aligned(a, 4) || !aligned(b, 4) || !aligned(out, 4))
+    return fail(M5B_EINVAL, "fp32 operands and output must be 4-byte aligned");
+  const long long a_bytes = fp32_split_bytes(m, k), b_bytes = fp32_split_bytes(n, k);
+  const long long chunks = fp32_chunks(k), ck = fp32_chunk_k(k);
+  // running sum of the chunks: the output itself when it is fp32, else scratch
+  const long long part_bytes =
+      (chunks > 1 && out_dtype != M5B_F32) ? (m * n * 4 + 255) / 256 * 256 : 0;
+  const long long need = a_bytes + b_bytes + part_bytes;
+  if (!workspace || workspace_bytes < need)
+    return fail(M5B_EINVAL,
+                "the fp32 GEMM needs m5b_gemm_workspace_bytes(m, n, k, M5B_MODE_FP32) = %lld bytes "
+                "of workspace (m5b_gemm_ex)", need);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* a3 = reinterpret_cast<float*>(ws);
+  float* b3 = reinterpret_cast<float*>(ws + a_bytes);
+  float* partial = part_bytes ? reinterpret_cast<float*>(ws + a_bytes + b_bytes)
+                              : static_cast<float*>(out);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_tf32_split(static_cast<const float*>(a), m, k, chunks, ck, a3, 2, st);
+  if (e == cudaSuccess) e = launch_tf32_split(static_cast<const float*>(b), n, k, chunks, ck, b3, 1, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fp32 operand split launch");
+  for (long long c = 0; c < chunks; ++c) {
+    const bool last = c + 1 == chunks;
+    GemmArgs g{};
+    g.epi = c == 0 ? EPI_PLAIN : EPI_ADD_ROWS;
+    g.N = static_cast<int>(n);
+    const int bn = gemm_block_n(g);
+    const bool pair = use_pair(EPI_PLAIN, m, n);
+    CUtensorMap ta, tb, tbh;
+    int rc = gemm_common(g, ta, tb, tbh, a3 + c * 3 * ck, b3 + c * 3 * ck, m, n, 3 * ck,
+                         kModeTf32Parts, bn, pair, 3 * chunks * ck);
+    if (rc) return rc;
+    g.quantized = 0;
+    g.bias = c == 0 ? nullptr : partial;
+    g.out = last ? out : partial;
+    g.out_dtype = last ? out_dtype : M5B_F32;
+    CUtensorMap to{};
+    if (last && (out_dtype == M5B_BF16 || out_dtype == M5B_F16) && n % 8 == 0 &&
+        aligned(out, 16)) {
+      rc = output_map(&to, out, out_dtype, m, n);
+      if (rc) return rc;
+      g.tma_store = 1;
+      g.ldo = n;
+      rc = gemm_launch(ta, tb, tbh, g, bn, pair, stream, &to);
+    } else {
+      rc = gemm_launch(ta, tb, tbh, g, bn, pair, stream);
+    }
+    if (rc) return rc;
+  }
+  return M5B_OK;
+}
+
+static int gemm_impl(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int mode,
+                     const float* a_scales, const float* b_scales, void* out, int out_dtype,
+                     const float* bias, const int32_t* bias_row_map, int64_t bias_rows,
+                     const void* residual, const void* gate, const int32_t* gate_row_map,
                      int64_t gate_rows, void* workspace, int64_t workspace_bytes, void* stream) {
   if (workspace_bytes < 0 || (workspace_bytes > 0 && !workspace))
     return fail(M5B_EINVAL, "workspace pointer is NULL");
   if (workspace && !aligned(workspace, 256))
     return fail(M5B_EINVAL, "workspace must be 256-byte aligned");
+  if (mode == M5B_MODE_FP32)  // split the operands first
+    return gemm_fp32(a, b, m, n, k, a_scales, b_scales, out, out_dtype, bias, bias_row_map,
+                     residual, gate, gate_row_map, workspace, workspace_bytes, stream);
   GemmArgs g{};
   g.epi = EPI_PLAIN;
   g.N = static_cast<int>(n);

@@ -467,14 +467,15 @@ __device__ __forceinline__ uint64_t smem_desc_k128(uint32_t smem_addr) {
 }
 
 // MMA kinds used by the GEMM.
-enum MmaKind : int { KIND_I8 = 0, KIND_F8 = 1, KIND_BF16 = 2, KIND_F16 = 3 };
+enum MmaKind : int { KIND_I8 = 0, KIND_F8 = 1, KIND_BF16 = 2, KIND_F16 = 3, KIND_TF32 = 4 };
 
 // Instruction descriptor: K-major A and B, dense, M x N (M = 128, or 256 for
 // a CTA pair).
 __host__ __device__ constexpr uint32_t make_idesc(int kind, int m, int n) {
-  // c_format: 1 = F32, 2 = S32; a/b format: S8 -> 1, E4M3 -> 0, BF16 -> 1, F16 -> 0
+  // c_format: 1 = F32, 2 = S32; a/b format: S8 -> 1, E4M3 -> 0, BF16 -> 1, F16 -> 0,
+  // TF32 -> 2 (kind::tf32)
   uint32_t c_fmt = (kind == KIND_I8) ? 2u : 1u;
-  uint32_t ab_fmt = (kind == KIND_I8 || kind == KIND_BF16) ? 1u : 0u;
+  uint32_t ab_fmt = kind == KIND_TF32 ? 2u : (kind == KIND_I8 || kind == KIND_BF16) ? 1u : 0u;
   return (c_fmt << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
 }
@@ -492,6 +493,12 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else if constexpr (KIND == KIND_TF32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
   } else {
@@ -632,6 +639,12 @@ __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uin
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else if constexpr (KIND == KIND_TF32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
   } else {

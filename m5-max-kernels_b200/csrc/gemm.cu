@@ -11,7 +11,8 @@
 //   warp 0     TMA producer: 128-byte K slices of A (128 rows) and B (BN rows)
 //              into a STAGES-deep ring of 128B-swizzled shared-memory tiles.
 //   warp 1     TMEM allocator + single-thread tcgen05.mma issuer
-//              (kind::i8 -> s32, kind::f8f6f4 E4M3 -> f32, kind::f16 -> f32),
+//              (kind::i8 -> s32, kind::f8f6f4 E4M3 -> f32, kind::f16 -> f32,
+//              kind::tf32 -> f32),
 //              M=128, N=BN, K=32 bytes per instruction; tcgen05.commit frees a
 //              ring slot when its MMAs retire.
 //   warps 2-5  epilogue (2-9 on CTA-pair tiles, each warp then draining half
@@ -134,6 +135,10 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
 #pragma unroll
     for (int i = 0; i < 32; ++i)
       if (full || col0 + i < N) v[i] = __fadd_rn(v[i], __ldg(g.bias + boff + col0 + i));
+  } else if (g.epi == EPI_ADD_ROWS) {  // (plain loads: the partial may be the output)
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (full || col0 + i < N) v[i] = __fadd_rn(v[i], g.bias[base + i]);
   } else if (g.epi == EPI_GATE_VEC || g.epi == EPI_GATE_TABLE) {
     const int64_t goff = (g.epi == EPI_GATE_TABLE) ? int64_t(g.gate_row_map[row]) * N : 0;
 #pragma unroll
@@ -241,6 +246,10 @@ __device__ __forceinline__ void epilogue_pack16(const GemmArgs& g, const uint32_
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (full || col0 + i < N) v[i] = __fadd_rn(v[i], __ldg(g.bias + boff + col0 + i));
+    } else if (g.epi == EPI_ADD_ROWS) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (full || col0 + i < N) v[i] = __fadd_rn(v[i], g.bias[base + i]);
     } else if (g.epi == EPI_GATE_VEC || g.epi == EPI_GATE_TABLE) {
       const int64_t goff = (g.epi == EPI_GATE_TABLE) ? int64_t(g.gate_row_map[row]) * N : 0;
 #pragma unroll
@@ -313,7 +322,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
                    const __grid_constant__ CUtensorMap tmap_out_v, const GemmArgs g) {
   using Cfg = GemmCfg<BN, QK, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr int K_ELEMS = (KIND == KIND_BF16 || KIND == KIND_F16) ? 64 : 128;
+  constexpr int K_ELEMS = KIND == KIND_TF32 ? 32 : (KIND == KIND_BF16 || KIND == KIND_F16) ? 64 : 128;
   constexpr uint32_t IDESC = make_idesc(KIND, Cfg::TILE_M, BN);
   constexpr uint32_t IDESC_HALF = make_idesc(KIND, Cfg::TILE_M, BN / 2);
 
@@ -1048,6 +1057,11 @@ cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
     M5B_KIND_CASE(KIND_F8)
     M5B_KIND_CASE(KIND_BF16)
     M5B_KIND_CASE(KIND_F16)
+    case KIND_TF32:  // plain epilogues only (the FP32 GEMM mode)
+      if (qk) return cudaErrorInvalidValue;
+      if (pair) return launch_k<KIND_TF32, 256, false, true>(M5B_ARGS);
+      if (bn == 128) return launch_k<KIND_TF32, 128, false, false>(M5B_ARGS);
+      return launch_k<KIND_TF32, 256, false, false>(M5B_ARGS);
     default: return cudaErrorInvalidValue;
   }
 #undef M5B_KIND_CASE

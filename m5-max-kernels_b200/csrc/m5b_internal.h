@@ -112,6 +112,32 @@ cudaError_t launch_rows16(const RowPrepArgs& a, int x_dtype, int block, int out,
 cudaError_t launch_mxint8(const void* x, int x_dtype, int64_t n, void* q, uint8_t* e,
                           cudaStream_t stream);
 
+// FP32 GEMM mode: out = [rows, chunks, 3, ck] parts (hi, hi|lo, hi|lo) of
+// each ck-column chunk of x [rows, k] (zero past k) for the three-product
+// TF32 GEMM; lo_part (1 or 2) names the part holding x - hi (tf32split.cu).
+cudaError_t launch_tf32_split(const float* x, int64_t rows, int64_t k, int64_t chunks, int64_t ck,
+                              float* out, int lo_part, cudaStream_t stream);
+// Internal GEMM mode of the split parts (never a user mode): TF32 operands.
+constexpr int kModeTf32Parts = 0x100;
+// K chunking of the FP32 mode: chunks of at most kFp32ChunkK columns (a
+// multiple of 4), each one TF32 GEMM over its 3 x CK split columns whose
+// result is added to the previous chunks' with one IEEE add (the tensor
+// core's FP32 accumulator loses up to about half an ulp per MMA step, so its
+// error grows with K; chunks bound it).
+constexpr long long kFp32ChunkK = 2048;
+inline long long fp32_chunks(long long k) {
+  const long long k4 = (k + 3) / 4 * 4;
+  return (k4 + kFp32ChunkK - 1) / kFp32ChunkK;
+}
+inline long long fp32_chunk_k(long long k) {  // CK: columns per chunk
+  const long long k4 = (k + 3) / 4 * 4, s = fp32_chunks(k);
+  return ((k4 + s - 1) / s + 3) / 4 * 4;
+}
+// Bytes of one split operand ([rows, S chunks, 3 parts, CK] fp32, 256-byte rounded).
+inline long long fp32_split_bytes(long long rows, long long k) {
+  return (rows * fp32_chunks(k) * 3 * fp32_chunk_k(k) * 4 + 255) / 256 * 256;
+}
+
 // Staged comparators (staged.cu).
 struct GatedAddArgs {
   const void* residual;        // [rows, K]
@@ -146,6 +172,8 @@ enum Epilogue : int {
   EPI_GATE_VEC = 3,    // out = R[m, n] + bf16(branch) * gate[n]
   EPI_GATE_TABLE = 4,  // out = R[m, n] + bf16(branch) * gate[gate_row_map[m], n]
   EPI_QK = 5,          // bf16 branch -> per-head RMSNorm * gamma -> split-half RoPE
+  EPI_ADD_ROWS = 6,    // ... + bias[m, n]: an fp32 [M, N] partial (the FP32 mode's K chunks;
+                       // plain loads, so bias may be the output itself)
 };
 
 struct GemmArgs {

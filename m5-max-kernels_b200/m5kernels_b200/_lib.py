@@ -18,7 +18,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libm5b200.so"
 # status codes and enums (must match include/m5b200.h)
 OK, EINVAL, EUNSUPPORTED, ECUDA = 0, 1, 2, 3
 F32, F16, BF16, I8, U8, I32 = 0, 1, 2, 3, 4, 5
-MODE = {"int8": 0, "fp8": 1, "bf16": 2, "fp16": 3}
+MODE = {"int8": 0, "fp8": 1, "bf16": 2, "fp16": 3, "fp32": 4}
 NORM = {"rms": 1, "layer": 2}
 DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.int8: I8,
               torch.uint8: U8, torch.int32: I32}

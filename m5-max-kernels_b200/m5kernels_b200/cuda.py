@@ -93,6 +93,10 @@ def gemm(a, b, mode="bf16", tile=(64, 64, 4, 1), a_scales=None, b_scales=None,
          gate_row_map=None):
     """A[M,K] @ B[N,K].T with INT32 (int8) or FP32 accumulation and a fused epilogue.
 
+    mode "fp32" (fp32 operands) runs three TF32 tensor-core products of the
+    operands' TF32 parts (A_hi B_hi + A_hi B_lo + A_lo B_hi): FP32 accuracy
+    (relative error ~1e-6, the reference's bar is 1e-4 relative L2).
+
     Quantized modes: out = (float(acc) * a_scales[m]) * b_scales[n].
     INT8 optionally adds an FP32 bias [N] or a bias table [P,N] selected by
     int32 bias_row_map[M].  INT8/BF16 optionally fuse the gated residual
@@ -109,7 +113,7 @@ def gemm(a, b, mode="bf16", tile=(64, 64, 4, 1), a_scales=None, b_scales=None,
     if k != kb:
         raise ValueError("K mismatch")
     if mode not in _lib.MODE:
-        if mode in ("fp32", "mxint8"):
+        if mode == "mxint8":
             raise NotImplementedError(f"{mode} GEMM is not part of the cuda-b200 backend")
         raise ValueError(f"unknown GEMM mode {mode!r}")
     if mode == "fp8" and k % 128:
@@ -117,14 +121,14 @@ def gemm(a, b, mode="bf16", tile=(64, 64, 4, 1), a_scales=None, b_scales=None,
             "FP8 requires K/row stride divisible by 128; padding is not implicit")
     if mode == "int8" and k > 133144:
         raise NotImplementedError("INT32 worst-case overflow bound exceeded")
-    elem = 1 if mode in ("int8", "fp8") else 2
-    if (k * elem) % 16:
+    elem = {"int8": 1, "fp8": 1, "bf16": 2, "fp16": 2, "fp32": 4}[mode]
+    if mode != "fp32" and (k * elem) % 16:  # (fp32 operands are re-laid out by the split pass)
         # TMA reads K-major rows whose stride must be a multiple of 16 bytes;
         # the reference keeps padding explicit (metal.py:186-190), so does this.
         raise NotImplementedError(
             f"K*{elem} bytes per row must be a multiple of 16 for TMA; padding is not implicit")
     expected = {"int8": (torch.int8,), "fp8": (torch.uint8,), "bf16": (torch.bfloat16,),
-                "fp16": (torch.float16,)}[mode]
+                "fp16": (torch.float16,), "fp32": (torch.float32,)}[mode]
     if a.dtype not in expected or b.dtype not in expected:
         raise ValueError("operand dtypes must match the declared mode")
     out_dtype = output_dtype or torch.float32
@@ -197,9 +201,11 @@ def gemm(a, b, mode="bf16", tile=(64, 64, 4, 1), a_scales=None, b_scales=None,
     lib = _lib.lib()
     # split-K workspace (zero-filled once, left zeroed by every call) for the
     # shapes that take the split schedule; None keeps the data-parallel one
-    from .linear import gemm_workspace
+    from .linear import fp32_workspace, gemm_workspace
 
-    ws = gemm_workspace(dev, int(lib.m5b_gemm_workspace_bytes(m, n, k, _lib.MODE[mode])))
+    nbytes = int(lib.m5b_gemm_workspace_bytes(m, n, k, _lib.MODE[mode]))
+    # (fp32: scratch for the operands' TF32 parts, separate from split-K's)
+    ws = fp32_workspace(dev, nbytes) if mode == "fp32" else gemm_workspace(dev, nbytes)
     check(lib.m5b_gemm_ex(
         ptr(a), ptr(b), m, n, k, _lib.MODE[mode], ptr(a_scales), ptr(b_scales), ptr(out),
         _lib.DTYPE_CODE[out_dtype], ptr(bias), ptr(bias_row_map),

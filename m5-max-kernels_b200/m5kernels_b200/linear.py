@@ -53,6 +53,19 @@ def gemm_workspace(device: torch.device, nbytes: int):
         return buf
 
 
+def fp32_workspace(device: torch.device, nbytes: int):
+    """Cached scratch of the FP32 GEMM mode (its split operands), one per device
+    and stream.  Kept apart from the split-K workspace, which must stay zeroed
+    between calls; this one is overwritten by every FP32 GEMM."""
+    key = _key(device, "fp32")
+    with _ws_lock:
+        buf = _workspaces.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            _workspaces[key] = buf
+        return buf
+
+
 def linear(x, wq, w_scales, mode="int8", *, block_size=0, signs=None,
            output_dtype=torch.bfloat16):
     """y = (acc(quantize(x [D H]), wq) * s_x) * w_scales, one call.

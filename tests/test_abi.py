@@ -95,6 +95,25 @@ def test_gemm_schedule_is_validated_on_the_host():
     assert lib.m5b_gemm_set_schedule(-1, 0) == _lib.OK
 
 
+def test_fp32_gemm_workspace_contract_without_a_gpu():
+    """The FP32 mode's workspace (the operands' TF32 parts) is sized on the host,
+    and a call without it fails before touching the device."""
+    from m5kernels_b200 import _lib
+
+    lib = _lib.lib()
+    fp32 = _lib.MODE["fp32"]
+    # [m, 3 K4] and [n, 3 K4] fp32 parts, each rounded to 256 bytes: K4 = 8 -> 96
+    # bytes a row, 384 -> 512 and 288 -> 512
+    assert lib.m5b_gemm_workspace_bytes(4, 3, 5, fp32) == 1024
+    # K = 3000: two chunks of 1500 columns -> [1000, 2, 3, 1500] parts per operand, and the
+    # chunks' fp32 running sum [1000, 1000]
+    assert lib.m5b_gemm_workspace_bytes(1000, 1000, 3000, fp32) == 2 * 1000 * 9000 * 4 + 4 * 10**6
+    fake = 1 << 20  # aligned, never dereferenced: the call fails first
+    rc = lib.m5b_gemm(fake, fake, 4, 3, 8, fp32, None, None, fake, _lib.F32, None, None, 0,
+                      None, None, None, 0, None)
+    assert rc == _lib.EINVAL and b"workspace" in lib.m5b_last_error()
+
+
 def test_operators_refuse_cpu_tensors():
     import m5kernels_b200 as m
     from m5kernels_b200._lib import ExtensionMissing

@@ -167,6 +167,8 @@ def test_every_schedule_gives_the_same_output(ops, shape):
     aq, sa = _q(ops, a)
     bq, sb = _q(ops, b)
     expect = co.gemm_epilogue(co.gemm_i8_acc_fast(aq.cpu(), bq.cpu()), sa.cpu(), sb.cpu())
+    aq, bq = _pad16(aq), _pad16(bq)  # explicit zero codes: whole 16-byte TMA strides
+    k = aq.shape[1]
     lib = _lib.lib()
     ws_default = lib.m5b_gemm_workspace_bytes(m, n, k, _lib.MODE["int8"])
     for split_k, group_m in cli.SCHEDULES:
@@ -322,3 +324,53 @@ def test_linear_rejects_bad_k(ops):
     wq = torch.ones(8, 40, device=DEV, dtype=torch.int8)
     with pytest.raises(NotImplementedError, match="16"):
         ops.linear(x, wq, torch.ones(8, device=DEV))
+
+
+FP32_SHAPES = [(1, 33, 5), (127, 65, 96), (300, 520, 1023), (512, 2048, 2048), (1000, 1000, 3000),
+               (64, 96, 16384)]
+
+
+@pytest.mark.parametrize("shape", FP32_SHAPES)
+def test_fp32_gemm_has_fp32_accuracy(ops, shape):
+    """FP32 operands (reference mode "fp32", src/m5kernels/metal.py:158-269): three
+    TF32 tensor-core products of the operands' TF32 parts, over K chunks of <= 2048
+    whose fp32 results are added.  Bar: relative L2 <= 5e-5 against the float64
+    product at every K (the reference accepts 1e-4, src/m5kernels/engine.py:473),
+    every output within 1e-4 of its |A| |B| scale; bf16 output is the fp32
+    result rounded; any K (the parts are zero-padded internally)."""
+    m, n, k = shape
+    g = torch.Generator().manual_seed(53)
+    a = torch.randn(m, k, generator=g) * 3.0
+    b = torch.randn(n, k, generator=g) * 0.02
+    y = ops.gemm(a.to(DEV), b.to(DEV), "fp32").cpu()
+    assert y.dtype == torch.float32
+    ref64 = a.double() @ b.double().T
+    assert ref.metrics(y.double().numpy(), ref64.numpy())["relative_l2"] <= 5e-5
+    scale = (a.double().abs() @ b.double().abs().T)
+    assert float(((y.double() - ref64).abs() / scale.clamp_min(1e-30)).max()) <= 1e-4
+    yb = ops.gemm(a.to(DEV), b.to(DEV), "fp32", output_dtype=torch.bfloat16).cpu()
+    assert torch.equal(yb, y.to(torch.bfloat16))
+
+
+def test_fp32_gemm_special_values_and_contract(ops):
+    """Infinities and NaNs propagate; scales, bias and gate are refused as for the
+    other float modes; the C entry point without a workspace says what it needs."""
+    from m5kernels_b200 import _lib
+
+    a = torch.ones(4, 8)
+    b = torch.ones(3, 8)
+    a[1, 2] = float("inf")
+    a[2, 0] = float("nan")
+    y = ops.gemm(a.to(DEV), b.to(DEV), "fp32").cpu()
+    assert torch.isinf(y[1]).all() and torch.isnan(y[2]).all()
+    assert torch.equal(y[0], torch.full((3,), 8.0)) and torch.equal(y[3], torch.full((3,), 8.0))
+    with pytest.raises(ValueError):
+        ops.gemm(a.to(DEV), b.to(DEV), "fp32", a_scales=torch.ones(4, device=DEV),
+                 b_scales=torch.ones(3, device=DEV))
+    with pytest.raises(NotImplementedError, match="INT8 only"):
+        ops.gemm(a.to(DEV), b.to(DEV), "fp32", bias=torch.ones(3, device=DEV))
+    out = torch.empty(4, 3, device=DEV)
+    ad, bd = a.to(DEV), b.to(DEV)
+    rc = _lib.lib().m5b_gemm(ad.data_ptr(), bd.data_ptr(), 4, 3, 8, _lib.MODE["fp32"], None, None,
+                             out.data_ptr(), _lib.F32, None, None, 0, None, None, None, 0, None)
+    assert rc == _lib.EINVAL and b"workspace" in _lib.lib().m5b_last_error()
