@@ -135,37 +135,72 @@ __device__ __forceinline__ uint32_t max_xorsign_abs_f16x2(uint32_t a, uint32_t b
   return d;
 }
 
-// OCP E4M3 code with round-to-nearest-even and saturation to +-448.
-__device__ __forceinline__ uint8_t e4m3_code(float v, float scale) {
-  float z = __fdiv_rn(v, scale);
-  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(z, __NV_SATFINITE, __NV_E4M3));
+// Exact E4M3 codes of four values (divide, then convert); out of line: it
+// runs only for words whose brackets disagree (a product within 2^-18 of a
+// rounding boundary) and for scales below 2^-100.
+static __device__ __noinline__ uint32_t e4m3_word_exact(float a, float b, float c, float d,
+                                                        float scale) {
+  return __nv_cvt_float2_to_fp8x2(make_float2(__fdiv_rn(a, scale), __fdiv_rn(b, scale)),
+                                  __NV_SATFINITE, __NV_E4M3) |
+         (static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(
+              make_float2(__fdiv_rn(c, scale), __fdiv_rn(d, scale)), __NV_SATFINITE, __NV_E4M3))
+          << 16);
 }
 
-// E4M3 codes of four values (v[0..3] -> bytes 0..3 of the word), two at a
-// time with the paired conversion (the .x value lands in the low byte).
-// Exactness: with a power-of-two scale (exact reciprocal) v * inv is the
-// quotient itself; otherwise v * inv * (1 -+ 2^-18) bracket RN(v / scale),
-// and the conversion is monotone, so a pair whose lower and upper bracket
-// codes agree has those codes; a pair where they differ is divided exactly.
+// OCP E4M3 codes (round to nearest even, saturated to +-448) of x / scale for
+// NW words of 4 values (v[4w .. 4w+3] -> bytes 0..3 of word w), with the
+// paired conversion.  Exactness: with a power-of-two scale (exact
+// reciprocal) v * inv is the quotient itself and is converted once;
+// otherwise v * inv * (1 -+ 2^-18) bracket RN(v / scale) and the conversion
+// is monotone, so a word whose lower and upper bracket codes agree has those
+// codes.  The words whose brackets disagree are collected in one mask and
+// only those are divided exactly (one rarely taken branch per NW words).
 // `fast` is false for scales below 2^-100 (every value divided exactly).
-__device__ __forceinline__ uint32_t e4m3_pair_code(float a, float b, float scale, float inv,
-                                                   bool fast, bool exact_inv) {
-  if (fast) {
-    const float2 t = __fmul2_rn(make_float2(a, b), make_float2(inv, inv));
-    if (exact_inv) return __nv_cvt_float2_to_fp8x2(t, __NV_SATFINITE, __NV_E4M3);
-    const uint32_t lo = __nv_cvt_float2_to_fp8x2(
-        __fmul2_rn(t, make_float2(1.0f - 0x1p-18f, 1.0f - 0x1p-18f)), __NV_SATFINITE, __NV_E4M3);
-    const uint32_t hi = __nv_cvt_float2_to_fp8x2(
-        __fmul2_rn(t, make_float2(1.0f + 0x1p-18f, 1.0f + 0x1p-18f)), __NV_SATFINITE, __NV_E4M3);
-    if (lo == hi) return lo;
+template <int NW>
+__device__ __forceinline__ void e4m3_words(const float* v, float scale, float inv, bool fast,
+                                           uint32_t* words) {
+  if (!fast) {
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+      words[w] = e4m3_word_exact(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3], scale);
+    return;
   }
-  return __nv_cvt_float2_to_fp8x2(make_float2(__fdiv_rn(a, scale), __fdiv_rn(b, scale)),
-                                  __NV_SATFINITE, __NV_E4M3);
-}
-__device__ __forceinline__ uint32_t e4m3_word(const float* v, float scale, float inv, bool fast) {
-  const bool exact_inv = (__float_as_uint(scale) & 0x007FFFFFu) == 0u;
-  return e4m3_pair_code(v[0], v[1], scale, inv, fast, exact_inv) |
-         (e4m3_pair_code(v[2], v[3], scale, inv, fast, exact_inv) << 16);
+  const float2 inv2 = make_float2(inv, inv);
+  if ((__float_as_uint(scale) & 0x007FFFFFu) == 0u) {  // exact reciprocal
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+      words[w] = __nv_cvt_float2_to_fp8x2(__fmul2_rn(make_float2(v[4 * w], v[4 * w + 1]), inv2),
+                                          __NV_SATFINITE, __NV_E4M3) |
+                 (static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(
+                      __fmul2_rn(make_float2(v[4 * w + 2], v[4 * w + 3]), inv2), __NV_SATFINITE,
+                      __NV_E4M3))
+                  << 16);
+    return;
+  }
+  const float2 dn = make_float2(1.0f - 0x1p-18f, 1.0f - 0x1p-18f);
+  const float2 up = make_float2(1.0f + 0x1p-18f, 1.0f + 0x1p-18f);
+  uint32_t bad = 0u;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    const float2 t0 = __fmul2_rn(make_float2(v[4 * w], v[4 * w + 1]), inv2);
+    const float2 t1 = __fmul2_rn(make_float2(v[4 * w + 2], v[4 * w + 3]), inv2);
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(__fmul2_rn(t0, dn), __NV_SATFINITE, __NV_E4M3) |
+                        (static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(
+                             __fmul2_rn(t1, dn), __NV_SATFINITE, __NV_E4M3))
+                         << 16);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(__fmul2_rn(t0, up), __NV_SATFINITE, __NV_E4M3) |
+                        (static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(
+                             __fmul2_rn(t1, up), __NV_SATFINITE, __NV_E4M3))
+                         << 16);
+    words[w] = lo;
+    bad |= (lo != hi ? 1u : 0u) << w;
+  }
+  if (bad != 0u) {
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+      if ((bad >> w) & 1u)
+        words[w] = e4m3_word_exact(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3], scale);
+  }
 }
 
 // Q/K post-processing on packed pairs (GEMM epilogue and the staged kernel).

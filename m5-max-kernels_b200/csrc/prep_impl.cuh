@@ -685,8 +685,7 @@ __global__ void __launch_bounds__(512)
 #pragma unroll
           for (int w0 = 0; w0 < kChunk / 4; w0 += 4) {
             uint32_t words[4];
-#pragma unroll
-            for (int w = 0; w < 4; ++w) words[w] = e4m3_word(v + 4 * (w0 + w), scale, rinv, fast);
+            e4m3_words<4>(v + 4 * w0, scale, rinv, fast, words);
             *reinterpret_cast<uint4*>(qrow + j0 + 4 * w0) =
                 make_uint4(words[0], words[1], words[2], words[3]);
           }

@@ -143,8 +143,7 @@ __device__ __forceinline__ void vec_codes(const uint4& raw, float scale, float i
   float v[V];
   if constexpr (OUT == OUT_E4M3) {
     unpack<T>(raw, v);
-#pragma unroll
-    for (int w = 0; w < V / 4; ++w) words[w] = e4m3_word(v + 4 * w, scale, inv, fast);
+    e4m3_words<V / 4>(v, scale, inv, fast, words);
   } else {
     if (fast) {
       if (pack_i8_vec<T>(raw, i8_bracket(inv, scale), words) != 0u) {

@@ -533,11 +533,8 @@ __global__ void __launch_bounds__(kThreads, MODE == kPlain ? 2 : 1)
           const float2* p = v + 8 * grp16;
           uint32_t words[4];
           if constexpr (OUT == OUT_E4M3) {
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              const float q4[4] = {p[2 * w].x, p[2 * w].y, p[2 * w + 1].x, p[2 * w + 1].y};
-              words[w] = e4m3_word(q4, scale, rinv, fast);
-            }
+            // the 8 pairs are 16 consecutive floats in element order
+            e4m3_words<4>(reinterpret_cast<const float*>(p), scale, rinv, fast, words);
           } else if (fast) {
             const I8Bracket br = i8_bracket(rinv, scale);
             uint32_t acc = 0u;

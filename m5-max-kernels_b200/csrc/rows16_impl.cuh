@@ -528,8 +528,7 @@ __global__ void __launch_bounds__(MAXT) __maxnreg__(MODE == kNormGated && MAXT =
           const float rinv = __frcp_rn(scale);
           const bool fast = scale >= 0x1p-100f;
           if constexpr (OUT == OUT_E4M3) {
-#pragma unroll
-            for (int w = 0; w < 4; ++w) words[w] = e4m3_word(vv + 4 * w, scale, rinv, fast);
+            e4m3_words<4>(vv, scale, rinv, fast, words);
           } else if (fast) {
             quant_i8_fast16(vv, scale, rinv, words);
           } else {
