@@ -46,7 +46,7 @@ WORKLOAD = "ffn_down_w8a8_online_quant_M4096_K16384_N4096"
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
 # the GEMM kernel, from ncu captures of this workload's per-rank shapes
 # (rows per rank -> bytes).  Recorded constants, not measured by this script.
-GEMM_TRAFFIC_BYTES = {4096: 315609088 + 24830976, 512: 75607552 + 3584512}
+GEMM_TRAFFIC_BYTES = {4096: 252967680 + 24065024, 512: 75607552 + 3584512}
 GEMM_TRAFFIC_SOURCE = ("ncu capture (1 launch, dram__bytes_read.sum + dram__bytes_write.sum) of "
                        "gemm_tc_kernel<i8,256,pair> on the per-rank shape; recorded constant")
 

@@ -453,7 +453,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
       int issued = 0;
       long long cur = work_start;
       Work w;
+      // INT8 data-parallel tiles walk K forward and backward in turn, so a
+      // tile starts on the k-slices its predecessor (and the other pairs of
+      // the same wave) just left in L2: fewer operand re-reads from DRAM.
+      // INT32 sums are exact in any order, so the result does not change;
+      // FP32-accumulating kinds keep the forward order.  Both CTAs of a pair
+      // walk the same work items, so they agree on the direction.
+      int tiles_done = 0;
       while (!*abort_flag && next_work(cur, w)) {
+        const bool backward = KIND == KIND_I8 && !sk && (tiles_done++ & 1);
         const int a_row = w.m_blk * Cfg::TILE_M + static_cast<int>(rank) * kBM;
         const int b_rows = w.whole ? Cfg::B_ROWS : Cfg::B_ROWS / 2;
         const int b_row = w.n_col + static_cast<int>(rank) * b_rows;
@@ -463,17 +471,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, g.status,
                                  DEV_TIMEOUT_PRODUCER))
             break;
+          const int kx = (backward ? w.kb1 - 1 - (kb - w.kb0) : kb) * K_ELEMS;
           if constexpr (PAIR) {
             // The even CTA expects both CTAs' bytes; each CTA loads its halves.
             if (leader) mbar_arrive_expect_tx(&full[stage], 2 * stage_bytes);
-            tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmap_a, &full[stage], kb * K_ELEMS,
-                             a_row);
-            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, bmap, &full[stage], kb * K_ELEMS,
-                             b_row);
+            tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmap_a, &full[stage], kx, a_row);
+            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, bmap, &full[stage], kx, b_row);
           } else {
             mbar_arrive_expect_tx(&full[stage], stage_bytes);
-            tma_load_2d(sA + stage * Cfg::A_BYTES, &tmap_a, &full[stage], kb * K_ELEMS, a_row);
-            tma_load_2d(sB + stage * Cfg::B_BYTES, bmap, &full[stage], kb * K_ELEMS, b_row);
+            tma_load_2d(sA + stage * Cfg::A_BYTES, &tmap_a, &full[stage], kx, a_row);
+            tma_load_2d(sB + stage * Cfg::B_BYTES, bmap, &full[stage], kx, b_row);
           }
           ++issued;
           if (++stage == STAGES) {
