@@ -226,9 +226,12 @@ M5B_API int64_t m5b_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int mo
  * swept by `m5bench tune`, src/m5kernels/cli.py:66-151).  It changes how
  * the work is scheduled, never the result (outputs are bit-identical under
  * every schedule).  split_k: -1 the library's rule, 0 data-parallel,
- * 2..4 that many CTA pairs per 256 x 256 tile over equal K ranges -- taken
- * by INT8 CTA-pair GEMMs given a workspace when all tiles x splits fit on the
- * GPU at once and each split keeps >= 8 k-blocks, else data-parallel.
+ * 2 two CTA pairs per 256 x 256 tile in one 4-CTA cluster, the second
+ * pair's INT32 partial sums moved into the first pair's shared memory (no
+ * workspace; tiles filling at most half of the pairs), 3..4 that many CTA
+ * pairs per tile over equal K ranges through the workspace -- taken by INT8
+ * CTA-pair GEMMs given one when all tiles x splits fit on the GPU at once;
+ * every split keeps >= 8 k-blocks, else data-parallel.
  * group_m: 0 the library's raster, else M-blocks walked per N-block group.
  * Every GEMM entry point called later from this thread uses it (also
  * m5b_gemm_workspace_bytes) until (-1, 0) restores the defaults.  No

@@ -582,8 +582,8 @@ static int output_map(CUtensorMap* map, void* out, int out_dtype, int64_t m, int
 // resident at once (T x S <= slots) and every split keeps kSplitKMinBlocks
 // k-blocks; otherwise the GEMM runs data-parallel.
 static int splitk_factor(int tiles, int nkb, int slots) {
-  if (tl_schedule.split_k == 0) return 0;
-  if (tl_schedule.split_k >= 2) {
+  if (tl_schedule.split_k == 0 || tl_schedule.split_k == 2) return 0;  // (2: cluster split-K)
+  if (tl_schedule.split_k >= 3) {
     const int s = tl_schedule.split_k;
     if (tiles <= 0 || int64_t(tiles) * s > slots || nkb / s < kSplitKMinBlocks) return 0;
     return s;
@@ -598,6 +598,19 @@ static int splitk_factor(int tiles, int nkb, int slots) {
   if (s > kSplitKMaxSplits) s = kSplitKMaxSplits;
   while (s >= 2 && nkb / s < kSplitKMinBlocks) --s;
   return s >= 2 ? s : 0;
+}
+
+// Cluster split-K (two pairs per tile in one 4-CTA cluster, partial sums
+// through shared memory, no workspace), on request (m5b_gemm_set_schedule
+// split_k = 2): INT8 CTA-pair GEMMs whose 256 x 256 tiles fill at most half
+// of the pairs, with >= kSplitKMinBlocks k-blocks per half.  Whole tiles on
+// two pairs move 2/3 of the operand bytes of the 64 N-halves they replace at
+// 512 rows of FFN-down, but measured the same step (44.5-45.0 against 44.6
+// us; GEMM 41.4 against 42.4 us between events), so the library's own rule
+// keeps the data-parallel halves there.
+static bool cluster_splitk(int tiles, int nkb, int slots) {
+  if (tl_schedule.split_k != 2) return false;
+  return tiles > 0 && 2 * tiles <= slots && nkb / 2 >= kSplitKMinBlocks;
 }
 
 static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh,
@@ -616,6 +629,7 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   g.num_full = tiles;
   g.num_units = tiles;
   g.sk = 0;
+  g.sk_cluster = 0;
   const int rem = tiles % slots;
   if (pair && tiles > slots && rem > 0 && 2 * rem <= slots) {
     g.num_full = tiles - rem;
@@ -646,6 +660,16 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
       g.num_units = tiles;
       grid = 2 * tiles * splits;
     }
+  }
+  if (!g.sk && pair && bn == 256 && g.kind == KIND_I8 && g.n_peers == 0 &&
+      cluster_splitk(tiles, g.num_k_blocks, slots)) {
+    g.sk = 1;
+    g.sk_cluster = 1;
+    g.sk_splits = 2;
+    g.sk_tiles = tiles;
+    g.num_full = tiles;
+    g.num_units = tiles;
+    grid = 4 * tiles;  // clusters of two pairs, one per tile
   }
   const CUtensorMap& o = to ? *to : tbh;
   cudaError_t e = launch_gemm(ta, tb, tbh, o, to_k ? *to_k : o, to_v ? *to_v : o, g, bn, grid,

@@ -652,12 +652,23 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
 }
-// Arrive on `bar` in both CTAs of the pair once the MMAs issued so far retire.
-__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+// Arrive on `bar` in both CTAs of the pair once the MMAs issued so far retire;
+// `pair_mask` names the pair's two CTAs in the cluster (0b11 << even rank).
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t pair_mask = 3) {
   asm volatile(
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
       " [%0], %1;" ::"r"(smem_u32(bar)),
-      "h"(static_cast<uint16_t>(3))
+      "h"(pair_mask)
+      : "memory");
+}
+// Bulk copy of `bytes` (a multiple of 16, 16-byte aligned) from this CTA's
+// shared memory into another CTA's of the cluster (cluster address from
+// map_to_rank), completing the transaction bytes on that CTA's mbarrier.
+__device__ __forceinline__ void bulk_copy_s2cluster(uint32_t dst_cluster, const void* src,
+                                                    uint32_t bytes, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst_cluster), "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
       : "memory");
 }
 

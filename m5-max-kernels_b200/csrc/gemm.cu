@@ -58,7 +58,7 @@ struct GemmCfg {
   // (Q/K pair tiles: 5 stages beside their 64 KB of staging.)
   static constexpr int STAGES = QK ? 5 : (STAGE_BYTES <= 32 * 1024 ? 6 : 4);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int BAR_BYTES = (2 * STAGES + 6) * 8 + 32;
+  static constexpr int BAR_BYTES = (2 * STAGES + 7) * 8 + 32;
   // Epilogue warps: 4, or 8 for pair tiles (each warp drains one of the tile's
   // two heads (Q/K), or half of its columns, for its 32 rows).
   static constexpr int EPI_WARPS = PAIR ? 8 : 4;
@@ -338,7 +338,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint64_t* fix_bar = drain + 1;  // split-K: partner partial sums landed in shared memory
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fix_bar + 1);
+  uint64_t* recv_ready = fix_bar + 1;  // cluster split-K: the receiving CTA's ring is free
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_ready + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // split-K hand-offs between the epilogue warps of this CTA (see below)
   volatile int* sk_ticket = reinterpret_cast<volatile int*>(tmem_slot + 2);
@@ -347,7 +348,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t rank = PAIR ? cluster_rank() : 0;  // position in the CTA pair
+  // Clusters are one CTA pair, or two pairs (ranks 0-1 and 2-3) under the
+  // cluster split-K schedule.
+  const uint32_t crank = PAIR ? cluster_rank() : 0;  // rank in the cluster
+  const uint32_t rank = crank & 1u;                   // position in the CTA pair
+  const uint32_t pair_even = crank & ~1u;             // the pair's even CTA
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << pair_even);
   const bool leader = rank == 0;
   const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
@@ -363,6 +369,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     }
     mbar_init(drain, 1);
     mbar_init(fix_bar, 1);
+    mbar_init(recv_ready, 1);
     *abort_flag = 0;
     *sk_ticket = 0;
     *sk_signal = 0;
@@ -390,7 +397,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote use
+  if constexpr (PAIR) cluster_sync();  // every CTA's barriers exist before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -411,8 +418,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     int n_blk;
     if (sk) {  // one item: a tile and this pair's K range of it
       if (cur != unit) return false;
-      w.tile = unit % g.sk_tiles;
-      const int split = unit / g.sk_tiles;
+      // cluster split-K: the two pairs of cluster c take tile c, splits 0 / 1
+      w.tile = g.sk_cluster ? unit >> 1 : unit % g.sk_tiles;
+      const int split = g.sk_cluster ? unit & 1 : unit / g.sk_tiles;
       w.kb0 = split * nkb / g.sk_splits;
       w.kb1 = (split + 1) * nkb / g.sk_splits;
       w.first = true;
@@ -547,7 +555,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
                            smem_desc_k128(b_base + k * 32), idesc, accumulate);
           }
           if constexpr (PAIR)
-            tc_commit_pair(&empty[stage]);
+            tc_commit_pair(&empty[stage], pair_mask);
           else
             tc_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -557,14 +565,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
         }
         if (!ok) break;
         if constexpr (PAIR)
-          tc_commit_pair(&acc_full[acc]);
+          tc_commit_pair(&acc_full[acc], pair_mask);
         else
           tc_commit(&acc_full[acc]);
       }
       if (!ok) {
         // Aborted: let every MMA already issued retire before TMEM is freed.
         if constexpr (PAIR)
-          tc_commit_pair(drain);
+          tc_commit_pair(drain, pair_mask);
         else
           tc_commit(drain);
         const unsigned long long t0 = globaltimer_ns();
@@ -582,8 +590,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
     const int ehalf = (warp - 2) >> 2;  // 8-warp Q/K epilogue: which head of the tile
     const int row_in_tile = static_cast<int>(rank) * kBM + quarter * 32 + lane;
     // acc_empty lives in the even CTA of a pair: the odd CTA arrives remotely.
-    const uint32_t acc_empty_remote0 = PAIR ? map_to_rank(&acc_empty[0], 0) : 0u;
-    const uint32_t acc_empty_remote1 = PAIR ? map_to_rank(&acc_empty[1], 0) : 0u;
+    const uint32_t acc_empty_remote0 = PAIR ? map_to_rank(&acc_empty[0], pair_even) : 0u;
+    const uint32_t acc_empty_remote1 = PAIR ? map_to_rank(&acc_empty[1], pair_even) : 0u;
     auto release_acc = [&](int acc) {
       if constexpr (PAIR)
         mbar_arrive_cluster(acc == 0 ? acc_empty_remote0 : acc_empty_remote1);
@@ -632,7 +640,80 @@ __global__ void __launch_bounds__(GemmCfg<BN, QK, PAIR>::THREADS, 1)
       // into the ring and adds it into its own TMEM accumulator; the ordinary
       // epilogue then reads complete sums.  (All of this CTA's MMAs have
       // retired once acc_full completed, so the ring's 192 KB are free.)
-      if (sk) {
+      if (sk && g.sk_cluster) {
+        // Cluster split-K: this cluster's two pairs took the two K halves of
+        // one tile.  The second pair (ranks 2-3) stages its partial sums in
+        // its idle ring and bulk-copies them into the ring of its
+        // counterpart in the first pair (rank - 2: the same 128 rows), once
+        // that CTA has announced its own MMAs done (recv_ready, its ring is
+        // then free) and armed its fix_bar for the bytes.  The first pair
+        // adds them into its TMEM accumulator and runs the epilogue.
+        uint4* ring = reinterpret_cast<uint4*>(smem);  // [chunk][4 words][row] uint4
+        constexpr int kChunks = BN / 32;
+        const int c_first = Cfg::EPI_WARPS == 8 ? ehalf * (kChunks / 2) : 0;
+        const int c_end = Cfg::EPI_WARPS == 8 ? c_first + kChunks / 2 : kChunks;
+        constexpr uint32_t kSlotBytes = kBM * BN * 4;
+        if (crank >= 2) {  // sender
+#pragma unroll 1
+          for (int c = c_first; c < c_end; ++c) {
+            uint32_t r[32];
+            tmem_ld32(taddr + c * 32, r);
+            tmem_wait_ld();
+            if (c == c_end - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) release_acc(acc);
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              ring[(c * 8 + q) * kBM + prow] =
+                  make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          }
+          fence_proxy_async_shared();  // the bulk copy (async proxy) reads these writes
+          __syncwarp();
+          stored_expect += Cfg::EPI_WARPS;
+          if (lane == 0) atomicAdd(sk_stored, 1);
+          if (sk_leader) {
+            spin_shared_at_least(sk_stored, stored_expect, abort_flag, g.status);
+            if (!*abort_flag &&
+                mbar_wait_bounded(recv_ready, 0, abort_flag, g.status, DEV_TIMEOUT_FIXUP)) {
+              const uint32_t dst = map_to_rank(ring, crank - 2);
+              const uint32_t bar = map_to_rank(fix_bar, crank - 2);
+              for (uint32_t off = 0; off < kSlotBytes; off += 16384)
+                bulk_copy_s2cluster(dst + off, reinterpret_cast<const uint8_t*>(ring) + off, 16384,
+                                    bar);
+            }
+          }
+          __syncwarp();
+          continue;  // (the kernel's closing cluster barrier keeps this ring alive until read)
+        }
+        if (sk_leader) {  // receiver: arm fix_bar, then let the sender copy
+          mbar_arrive_expect_tx(fix_bar, kSlotBytes);
+          mbar_arrive_cluster(map_to_rank(recv_ready, crank + 2));
+        }
+        if (!mbar_wait_bounded(fix_bar, fix_phase, abort_flag, g.status, DEV_TIMEOUT_FIXUP))
+          break;
+        fix_phase ^= 1u;
+#pragma unroll 1
+        for (int c = c_first; c < c_end; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint4 pv = ring[(c * 8 + q) * kBM + prow];
+            r[4 * q] += pv.x;
+            r[4 * q + 1] += pv.y;
+            r[4 * q + 2] += pv.z;
+            r[4 * q + 3] += pv.w;
+          }
+          tmem_st32(taddr + c * 32, r);
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        tc_fence_after();
+      } else if (sk) {
         const int others = g.sk_splits - 1;
         int* ctr = g.sk_ctr + (w.tile * 2 + static_cast<int>(rank)) * 2;
         uint4* ring = reinterpret_cast<uint4*>(smem);  // [chunk][4 words][row] uint4
@@ -1028,7 +1109,7 @@ static cudaError_t launch_k(const CUtensorMap& ta, const CUtensorMap& tb, const 
   unsigned n_attr = 0;
   if (PAIR) {
     attr[n_attr].id = cudaLaunchAttributeClusterDimension;
-    attr[n_attr].val.clusterDim.x = 2;
+    attr[n_attr].val.clusterDim.x = g.sk && g.sk_cluster ? 4 : 2;
     attr[n_attr].val.clusterDim.y = 1;
     attr[n_attr].val.clusterDim.z = 1;
     ++n_attr;

@@ -228,6 +228,10 @@ struct GemmArgs {
   // at zero and the finishing pair resets them, so they are zero again after
   // every launch.
   int sk;                     // 1: split-K schedule
+  // 1: cluster split-K -- the launch is clusters of four CTAs (two pairs),
+  // one cluster per tile, S = 2; the second pair's partial sums move into
+  // the first pair's shared memory by a bulk copy (no workspace, no tickets)
+  int sk_cluster;
   int sk_splits;              // S >= 2 pairs per tile
   int sk_tiles;               // T tiles; the launch has T * S CTA pairs
   int* sk_ctr;                // [tiles][2 CTAs][ticket, done]

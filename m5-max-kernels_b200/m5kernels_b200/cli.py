@@ -86,9 +86,10 @@ def _bench(args) -> int:
     return 1 if bad else 0
 
 
-# (split_k, group_m): the library's rule, data-parallel, split-K factors,
-# raster groups of 1, 4 and 16 M-blocks -- eight candidates, as the reference
-# sweeps eight tiles.
+# (split_k, group_m): the library's rule, data-parallel, cluster split-K (2:
+# two CTA pairs per tile through shared memory), split-K 3 and 4 through the
+# workspace, raster groups of 1, 4 and 16 M-blocks -- eight candidates, as
+# the reference sweeps eight tiles.
 SCHEDULES = [(-1, 0), (0, 0), (2, 0), (3, 0), (4, 0), (-1, 1), (-1, 4), (-1, 16)]
 
 

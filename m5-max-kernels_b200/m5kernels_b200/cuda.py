@@ -32,8 +32,10 @@ def gemm_schedule(split_k: int = -1, group_m: int = 0):
 
     The B200 counterpart of the reference's Metal `tile` (what `m5bench tune`
     sweeps, src/m5kernels/cli.py:66-151): split_k -1 = the library's rule,
-    0 = data-parallel, 2..4 = CTA pairs per 256 x 256 tile over equal K ranges
-    (INT8 GEMMs with a workspace, where every unit fits on the GPU at once);
+    0 = data-parallel, 2 = two CTA pairs per 256 x 256 tile in one 4-CTA
+    cluster (partial sums through shared memory), 3..4 = CTA pairs per tile
+    over equal K ranges through the workspace (INT8 GEMMs, where every unit
+    fits on the GPU at once);
     group_m 0 = the library's raster, else M-blocks per raster group.  Results
     are identical under every schedule; only the time changes.
     """

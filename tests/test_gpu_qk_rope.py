@@ -131,3 +131,27 @@ def test_qk_rope_splitk_bit_exact(ops, shape, monkeypatch):
     dp = ops.projection_qk_rope(*args, a_scales=sa, b_scales=sb, epsilon=1e-5)
     assert torch.equal(dp, y)
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("shape", [(512, 4096, 4096), (600, 1408, 8192)])
+def test_qk_rope_cluster_splitk_bit_exact(ops, shape):
+    """The cluster split-K schedule (two CTA pairs per tile in one 4-CTA
+    cluster, partial sums through shared memory) under the Q/K epilogue:
+    bit-identical to the C epilogue and to the data-parallel schedule."""
+    from m5kernels_b200 import _lib
+
+    m, n, k = shape
+    half = 64
+    x, w, gamma, cos, sin = _inputs(m, n, k, half, seed=67)
+    aq, sa = ops.quantize(x.to(DEV), "int8")
+    bq, sb = ops.quantize(w.to(DEV), "int8")
+    args = (aq, bq, gamma.to(DEV), cos.to(DEV), sin.to(DEV), "int8")
+    with ops.gemm_schedule(2, 0):
+        y = ops.projection_qk_rope(*args, a_scales=sa, b_scales=sb, epsilon=1e-5)
+    acc = co.gemm_i8_acc_fast(aq.cpu(), bq.cpu()).float()
+    expect = co.qk_rope_from_acc(acc, sa.cpu(), sb.cpu(), gamma, cos, sin, half, 1e-5)
+    assert torch.equal(y.cpu(), expect)
+    with ops.gemm_schedule(0, 0):
+        dp = ops.projection_qk_rope(*args, a_scales=sa, b_scales=sb, epsilon=1e-5)
+    assert torch.equal(dp, y)
+    assert _lib.device_status() == 0
