@@ -833,6 +833,20 @@ def run_b200(args, world, rank, local):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
     e2e_value = (ops_job if world > 1 else ops_rank) / (e2e_ms * 1e-3) / 1e12
 
+    # The link's own ceiling for the e2e copies: the same pinned host -> device
+    # copies of the activations, back to back with nothing else running.
+    c0 = torch.cuda.Event(enable_timing=True)
+    c1 = torch.cuda.Event(enable_timing=True)
+    dev_a[0].copy_(host_a[0], non_blocking=True)
+    torch.cuda.synchronize()
+    c0.record(stream)
+    for i in range(e2e_steps):
+        dev_a[i % 2].copy_(host_a[i % nsets], non_blocking=True)
+    c1.record(stream)
+    torch.cuda.synchronize()
+    h2d_copy_ms = max_over_ranks(c0.elapsed_time(c1) / e2e_steps)
+    h2d_bytes = m * K * 2
+
     peaks = _peaks()
     int8_peak = 2.0 * peaks["bf16"]  # dense INT8 = 2x dense BF16 on B200 (4.5 / 2.25 PF nominal)
     gemm_tops = ops_rank / (gemm_ms_max * 1e-3) / 1e12
@@ -867,7 +881,13 @@ def run_b200(args, world, rank, local):
                                                  "threads")} if cb else None),
             "cpu_baseline_omp": omp,
             "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": m * K * 2,
-                    "d2h_bytes_per_step": m * N * 2, "api": "m5b_linear_ex"},
+                    "d2h_bytes_per_step": m * N * 2, "api": "m5b_linear_ex",
+                    # host -> device rate inside the e2e steps against the same
+                    # copies timed alone (the PCIe ceiling of this path)
+                    "link": {"bound": "host->device copies",
+                             "h2d_gbs_in_e2e": h2d_bytes / (e2e_ms * 1e-3) / 1e9,
+                             "h2d_gbs_copies_alone": h2d_bytes / (h2d_copy_ms * 1e-3) / 1e9,
+                             "frac": h2d_copy_ms / e2e_ms}},
             "clocks": clock,
             "gpu_launches": 2 * args.steps,
         }
