@@ -83,7 +83,10 @@ __device__ __forceinline__ float int8_code_near_tie(float x, float s, float t, f
   return fminf(fmaxf(q, -127.0f), 127.0f);
 }
 
-// Bracketed INT8 rounding of packed pairs (sm_100 FFMA2).  With
+// Bracketed INT8 rounding of packed pairs (sm_100 FFMA2), used where the
+// code is not rint of a single quotient (the RMS folding's
+// rint(RN(RN(v / peak) * 127)), prep_impl.cuh); plain per-token codes use
+// i8_pair_div below.  With
 // inv = RN(1/s), inv_hi = RN(inv (1 + 2^-21)) and inv_lo = RN(inv (1 - 2^-21)),
 // x*inv_hi and x*inv_lo (exact products inside the FMA) bracket RN(x/s) for
 // every x: the three rounding errors are at most 2^-24 each (2^-22.4 together),
@@ -116,6 +119,32 @@ __device__ __forceinline__ float2 i8_pair(float2 v, const I8Bracket& b, uint32_t
   acc |= (__float_as_uint(h.x) ^ __float_as_uint(l.x)) | (__float_as_uint(h.y) ^ __float_as_uint(l.y));
   return h;
 }
+// INT8 codes of packed pairs from the correctly rounded quotient, without a
+// division: with y = RN(1/s), q = RN(x y) and the residual r = x - q s (exact
+// in one FMA), RN(q + r y) is RN(x / s) -- Markstein's correction step
+// (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Develop. 34(1), 1990), which holds when
+// no intermediate underflows.  With s >= kI8DivMinScale every intermediate is
+// a normal number for |x| >= s/4, the only values whose code can be nonzero;
+// below that the result is within a few ulps of x/s and rounds to 0 like it.
+// Adding 1.5*2^23 then rounds to the nearest integer, ties to even (rint), and
+// the low byte of the sum is the two's-complement int8 code; |x| <= 127.0001 s
+// keeps it inside +-127, so no clip is needed.  Branch-free: every element
+// costs the same four packed operations per pair.
+constexpr float kI8DivMinScale = 0x1p-90f;
+struct I8Div {
+  float2 y, ns;  // RN(1/s), -s
+};
+__device__ __forceinline__ I8Div i8_div(float inv, float scale) {
+  return I8Div{make_float2(inv, inv), make_float2(-scale, -scale)};
+}
+__device__ __forceinline__ float2 i8_pair_div(float2 x, const I8Div& d) {
+  const float2 q = __fmul2_rn(x, d.y);
+  const float2 r = __ffma2_rn(q, d.ns, x);  // x - q s, exact
+  const float2 qc = __ffma2_rn(r, d.y, q);  // RN(x / s)
+  return __fadd2_rn(qc, make_float2(12582912.0f, 12582912.0f));
+}
+
 // Four int8 codes (low bytes of a, b, c, d) packed into one word.
 __device__ __forceinline__ uint32_t pack4_low_bytes(float a, float b, float c, float d) {
   return __byte_perm(__byte_perm(__float_as_uint(a), __float_as_uint(b), 0x0040),

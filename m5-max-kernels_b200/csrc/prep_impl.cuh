@@ -79,55 +79,28 @@ __device__ __forceinline__ uint32_t quant_e4m3(float v, float scale, float inv, 
 // low byte of the sum's bit pattern is the two's-complement int8 of rint(t).
 constexpr float kRoundMagic = 12582912.0f;
 
-// Sixteen values by value (registers), for the out-of-line near-tie path.
+// Sixteen values by value (registers), for the out-of-line exact paths.
 struct Vals16 {
   float4 a, b, c, d;
 };
 
-// Exact codes of 16 values of which at least one has its product within
-// 2^-14 of a half-integer: the reciprocal-product code per element, and the
-// division-free decision of int8_code_near_tie where it is needed.  Out of
-// line: it runs for a small fraction of 16-value groups.
-static __device__ __noinline__ uint4 quant_i8_near_tie16(Vals16 in, float scale, float inv) {
-  constexpr float kNear = 0.5f - 0x1p-14f;
-  const float v[16] = {in.a.x, in.a.y, in.a.z, in.a.w, in.b.x, in.b.y, in.b.z, in.b.w,
-                       in.c.x, in.c.y, in.c.z, in.c.w, in.d.x, in.d.y, in.d.z, in.d.w};
-  uint32_t w[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    const float t = __fmul_rn(v[e], inv);
-    float m = __fadd_rn(t, kRoundMagic);
-    const float r = __fsub_rn(m, kRoundMagic);
-    if (fabsf(__fsub_rn(t, r)) > kNear)
-      m = __fadd_rn(int8_code_near_tie(v[e], scale, t, r), kRoundMagic);
-    w[e >> 2] |= (__float_as_uint(m) & 0xFFu) << (8 * (e & 3));
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-// Quantize 16 values to int8 codes packed four per word by bracketed
-// rounding of packed pairs (i8_pair, common.cuh); a group whose brackets
-// disagree somewhere is redone by quant_i8_near_tie16.  Requires
-// scale >= 2^-100.
 __device__ __forceinline__ void quant_i8_fast16(const float* v, float scale, float inv,
                                                 uint32_t* words) {
-  const I8Bracket br = i8_bracket(inv, scale);
-  uint32_t acc = 0u;
+  if (scale >= kI8DivMinScale) {
+    const I8Div d = i8_div(inv, scale);
 #pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    const float2 m0 = i8_pair(make_float2(v[4 * w], v[4 * w + 1]), br, acc);
-    const float2 m1 = i8_pair(make_float2(v[4 * w + 2], v[4 * w + 3]), br, acc);
-    words[w] = pack4_low_bytes(m0.x, m0.y, m1.x, m1.y);
-  }
-  if (acc != 0u) {
-    const Vals16 in{make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]),
-                    make_float4(v[8], v[9], v[10], v[11]),
-                    make_float4(v[12], v[13], v[14], v[15])};
-    const uint4 q = quant_i8_near_tie16(in, scale, inv);
-    words[0] = q.x;
-    words[1] = q.y;
-    words[2] = q.z;
-    words[3] = q.w;
+    for (int w = 0; w < 4; ++w) {
+      const float2 m0 = i8_pair_div(make_float2(v[4 * w], v[4 * w + 1]), d);
+      const float2 m1 = i8_pair_div(make_float2(v[4 * w + 2], v[4 * w + 3]), d);
+      words[w] = pack4_low_bytes(m0.x, m0.y, m1.x, m1.y);
+    }
+  } else {  // scale below 2^-90: divide exactly
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+      words[w] = (quant_i8(v[4 * w], scale, inv, false) & 0xFF) |
+                 ((quant_i8(v[4 * w + 1], scale, inv, false) & 0xFF) << 8) |
+                 ((quant_i8(v[4 * w + 2], scale, inv, false) & 0xFF) << 16) |
+                 ((quant_i8(v[4 * w + 3], scale, inv, false) & 0xFF) << 24);
   }
 }
 

@@ -28,7 +28,6 @@ namespace {
 
 using namespace qv;
 
-constexpr int kTieQueue = 64;  // queued near-tie vectors per warp and row
 
 template <int NT>
 __device__ __forceinline__ float cta_peak(float peak, float* red) {
@@ -53,9 +52,6 @@ __global__ void __launch_bounds__(NT)
                       float* __restrict__ s) {
   constexpr int V = kVec<T>;
   __shared__ float red[NT / 32];
-  __shared__ uint4 tie_raw[NT / 32][kTieQueue];
-  __shared__ int tie_idx[NT / 32][kTieQueue];
-  __shared__ int tie_n[NT / 32];
   const int tid = threadIdx.x;
   const int nvec = static_cast<int>(K / V);  // K % V == 0 on this path
   const float qmax = OUT == OUT_E4M3 ? 448.0f : 127.0f;
@@ -89,41 +85,19 @@ __global__ void __launch_bounds__(NT)
       const float inv = __frcp_rn(scale);
       const bool fast = scale >= 0x1p-100f;
       if (tid == 0) s[row] = scale;
-      if (OUT == OUT_INT8 && fast) {
-        // Bracketed codes for every vector; a vector whose brackets disagree
-        // (a quotient next to a half-integer) is queued and redone exactly
-        // after the pass by the whole warp, one queued vector per lane, so
-        // the exact path does not serialise the warp vector by vector.
-        const I8Bracket br = i8_bracket(inv, scale);
-        const int warp = tid >> 5, lane = tid & 31;
-        if (lane == 0) tie_n[warp] = 0;
-        __syncwarp();
+      if (OUT == OUT_INT8 && scale >= kI8DivMinScale) {
+        // Codes from the correctly rounded quotients of packed pairs
+        // (i8_pair_div): the same operations for every vector, no branch.
+        const I8Div d = i8_div(inv, scale);
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
           const int j = tid + i * NT;
           if (EXACT || j < nvec) {
             uint32_t words[V / 4];
-            const uint32_t acc = pack_i8_vec<T>(raw[i], br, words);
+            pack_i8_vec<T>(raw[i], d, words);
             store_codes<T>(qr, j, words);
-            if (acc != 0u) {
-              const int slot = atomicAdd(&tie_n[warp], 1);
-              if (slot < kTieQueue) {
-                tie_raw[warp][slot] = raw[i];
-                tie_idx[warp][slot] = j;
-              } else {  // queue full: redo in place
-                const uint2 w = i8_words_near_tie<T>(raw[i], scale, inv);
-                store_codes<T>(qr, j, reinterpret_cast<const uint32_t*>(&w));
-              }
-            }
           }
         }
-        __syncwarp();
-        const int n = min(tie_n[warp], kTieQueue);
-        for (int k = lane; k < n; k += 32) {
-          const uint2 w = i8_words_near_tie<T>(tie_raw[warp][k], scale, inv);
-          store_codes<T>(qr, tie_idx[warp][k], reinterpret_cast<const uint32_t*>(&w));
-        }
-        __syncwarp();
       } else {
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {

@@ -1,6 +1,6 @@
 // Per-vector helpers of the per-token quantization (16-byte vectors of 8
-// bf16 / fp16 or 4 fp32 values): row peak, bracketed INT8 codes with the exact
-// near-tie path, E4M3 codes, code stores.  Shared by the quantize kernel
+// bf16 / fp16 or 4 fp32 values): row peak, INT8 codes from correctly rounded
+// quotients, E4M3 codes, code stores.  Shared by the quantize kernel
 // (quant.cu) and the fused quantize + GEMM kernel (gemm.cu).
 //
 // Reference arithmetic: src/m5kernels/numerics.py:29-46 (quantize_reference):
@@ -72,16 +72,12 @@ __device__ __forceinline__ void unpack(const uint4& raw, float* out) {
 }
 
 // INT8 codes of one 16-byte vector (8 bf16/fp16 or 4 fp32 values) packed
-// into words by bracketed rounding of packed pairs (i8_pair).  Returns the
-// bracket disagreement bits: nonzero means some element may round
-// differently from the reference, and the vector is redone by
-// i8_words_near_tie.
+// into words, from the correctly rounded quotients of packed pairs
+// (i8_pair_div).  Requires scale >= kI8DivMinScale.
 template <typename T>
-__device__ __forceinline__ uint32_t pack_i8_vec(const uint4& raw, const I8Bracket& br,
-                                                uint32_t* words) {
+__device__ __forceinline__ void pack_i8_vec(const uint4& raw, const I8Div& d, uint32_t* words) {
   constexpr int PAIRS = sizeof(T) == 2 ? 4 : 2;
   float2 m[PAIRS];
-  uint32_t acc = 0u;
 #pragma unroll
   for (int p = 0; p < PAIRS; ++p) {
     float2 v;
@@ -97,36 +93,11 @@ __device__ __forceinline__ uint32_t pack_i8_vec(const uint4& raw, const I8Bracke
       v = make_float2(reinterpret_cast<const float*>(&raw)[2 * p],
                       reinterpret_cast<const float*>(&raw)[2 * p + 1]);
     }
-    m[p] = i8_pair(v, br, acc);
+    m[p] = i8_pair_div(v, d);
   }
 #pragma unroll
   for (int w = 0; w < PAIRS / 2; ++w)
     words[w] = pack4_low_bytes(m[2 * w].x, m[2 * w].y, m[2 * w + 1].x, m[2 * w + 1].y);
-  return acc;
-}
-
-// The exact codes of a vector that holds a product next to a half-integer:
-// per element the reciprocal-product code, and for an element within 2^-14
-// of a half-integer the division-free decision of int8_code_near_tie.  Kept
-// out of line: it runs for a small fraction of vectors.  Requires
-// scale >= 2^-100.
-template <typename T>
-__device__ __noinline__ uint2 i8_words_near_tie(uint4 raw, float scale, float inv) {
-  constexpr int V = kVec<T>;
-  constexpr float kNear = 0.5f - 0x1p-14f;
-  float v[V];
-  unpack<T>(raw, v);
-  uint32_t w[2] = {0u, 0u};
-#pragma unroll
-  for (int e = 0; e < V; ++e) {
-    const float t = __fmul_rn(v[e], inv);
-    float m = __fadd_rn(t, kMagic);
-    const float r = __fadd_rn(m, -kMagic);
-    if (fabsf(__fsub_rn(t, r)) > kNear)
-      m = __fadd_rn(int8_code_near_tie(v[e], scale, t, r), kMagic);
-    w[e >> 2] |= (__float_as_uint(m) & 0xFFu) << (8 * (e & 3));
-  }
-  return make_uint2(w[0], w[1]);
 }
 
 static __device__ __forceinline__ uint32_t code_i8_exact(float v, float scale) {
@@ -145,13 +116,9 @@ __device__ __forceinline__ void vec_codes(const uint4& raw, float scale, float i
     unpack<T>(raw, v);
     e4m3_words<V / 4>(v, scale, inv, fast, words);
   } else {
-    if (fast) {
-      if (pack_i8_vec<T>(raw, i8_bracket(inv, scale), words) != 0u) {
-        const uint2 w = i8_words_near_tie<T>(raw, scale, inv);
-        words[0] = w.x;
-        if constexpr (V == 8) words[1] = w.y;
-      }
-    } else {  // scale below 2^-100: the reciprocal product is not trustworthy
+    if (fast && scale >= kI8DivMinScale) {
+      pack_i8_vec<T>(raw, i8_div(inv, scale), words);
+    } else {  // scale below 2^-90: divide exactly
       unpack<T>(raw, v);
 #pragma unroll
       for (int w = 0; w < V / 4; ++w)

@@ -535,27 +535,16 @@ __global__ void __launch_bounds__(kThreads, MODE == kPlain ? 2 : 1)
           if constexpr (OUT == OUT_E4M3) {
             // the 8 pairs are 16 consecutive floats in element order
             e4m3_words<4>(reinterpret_cast<const float*>(p), scale, rinv, fast, words);
-          } else if (fast) {
-            const I8Bracket br = i8_bracket(rinv, scale);
-            uint32_t acc = 0u;
+          } else if (scale >= kI8DivMinScale) {
+            // correctly rounded quotients of the packed pairs (i8_pair_div)
+            const I8Div d = i8_div(rinv, scale);
 #pragma unroll
             for (int w = 0; w < 4; ++w) {
-              const float2 m0 = i8_pair(p[2 * w], br, acc);
-              const float2 m1 = i8_pair(p[2 * w + 1], br, acc);
+              const float2 m0 = i8_pair_div(p[2 * w], d);
+              const float2 m1 = i8_pair_div(p[2 * w + 1], d);
               words[w] = pack4_low_bytes(m0.x, m0.y, m1.x, m1.y);
             }
-            if (acc != 0u) {
-              const Vals16 in{make_float4(p[0].x, p[0].y, p[1].x, p[1].y),
-                              make_float4(p[2].x, p[2].y, p[3].x, p[3].y),
-                              make_float4(p[4].x, p[4].y, p[5].x, p[5].y),
-                              make_float4(p[6].x, p[6].y, p[7].x, p[7].y)};
-              const uint4 qv = quant_i8_near_tie16(in, scale, rinv);
-              words[0] = qv.x;
-              words[1] = qv.y;
-              words[2] = qv.z;
-              words[3] = qv.w;
-            }
-          } else {  // scale below 2^-100: divide exactly
+          } else {  // scale below 2^-90: divide exactly
 #pragma unroll
             for (int w = 0; w < 4; ++w)
               words[w] = (quant_i8(p[2 * w].x, scale, rinv, false) & 0xFF) |

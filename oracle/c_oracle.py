@@ -106,6 +106,10 @@ def lib() -> ctypes.CDLL:
         _lib.m5o_rms_quantize.restype = None
         _lib.m5o_quantize_mxint8.argtypes = [P, I32, I64, I64, P, P]
         _lib.m5o_quantize_mxint8.restype = None
+        _lib.m5o_check_i8_div_free.argtypes = [P, I64, P]
+        _lib.m5o_check_i8_div_free.restype = I64
+        _lib.m5o_check_i8_div_free_f32.argtypes = [I64, ctypes.c_uint64, P]
+        _lib.m5o_check_i8_div_free_f32.restype = I64
     return _lib
 
 

@@ -436,3 +436,71 @@ void m5o_qk_rope_from_acc(const float* accf, int64_t M, int64_t N, const float* 
     }
   }
 }
+
+/* ------------------------------------------------------------------------
+ * The kernels' division-free INT8 code (csrc/common.cuh, i8_pair_div),
+ * restated to check its claim here: with y = RN(1/s), q = RN(x y),
+ * r = fma(-q, s, x) and c = fma(r, y, q) (Markstein's correction step),
+ * rint(c) == rint(RN(x / s)) for every s >= 2^-90 and |x| <= 127.0001 s.
+ * m5o_check_i8_div_free counts, over the given scales and every finite bf16
+ * value x in that domain, the x whose two codes differ (0 expected);
+ * m5o_check_i8_div_free_f32 does the same for `samples` fp32 pairs (x, s)
+ * drawn by a fixed generator, half of them next to (k + 1/2) s.  *tested
+ * receives the number of pairs compared. */
+static float f32_of_bits(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+static uint32_t bits_of_f32(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+
+static float i8_div_free_code(float x, float s, float y) {
+  const float q = x * y;
+  const float r = fmaf(-q, s, x);
+  return rintf(fmaf(r, y, q));
+}
+
+int64_t m5o_check_i8_div_free(const float* scales, int64_t n, int64_t* tested) {
+  int64_t bad = 0, count = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const float s = scales[i];
+    if (!(s >= 0x1p-90f) || !isfinite(s)) continue;
+    const float y = 1.0f / s;
+    for (uint32_t h = 0; h < 65536u; ++h) {
+      const float x = bf16_to_f32((uint16_t)h);
+      if (!isfinite(x) || fabsf(x) > 127.0001f * s) continue;
+      ++count;
+      if (i8_div_free_code(x, s, y) != rintf(x / s)) ++bad;
+    }
+  }
+  if (tested) *tested = count;
+  return bad;
+}
+
+int64_t m5o_check_i8_div_free_f32(int64_t samples, uint64_t seed, int64_t* tested) {
+  uint64_t st = seed ? seed : 0x9E3779B97F4A7C15ull;
+  int64_t bad = 0, count = 0;
+  for (int64_t t = 0; t < samples; ++t) {
+    st ^= st << 13; st ^= st >> 7; st ^= st << 17;
+    const uint32_t e = (uint32_t)(37 + st % 190);  /* scales 2^-90 .. 2^99 */
+    st ^= st << 13; st ^= st >> 7; st ^= st << 17;
+    const float s = f32_of_bits((e << 23) | (uint32_t)(st & 0x7FFFFFu));
+    st ^= st << 13; st ^= st >> 7; st ^= st << 17;
+    float x;
+    if (t & 1) {  /* within 4 ulps of (k + 1/2) s */
+      x = ((float)(int64_t)(st % 254) - 127.0f + 0.5f) * s;
+      x = f32_of_bits(bits_of_f32(x) + (uint32_t)((int)((st >> 20) % 9) - 4));
+    } else {
+      x = ((float)(st % 2000001u) / 1000000.0f - 1.0f) * 127.0f * s;
+    }
+    if (!isfinite(x) || fabsf(x) > 127.0001f * s) continue;
+    ++count;
+    if (i8_div_free_code(x, s, 1.0f / s) != rintf(x / s)) ++bad;
+  }
+  if (tested) *tested = count;
+  return bad;
+}
