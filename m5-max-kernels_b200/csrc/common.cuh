@@ -83,42 +83,6 @@ __device__ __forceinline__ float int8_code_near_tie(float x, float s, float t, f
   return fminf(fmaxf(q, -127.0f), 127.0f);
 }
 
-// Bracketed INT8 rounding of packed pairs (sm_100 FFMA2), used where the
-// code is not rint of a single quotient (the RMS folding's
-// rint(RN(RN(v / peak) * 127)), prep_impl.cuh); plain per-token codes use
-// i8_pair_div below.  With
-// inv = RN(1/s), inv_hi = RN(inv (1 + 2^-21)) and inv_lo = RN(inv (1 - 2^-21)),
-// x*inv_hi and x*inv_lo (exact products inside the FMA) bracket RN(x/s) for
-// every x: the three rounding errors are at most 2^-24 each (2^-22.4 together),
-// inside the 2^-21 margin.  Adding 1.5*2^23 in the same FMA rounds each bracket end to
-// the nearest integer, ties to even (the constant is even), so the low byte
-// of the result is the two's-complement int8 of rint(end).  rint is monotone,
-// so when both ends give the same integer it is rint(RN(x/s)), the
-// reference's code; `acc` collects the bits where the ends differ, and a
-// nonzero acc sends the group to an exact path.  |x| <= 127.0001 s keeps the
-// ends inside +-127.5, so no clipping is needed.  Requires s >= 2^-100.
-struct I8Bracket {
-  float2 lo, hi;
-};
-// A power-of-two scale has an exact reciprocal: x*inv is then x/s itself and
-// one end suffices (both ends equal, acc stays zero).  Such scales are the
-// ones under which 16-bit inputs land exactly on half-integers (a row peak
-// of 127 * 2^e), so without this shortcut those rows would take the exact
-// path element by element.
-__device__ __forceinline__ I8Bracket i8_bracket(float inv, float scale) {
-  if ((__float_as_uint(scale) & 0x007FFFFFu) == 0u)
-    return I8Bracket{make_float2(inv, inv), make_float2(inv, inv)};
-  const float lo = __fmul_rn(inv, 1.0f - 0x1p-21f), hi = __fmul_rn(inv, 1.0f + 0x1p-21f);
-  return I8Bracket{make_float2(lo, lo), make_float2(hi, hi)};
-}
-// Codes of one pair in the low bytes of the returned words' bit patterns.
-__device__ __forceinline__ float2 i8_pair(float2 v, const I8Bracket& b, uint32_t& acc) {
-  const float2 mag = make_float2(12582912.0f, 12582912.0f);
-  const float2 h = __ffma2_rn(v, b.hi, mag);
-  const float2 l = __ffma2_rn(v, b.lo, mag);
-  acc |= (__float_as_uint(h.x) ^ __float_as_uint(l.x)) | (__float_as_uint(h.y) ^ __float_as_uint(l.y));
-  return h;
-}
 // INT8 codes of packed pairs from the correctly rounded quotient, without a
 // division: with y = RN(1/s), q = RN(x y) and the residual r = x - q s (exact
 // in one FMA), RN(q + r y) is RN(x / s) -- Markstein's correction step
@@ -138,11 +102,16 @@ struct I8Div {
 __device__ __forceinline__ I8Div i8_div(float inv, float scale) {
   return I8Div{make_float2(inv, inv), make_float2(-scale, -scale)};
 }
-__device__ __forceinline__ float2 i8_pair_div(float2 x, const I8Div& d) {
+// RN(x / s) of a packed pair (the corrected quotient itself): exact wherever
+// |x / s| >= 2^-12 and s >= kI8DivMinScale (the RMS folding's codes,
+// prep_impl.cuh, use it there).  The sign of a zero quotient is not kept.
+__device__ __forceinline__ float2 quot_pair_div(float2 x, const I8Div& d) {
   const float2 q = __fmul2_rn(x, d.y);
   const float2 r = __ffma2_rn(q, d.ns, x);  // x - q s, exact
-  const float2 qc = __ffma2_rn(r, d.y, q);  // RN(x / s)
-  return __fadd2_rn(qc, make_float2(12582912.0f, 12582912.0f));
+  return __ffma2_rn(r, d.y, q);             // RN(x / s)
+}
+__device__ __forceinline__ float2 i8_pair_div(float2 x, const I8Div& d) {
+  return __fadd2_rn(quot_pair_div(x, d), make_float2(12582912.0f, 12582912.0f));
 }
 
 // Four int8 codes (low bytes of a, b, c, d) packed into one word.

@@ -79,11 +79,6 @@ __device__ __forceinline__ uint32_t quant_e4m3(float v, float scale, float inv, 
 // low byte of the sum's bit pattern is the two's-complement int8 of rint(t).
 constexpr float kRoundMagic = 12582912.0f;
 
-// Sixteen values by value (registers), for the out-of-line exact paths.
-struct Vals16 {
-  float4 a, b, c, d;
-};
-
 __device__ __forceinline__ void quant_i8_fast16(const float* v, float scale, float inv,
                                                 uint32_t* words) {
   if (scale >= kI8DivMinScale) {
@@ -106,43 +101,40 @@ __device__ __forceinline__ void quant_i8_fast16(const float* v, float scale, flo
 
 // Codes of the RMS preparation, rint(RN(RN(v / peak) * 127)) clipped to
 // +-127 (the reference's order: divide by the row peak, then scale by 127),
-// for 16 values.  Both roundings together move the result by less than
-// 2^-23 relative, so products with RN(127 / peak)(1 -+ 2^-21), which bracket
-// it, decide the integer whenever they agree; a group where they disagree
-// somewhere is redone exactly by rel_i8_exact16.  Requires peak >= 2^-100.
-static __device__ __noinline__ uint4 rel_i8_exact16(Vals16 in, float peak) {
-  const float v[16] = {in.a.x, in.a.y, in.a.z, in.a.w, in.b.x, in.b.y, in.b.z, in.b.w,
-                       in.c.x, in.c.y, in.c.z, in.c.w, in.d.x, in.d.y, in.d.z, in.d.w};
-  uint32_t w[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    const float c = rintf(__fmul_rn(__fdiv_rn(v[e], peak), 127.0f));
-    const int code = static_cast<int>(fminf(fmaxf(c, -127.0f), 127.0f));
-    w[e >> 2] |= (static_cast<uint32_t>(code) & 0xFFu) << (8 * (e & 3));
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
-
+// for 16 values: the correctly rounded quotients of packed pairs
+// (quot_pair_div, exact wherever a code can be nonzero), times 127, rounded
+// to integers by the magic constant.  |v| <= peak keeps the codes inside
+// +-127.  Peaks below kI8DivMinScale divide each value exactly.
 __device__ __forceinline__ void rel_i8_fast16(const float* v, float peak, uint32_t* words) {
-  const float r = __fdiv_rn(127.0f, peak);
-  const float lo = __fmul_rn(r, 1.0f - 0x1p-21f), hi = __fmul_rn(r, 1.0f + 0x1p-21f);
-  const I8Bracket br{make_float2(lo, lo), make_float2(hi, hi)};
-  uint32_t acc = 0u;
+  if (peak < kI8DivMinScale) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      uint32_t x = 0u;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float c = rintf(__fmul_rn(__fdiv_rn(v[4 * w + e], peak), 127.0f));
+        const int code = static_cast<int>(fminf(fmaxf(c, -127.0f), 127.0f));
+        x |= (static_cast<uint32_t>(code) & 0xFFu) << (8 * e);
+      }
+      words[w] = x;
+    }
+    return;
+  }
+  const I8Div d = i8_div(__frcp_rn(peak), peak);
+  // RN(q * 127), then rint by the magic add: two separately rounded scalar
+  // operations (__fmul_rn / __fadd_rn are never merged into a multiply-add;
+  // a merged form, RN(q * 127 + magic), rounds products next to a
+  // half-integer differently -- observed with the packed forms).
+  auto code2 = [&](float2 x) -> float2 {
+    const float2 q = quot_pair_div(x, d);
+    return make_float2(__fadd_rn(__fmul_rn(q.x, 127.0f), kRoundMagic),
+                       __fadd_rn(__fmul_rn(q.y, 127.0f), kRoundMagic));
+  };
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
-    const float2 m0 = i8_pair(make_float2(v[4 * w], v[4 * w + 1]), br, acc);
-    const float2 m1 = i8_pair(make_float2(v[4 * w + 2], v[4 * w + 3]), br, acc);
+    const float2 m0 = code2(make_float2(v[4 * w], v[4 * w + 1]));
+    const float2 m1 = code2(make_float2(v[4 * w + 2], v[4 * w + 3]));
     words[w] = pack4_low_bytes(m0.x, m0.y, m1.x, m1.y);
-  }
-  if (acc != 0u) {
-    const Vals16 in{make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]),
-                    make_float4(v[8], v[9], v[10], v[11]),
-                    make_float4(v[12], v[13], v[14], v[15])};
-    const uint4 q = rel_i8_exact16(in, peak);
-    words[0] = q.x;
-    words[1] = q.y;
-    words[2] = q.z;
-    words[3] = q.w;
   }
 }
 

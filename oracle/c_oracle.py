@@ -110,6 +110,8 @@ def lib() -> ctypes.CDLL:
         _lib.m5o_check_i8_div_free.restype = I64
         _lib.m5o_check_i8_div_free_f32.argtypes = [I64, ctypes.c_uint64, P]
         _lib.m5o_check_i8_div_free_f32.restype = I64
+        _lib.m5o_check_div_free_quotient.argtypes = [P, I64, F, F, I64, ctypes.c_uint64, P]
+        _lib.m5o_check_div_free_quotient.restype = I64
     return _lib
 
 

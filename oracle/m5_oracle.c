@@ -504,3 +504,47 @@ int64_t m5o_check_i8_div_free_f32(int64_t samples, uint64_t seed, int64_t* teste
   if (tested) *tested = count;
   return bad;
 }
+
+/* The corrected quotient itself, for the RMS folding's
+ * rint(RN(RN(v / peak) * 127)): c == RN(x / s) whenever s >= 2^-90 and
+ * min_ratio <= |RN(x / s)| <= max_ratio.  Counts the finite bf16 values x
+ * (over the given scales) and the `samples` random fp32 values for which c
+ * and the IEEE quotient differ; *tested receives the number compared. */
+int64_t m5o_check_div_free_quotient(const float* scales, int64_t n, float min_ratio,
+                                    float max_ratio, int64_t samples, uint64_t seed,
+                                    int64_t* tested) {
+  int64_t bad = 0, count = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const float s = scales[i];
+    if (!(s >= 0x1p-90f) || !isfinite(s)) continue;
+    const float y = 1.0f / s;
+    for (uint32_t h = 0; h < 65536u; ++h) {
+      const float x = bf16_to_f32((uint16_t)h);
+      if (!isfinite(x)) continue;
+      const float ref = x / s;
+      if (!(fabsf(ref) >= min_ratio && fabsf(ref) <= max_ratio)) continue;
+      ++count;
+      const float q = x * y, r = fmaf(-q, s, x), c = fmaf(r, y, q);
+      if (bits_of_f32(c) != bits_of_f32(ref)) ++bad;
+    }
+  }
+  uint64_t st = seed ? seed : 0x2545F4914F6CDD1Dull;
+  for (int64_t t = 0; t < samples; ++t) {
+    st ^= st << 13; st ^= st >> 7; st ^= st << 17;
+    const uint32_t e = (uint32_t)(37 + st % 190);
+    st ^= st << 13; st ^= st >> 7; st ^= st << 17;
+    const float s = f32_of_bits((e << 23) | (uint32_t)(st & 0x7FFFFFu));
+    st ^= st << 13; st ^= st >> 7; st ^= st << 17;
+    /* a ratio log-uniform in [min_ratio, max_ratio], random sign */
+    const double u = (double)(st >> 11) / 9007199254740992.0;
+    const double ratio = exp(log((double)min_ratio) + u * (log((double)max_ratio) - log((double)min_ratio)));
+    const float x = (float)((st & 1) ? -ratio : ratio) * s;
+    const float ref = x / s;
+    if (!isfinite(x) || !(fabsf(ref) >= min_ratio && fabsf(ref) <= max_ratio)) continue;
+    ++count;
+    const float y = 1.0f / s, q = x * y, r = fmaf(-q, s, x), c = fmaf(r, y, q);
+    if (bits_of_f32(c) != bits_of_f32(ref)) ++bad;
+  }
+  if (tested) *tested = count;
+  return bad;
+}

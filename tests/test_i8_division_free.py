@@ -6,8 +6,11 @@ reference's code (src/m5kernels/numerics.py:29-46), for every scale
 s >= 2^-90 and |x| <= 127.0001 s.  These CPU checks (the C restatement in
 oracle/m5_oracle.c) compare the two codes for every bf16 value against scales
 of bf16 row peaks, scales with significands next to 1 and 2, the 2^-90 edge,
-and random scales, plus fp32 values next to half-integer quotients.  The GPU
-tests check the kernels themselves against the IEEE-division oracle."""
+and random scales, plus fp32 values next to half-integer quotients.  The RMS
+folding's codes, rint(RN(RN(v / peak) * 127)), need the corrected
+quotient itself to equal RN(x / s) wherever a code can be nonzero
+(|x / s| >= 2^-12), which the last test checks.  The GPU tests check the
+kernels themselves against the IEEE-division oracle."""
 
 import ctypes
 import struct
@@ -46,4 +49,13 @@ def test_fp32_codes_match_ieee_division():
     tested = ctypes.c_int64(0)
     bad = co.lib().m5o_check_i8_div_free_f32(2_000_000, 11, ctypes.byref(tested))
     assert tested.value > 1_500_000
+    assert bad == 0
+
+
+def test_corrected_quotient_is_the_ieee_quotient():
+    s = _scales()
+    tested = ctypes.c_int64(0)
+    bad = co.lib().m5o_check_div_free_quotient(s.ctypes.data, s.size, 2.0 ** -12, 448.5,
+                                                2_000_000, 13, ctypes.byref(tested))
+    assert tested.value > 10_000_000
     assert bad == 0
