@@ -15,8 +15,6 @@
 namespace m5b {
 namespace qv {
 
-constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: RNE to integer for |t| < 2^22
-
 // Running row peak max|x|.  16-bit inputs stay packed: one
 // max.xorsign.abs per pair of words (the magnitudes are exact, the sign bits
 // are cleared at the end); fp32 inputs use FMNMX with |.|.
